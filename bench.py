@@ -1,0 +1,457 @@
+"""Benchmark of the two-stage block-sparse attention forward on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 3]
+                    [--impl ours|reference] [--scaling weak|strong]
+
+A *step* is one forward pass (pool -> score/select -> fine) over one batch of
+synthetic inputs of the chosen workload (default: B1 H8 N32768 D64, bf16,
+block_size 64, top_k 16, causal -- the shape the reference's headline numbers
+are quoted on).  Rank 0 prints one JSON line.
+
+* ``value``: effective TFLOP/s (FLOPs of the reference's benchmark/flops.py
+  model, summed over every unit all ranks processed, divided by the max over
+  ranks of the CUDA-event time of K steps), inputs resident in HBM, L2
+  flushed before every step.
+* ``e2e``: the same metric through the public variant API with pinned host
+  buffers: host->device copies of Q, K, V and the device->host copy of O are
+  inside the timed region.
+* ``roofline``: the fine-stage kernel, FLOPs per launch / its event time
+  against the measured bf16 dense peak.
+* ``cpu_baseline``: the numpy restatement of the reference's block_indexer
+  timed on this host's cores on a bounded sample (rank 0, N=1 only).
+
+``--impl reference`` times the reference algorithm on the host cores (the
+oracle port of attention/block_indexer.py) on the same workload and prints
+the same line with ``"impl": "reference"``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "block-sparse attn fwd ms + effective TFLOPS & HBM GB/s at N=32k, 1/2/4/8 B200"
+
+WORKLOADS = {
+    1: dict(B=1, H=8, N=1024, D=64, block_size=64, top_k=16, causal=True, dist="normal"),
+    2: dict(B=1, H=8, N=8192, D=64, block_size=64, top_k=16, causal=False, dist="normal"),
+    3: dict(B=1, H=8, N=32768, D=64, block_size=64, top_k=16, causal=True, dist="normal"),
+    4: dict(B=2, H=32, N=32768, D=128, block_size=64, top_k=32, causal=True, dist="clustered"),
+    5: dict(B=1, H=16, N=131072, D=64, block_size=128, top_k=16, causal=True, dist="block_scaled"),
+}
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_FLUSH_BYTES = 256 << 20
+STAGES = ["pool", "select", "bucket", "fine", "combine"]
+
+
+def workload_name(cfg):
+    return (f"block-sparse attention fwd B{cfg['B']} H{cfg['H']} N{cfg['N']} D{cfg['D']} "
+            f"bs{cfg['block_size']} k{cfg['top_k']} {'causal' if cfg['causal'] else 'non-causal'} "
+            f"{cfg['dist']}")
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def per_query_flops(cfg):
+    from flash_vs_sparse_attention_b200.flops import compute_flops
+    return compute_flops(1, 1, cfg["N"], cfg["D"], "block_indexer_b200", cfg["block_size"],
+                         cfg["top_k"]) // cfg["N"]
+
+
+# --------------------------------------------------------------------------
+# Clock sampling during the timed region.
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        import tempfile
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                f = [x.strip() for x in line.split(",")]
+                if len(f) >= 9 and f[1].replace(".", "").isdigit():
+                    rows.append(f)
+        except OSError:
+            pass
+        finally:
+            if self.path:
+                try:
+                    os.unlink(self.path)
+                except OSError:
+                    pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()),
+                "samples": len(rows), "reasons": reasons}
+
+
+# --------------------------------------------------------------------------
+def gpu_inputs(cfg, n_units, seed, device):
+    """Synthetic (1, n_units, N, D) bf16 inputs generated on the device with the
+    workload's value distribution."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    N, D, bs = cfg["N"], cfg["D"], cfg["block_size"]
+    shape = (1, n_units, N, D)
+
+    def randn(*s):
+        return torch.randn(*s, generator=g, device=device, dtype=torch.float32)
+
+    if cfg["dist"] == "normal":
+        out = [randn(*shape) for _ in range(3)]
+    elif cfg["dist"] == "block_scaled":
+        nb = N // bs
+        out = []
+        for _ in range(3):
+            sc = torch.rand(1, n_units, nb, 1, 1, generator=g, device=device) * 1.5 + 0.5
+            out.append((randn(1, n_units, nb, bs, D) * sc).reshape(shape))
+    elif cfg["dist"] == "clustered":
+        nb = N // bs
+        centres = randn(1, n_units, 64, D)
+        ck = torch.randint(0, 64, (1, n_units, nb), generator=g, device=device)
+        cq = torch.randint(0, 64, (1, n_units, nb), generator=g, device=device)
+
+        def blocks(ids):
+            c = torch.gather(centres, 2, ids[..., None].expand(-1, -1, -1, D))
+            return c[:, :, :, None, :].expand(-1, -1, -1, bs, -1).reshape(shape)
+
+        kc = blocks(ck)
+        out = [blocks(cq) + 0.1 * randn(*shape), kc + 0.1 * randn(*shape), kc + 0.1 * randn(*shape)]
+    else:
+        raise ValueError(cfg["dist"])
+    return [t.to(torch.bfloat16).contiguous() for t in out]
+
+
+def run_ours(args, cfg):
+    import torch
+    import torch.distributed as dist
+
+    from flash_vs_sparse_attention_b200 import _lib
+    from flash_vs_sparse_attention_b200 import block_indexer_b200 as bi
+    from flash_vs_sparse_attention_b200 import flops as F
+    from flash_vs_sparse_attention_b200.sharding import unit_range
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    U = cfg["B"] * cfg["H"]
+    if args.scaling == "weak":
+        my_units = U
+        total_units = U * world
+    else:
+        a, b = unit_range(U, world, rank)
+        my_units = b - a
+        total_units = U
+    if my_units == 0:
+        raise SystemExit("strong scaling with more ranks than units")
+    Q, K, V = gpu_inputs(cfg, my_units, seed=1000 + rank, device=dev)
+    O = torch.empty_like(Q)
+    L = _lib.lib()
+    p = bi.problem(1, my_units, cfg["N"], cfg["D"], cfg["causal"], cfg["block_size"], cfg["top_k"])
+    ws_bytes = bi.workspace_bytes(p)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    n_launch = ctypes.c_int(0)
+    ev_arr = (ctypes.c_void_p * len(STAGES))()
+
+    def forward(stage_events=None):
+        if stage_events is not None:
+            for i, e in enumerate(stage_events):
+                ev_arr[i] = ctypes.c_void_p(e.cuda_event)
+            evp = ev_arr
+        else:
+            evp = None
+        st = L.bsa_forward_ex(ctypes.byref(p), ctypes.c_void_p(Q.data_ptr()),
+                              ctypes.c_void_p(K.data_ptr()), ctypes.c_void_p(V.data_ptr()),
+                              ctypes.c_void_p(O.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
+                              ctypes.c_size_t(ws_bytes), sp, evp, len(STAGES) if evp else 0,
+                              ctypes.byref(n_launch))
+        _lib.check(st, "bsa_forward_ex")
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        forward()
+    torch.cuda.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    stage_ev = [[torch.cuda.Event(enable_timing=True) for _ in STAGES] for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches = 0
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            forward(stage_ev[i])
+            ends[i].record(stream)
+            launches += n_launch.value
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    stage_ms = {name: [] for name in STAGES}
+    for i in range(args.steps):
+        prev = starts[i]
+        for name, e in zip(STAGES, stage_ev[i]):
+            stage_ms[name].append(prev.elapsed_time(e))
+            prev = e
+    total = torch.tensor([sum(step_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(total, op=dist.ReduceOp.MAX)
+    total_ms = total.item()
+    ms_per_step = total_ms / args.steps
+    flops_step = F.compute_flops(1, total_units, cfg["N"], cfg["D"], "block_indexer_b200",
+                                 cfg["block_size"], cfg["top_k"])
+    value = flops_step * args.steps / (total_ms * 1e-3) / 1e12
+    hbm_bytes = F.min_hbm_bytes(1, total_units, cfg["N"], cfg["D"])
+
+    # ---- end to end through the public API with pinned host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        Qh, Kh, Vh = (t.cpu().pin_memory() for t in (Q, K, V))
+        Oh = torch.empty(Q.shape, dtype=Q.dtype).pin_memory()
+        Qd, Kd, Vd = (torch.empty_like(t) for t in (Q, K, V))
+
+        def e2e_step():
+            Qd.copy_(Qh, non_blocking=True)
+            Kd.copy_(Kh, non_blocking=True)
+            Vd.copy_(Vh, non_blocking=True)
+            out = bi.attention(Qd, Kd, Vd, causal=cfg["causal"], block_size=cfg["block_size"],
+                               top_k=cfg["top_k"])
+            Oh.copy_(out, non_blocking=True)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        torch.cuda.synchronize()
+        es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        es.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        ee.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([es.elapsed_time(ee)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = t.item()
+        e2e = {"value": round(flops_step * args.steps / (e2e_ms * 1e-3) / 1e12, 4),
+               "unit": "TFLOP/s", "ms_per_step": round(e2e_ms / args.steps, 4),
+               "h2d_bytes_per_step": 3 * Q.numel() * Q.element_size(),
+               "d2h_bytes_per_step": O.numel() * O.element_size()}
+        del Qh, Kh, Vh, Oh, Qd, Kd, Vd
+
+    # ---- roofline of the fine-stage kernel ----
+    peaks, peak_kind = load_peaks()
+    fine_ms = statistics.mean(stage_ms["fine"])
+    fine_flops = F.fine_matmul_flops(1, my_units, cfg["N"], cfg["D"], cfg["block_size"], cfg["top_k"])
+    achieved = fine_flops / (fine_ms * 1e-3) / 1e12 if fine_ms > 0 else None
+    peak = float(peaks["bf16_tflops"])
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        try:
+            traffic = json.load(open(tpath)).get(f"config{args.config}", {}).get("fine")
+        except (OSError, ValueError):
+            traffic = None
+    roofline = {"kernel": "fine (tensor-core, key-block-stationary)", "bound": "tensor",
+                "achieved": round(achieved, 2) if achieved else None, "peak": peak,
+                "unit": "TFLOP/s", "frac": round(achieved / peak, 4) if achieved else None,
+                "peak_source": f"{peak_kind} bf16_tflops (burst)",
+                "traffic": traffic, "flops_per_launch": fine_flops,
+                "launch_ms": round(fine_ms, 4)}
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": workload_name(cfg), "units_per_gpu": my_units,
+                       "total_units": total_units, "global_batch": cfg["B"] * (world if args.scaling == "weak" else 1),
+                       "heads": cfg["H"], "seq_len": cfg["N"], "head_dim": cfg["D"],
+                       "block_size": cfg["block_size"], "top_k": cfg["top_k"],
+                       "causal": cfg["causal"], "parallelism": f"head-sharded x{world}",
+                       "l2": f"flushed before every step ({L2_FLUSH_BYTES >> 20} MiB write, outside the events)"},
+            "hbm_gbs": round(hbm_bytes * args.steps / (total_ms * 1e-3) / 1e9, 2),
+            "hbm_gbs_note": "compulsory bytes (read Q,K,V + write O) / step time",
+            "stages_ms": {k: round(statistics.mean(v), 4) for k, v in stage_ms.items()},
+            "roofline": roofline, "clocks": clk.summary(), "e2e": e2e,
+            "gpu_launches": launches,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(cfg, args)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+# --------------------------------------------------------------------------
+def cpu_sample(cfg, n_rows, seed=0):
+    """Bounded CPU sample: ``n_rows`` query rows of unit 0, in whole 512-row
+    chunks spread evenly over the sequence (causal rows late in the sequence
+    see more blocks, early ones fewer)."""
+    from oracle import unit_inputs
+    q, k, v = unit_inputs(cfg, 0, seed)
+    N = cfg["N"]
+    chunks = max(1, n_rows // 512)
+    starts = sorted({int(round(x)) * 512 for x in
+                     [i * (N // 512 - 1) / max(1, chunks - 1) for i in range(chunks)]})
+    rows = [list(range(s, min(N, s + 512))) for s in starts]
+    return q, k, v, rows
+
+
+def time_oracle(cfg, q, k, v, rows_list, threads):
+    """Run the oracle's attention on each row chunk with ``threads`` workers."""
+    import concurrent.futures as cf
+    import numpy as np
+    from oracle import attention_unit
+    from oracle.block_indexer_np import _limit_blas_threads
+
+    def one(rows):
+        attention_unit(q, k, v, cfg["causal"], cfg["block_size"], cfg["top_k"],
+                       rows=np.asarray(rows))
+
+    t0 = time.perf_counter()
+    with _limit_blas_threads(1), cf.ThreadPoolExecutor(threads) as ex:
+        list(ex.map(one, rows_list))
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(cfg, args):
+    threads = os.cpu_count() or 1
+    q, k, v, rows = cpu_sample(cfg, args.cpu_rows)
+    n = sum(len(r) for r in rows)
+    time_oracle(cfg, q, k, v, rows[:1], threads)  # warm-up
+    secs = time_oracle(cfg, q, k, v, rows, threads)
+    fl = per_query_flops(cfg) * n
+    return {"value": round(fl / secs / 1e12, 6), "unit": "TFLOP/s", "cores": threads,
+            "kind": "port", "seconds": round(secs, 3),
+            "sample": f"{n} query rows of unit 0 ({len(rows)} chunks of 512 spread over N) through "
+                      f"the numpy restatement of attention/block_indexer.py, {threads} threads"}
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    q, k, v, rows = cpu_sample(cfg, args.cpu_rows)
+    n = sum(len(r) for r in rows)
+    fl = per_query_flops(cfg) * n
+    for _ in range(args.warmup):
+        time_oracle(cfg, q, k, v, rows, threads)
+    times = [time_oracle(cfg, q, k, v, rows, threads) for _ in range(args.steps)]
+    total = sum(times)
+    value = fl * args.steps / total / 1e12
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    sample = (f"{n} query rows of unit 0 per step ({len(rows)} chunks of 512 spread over N), numpy "
+              f"restatement of attention/block_indexer.py, {threads} host threads")
+    line = {
+        "metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": workload_name(cfg), "seq_len": cfg["N"], "head_dim": cfg["D"],
+                   "block_size": cfg["block_size"], "top_k": cfg["top_k"], "causal": cfg["causal"],
+                   "parallelism": "host cores of rank 0", "sample_rows": n},
+        "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=3, choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="weak: every GPU runs the whole workload's units; strong: the units are split")
+    ap.add_argument("--cpu-rows", type=int, default=16384, help="query rows in the CPU sample")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be at least 3")
+    cfg = WORKLOADS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

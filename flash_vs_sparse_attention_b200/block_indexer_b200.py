@@ -1,0 +1,161 @@
+"""The B200 variant of the reference's two-stage block-indexer attention.
+
+Drop-in for ``attention/block_indexer_triton.py`` / ``attention/block_indexer.py``:
+same call ``attention(Q, K, V, causal=False, block_size=64, top_k=16)``, same
+(batch, heads, seq_len, head_dim) layout in and out, same asserts and the same
+``RuntimeError`` (naming the variant) when the backend is unavailable.  All
+arithmetic runs in the hand-written sm_100a kernels of ``libbsattn.so``,
+called through its C ABI; torch provides device memory and the current stream.
+
+Register it in the reference's benchmark like its own variants
+(benchmark/runner.py:13-20)::
+
+    VARIANTS['block_indexer_b200'] = functools.partial(
+        block_indexer_b200.attention, block_size=64, top_k=16)
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+VARIANT = "block_indexer_b200"
+
+# Workspace cap per call; units are processed in passes that fit it.
+DEFAULT_WORKSPACE_CAP = 4 << 30
+
+
+def _require_backend():
+    if not torch.cuda.is_available():
+        raise RuntimeError(
+            f"{VARIANT} requires CUDA and an sm_100a GPU (NVIDIA B200). "
+            "Use the reference's block_indexer for CPU testing.")
+    return _lib.lib(VARIANT)
+
+
+def _check_inputs(Q, K, V):
+    if not (Q.shape == K.shape == V.shape) or Q.dim() != 4:
+        raise ValueError(f"{VARIANT}: Q, K, V must share one (B, H, N, D) shape; got "
+                         f"{tuple(Q.shape)}, {tuple(K.shape)}, {tuple(V.shape)}")
+    for name, t in (("Q", Q), ("K", K), ("V", V)):
+        if t.device.type != "cuda":
+            raise RuntimeError(f"{VARIANT}: {name} must be a CUDA tensor (got {t.device})")
+        if t.dtype != torch.bfloat16:
+            raise TypeError(f"{VARIANT}: {name} must be torch.bfloat16 (got {t.dtype})")
+    if not (Q.device == K.device == V.device):
+        raise RuntimeError(f"{VARIANT}: Q, K, V must be on one device")
+
+
+def problem(B, H, N, D, causal, block_size, top_k, flags=0, scale=0.0):
+    return _lib.Problem(B, H, N, D, block_size, top_k, int(bool(causal)), float(scale), int(flags))
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def workspace_bytes(p, cap=DEFAULT_WORKSPACE_CAP):
+    """Workspace for one call: all units in one pass when it fits ``cap``,
+    otherwise the largest number of units per pass that does."""
+    L = _lib.lib(VARIANT)
+    pp = ctypes.byref(p)
+    units = p.batch * p.heads
+    need = L.bsa_workspace_bytes(pp, 0)
+    if need == 0:
+        _lib.check(L.bsa_check_problem(pp), VARIANT)
+    if need <= cap:
+        return need
+    one = L.bsa_workspace_bytes(pp, 1)
+    g = max(1, min(units, cap // max(one, 1)))
+    while g > 1 and L.bsa_workspace_bytes(pp, g) > cap:
+        g -= 1
+    return L.bsa_workspace_bytes(pp, g)
+
+
+def attention(Q, K, V, causal=False, block_size=64, top_k=16, *, flags=0,
+              workspace_cap=DEFAULT_WORKSPACE_CAP):
+    """
+    Q, K, V: (batch, heads, seq_len, head_dim) bf16 CUDA tensors
+    returns: (batch, heads, seq_len, head_dim) bf16
+
+    Two-stage content-adaptive sparse attention (block_indexer.py:4-86):
+      Coarse: score each query against per-block mean-pooled keys; keep the
+              top_k blocks per query token (ties to the lower block index).
+      Fine:   exact softmax attention over the top_k * block_size keys kept.
+    """
+    L = _require_backend()
+    B, H, N, D = Q.shape
+    assert N % block_size == 0, f"seq_len {N} must be divisible by block_size {block_size}"
+    num_blocks = N // block_size
+    assert top_k <= num_blocks, f"top_k {top_k} exceeds num_blocks {num_blocks}"
+    _check_inputs(Q, K, V)
+    Qc, Kc, Vc = Q.contiguous(), K.contiguous(), V.contiguous()
+    p = problem(B, H, N, D, causal, block_size, top_k, flags)
+    with torch.cuda.device(Q.device):
+        O = torch.empty_like(Qc)
+        nbytes = workspace_bytes(p, workspace_cap)
+        ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=Q.device)
+        st = L.bsa_forward(ctypes.byref(p), _ptr(Qc), _ptr(Kc), _ptr(Vc), _ptr(O), _ptr(ws),
+                           ctypes.c_size_t(ws.numel()), _stream(Q.device))
+        _lib.check(st, VARIANT)
+    return O
+
+
+def pool_k(K, block_size=64):
+    """Stage 1: per-block key means, (B, H, nb, D) fp32, plus the (2, B, H, nb,
+    D) bf16 hi/lo split the tensor-core scorer reads."""
+    L = _require_backend()
+    B, H, N, D = K.shape
+    assert N % block_size == 0, f"seq_len {N} must be divisible by block_size {block_size}"
+    Kc = K.contiguous()
+    p = problem(B, H, N, D, False, block_size, 1)
+    nb = N // block_size
+    with torch.cuda.device(K.device):
+        K_repr = torch.empty(B, H, nb, D, dtype=torch.float32, device=K.device)
+        K_split = torch.empty(2, B, H, nb, D, dtype=torch.bfloat16, device=K.device)
+        _lib.check(L.bsa_pool_k(ctypes.byref(p), _ptr(Kc), _ptr(K_repr), _ptr(K_split),
+                                _stream(K.device)), VARIANT)
+    return K_repr, K_split
+
+
+def select_blocks(Q, K, causal=False, block_size=64, top_k=16, *, flags=0):
+    """Stages 1-3: the selected blocks of every query row, (B, H, N, top_k)
+    int32 in ascending block order, -1 in slots left empty (fewer than top_k
+    eligible blocks)."""
+    L = _require_backend()
+    B, H, N, D = Q.shape
+    assert N % block_size == 0, f"seq_len {N} must be divisible by block_size {block_size}"
+    assert top_k <= N // block_size, f"top_k {top_k} exceeds num_blocks {N // block_size}"
+    K_repr, K_split = pool_k(K, block_size)
+    Qc = Q.contiguous()
+    p = problem(B, H, N, D, causal, block_size, top_k, flags)
+    with torch.cuda.device(Q.device):
+        idx = torch.empty(B, H, N, top_k, dtype=torch.int32, device=Q.device)
+        _lib.check(L.bsa_select_blocks(ctypes.byref(p), _ptr(Qc), _ptr(K_repr), _ptr(K_split),
+                                       _ptr(idx), _stream(Q.device)), VARIANT)
+    return idx
+
+
+def fine(Q, K, V, idx, causal=False, block_size=64, *, flags=0):
+    """Stage 4: attention of every query over the blocks ``idx`` lists."""
+    L = _require_backend()
+    B, H, N, D = Q.shape
+    top_k = idx.shape[-1]
+    _check_inputs(Q, K, V)
+    Qc, Kc, Vc = Q.contiguous(), K.contiguous(), V.contiguous()
+    idxc = idx.to(torch.int32).contiguous()
+    p = problem(B, H, N, D, causal, block_size, top_k, flags)
+    with torch.cuda.device(Q.device):
+        O = torch.empty_like(Qc)
+        need = L.bsa_fine_workspace_bytes(ctypes.byref(p))
+        ws = torch.empty(max(need, 16), dtype=torch.uint8, device=Q.device)
+        _lib.check(L.bsa_fine(ctypes.byref(p), _ptr(Qc), _ptr(Kc), _ptr(Vc), _ptr(idxc), _ptr(O),
+                              _ptr(ws), ctypes.c_size_t(ws.numel()), _stream(Q.device)), VARIANT)
+    return O

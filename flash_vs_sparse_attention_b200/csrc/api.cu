@@ -1,0 +1,246 @@
+// C ABI entry points (include/bsattn.h): validation, workspace layout and the
+// stage sequence of one forward pass.
+#include <cstdarg>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+#include "launchers.cuh"
+
+namespace bsa {
+
+static thread_local std::string g_last_error;
+
+static int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+static int cuda_fail(cudaError_t e, const char* what) {
+  return fail(BSA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+static int check(const bsa_problem* p) {
+  if (p == nullptr) return fail(BSA_ERR_INVALID, "problem is NULL");
+  if (p->batch < 1 || p->heads < 1 || p->seq_len < 1 || p->head_dim < 1)
+    return fail(BSA_ERR_INVALID, "dimensions must be positive (B=%d H=%d N=%d D=%d)", p->batch,
+                p->heads, p->seq_len, p->head_dim);
+  if (p->block_size < 1) return fail(BSA_ERR_INVALID, "block_size %d must be positive", p->block_size);
+  if (p->seq_len % p->block_size != 0)
+    return fail(BSA_ERR_INVALID, "seq_len %d must be divisible by block_size %d", p->seq_len,
+                p->block_size);
+  const int nb = p->seq_len / p->block_size;
+  if (p->top_k < 1 || p->top_k > nb)
+    return fail(BSA_ERR_INVALID, "top_k %d exceeds num_blocks %d", p->top_k, nb);
+  if (p->causal != 0 && p->causal != 1) return fail(BSA_ERR_INVALID, "causal must be 0 or 1");
+  if (p->head_dim % 8 != 0 || p->head_dim > 256)
+    return fail(BSA_ERR_UNSUPPORTED, "head_dim %d must be a multiple of 8 and at most 256",
+                p->head_dim);
+  if (p->top_k > 64) return fail(BSA_ERR_UNSUPPORTED, "top_k %d above 64 is not supported", p->top_k);
+  if ((int64_t)p->batch * p->heads > (1 << 30) || (int64_t)p->seq_len * p->top_k > (1LL << 31) - 1)
+    return fail(BSA_ERR_UNSUPPORTED, "problem too large for 32-bit list indices");
+  return BSA_OK;
+}
+
+static Shape make_shape(const bsa_problem* p, int units) {
+  Shape s;
+  s.units = units;
+  s.N = p->seq_len;
+  s.D = p->head_dim;
+  s.bs = p->block_size;
+  s.nb = p->seq_len / p->block_size;
+  s.k = p->top_k;
+  s.causal = p->causal;
+  s.scale = p->scale > 0.f ? p->scale : 1.0f / sqrtf((float)p->head_dim);
+  return s;
+}
+
+static bool aligned16(const void* ptr) { return ((uintptr_t)ptr & 15u) == 0; }
+
+// ---------------------------------------------------------------------------
+// Workspace layout for `units` units per pass.  Every region is 256-byte
+// aligned.  Regions of the tensor-core fine stage are present only when that
+// stage will run.
+struct Layout {
+  size_t krepr, khi, klo, idx, fine, total;
+  size_t fine_bytes;
+};
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static Layout layout_for(const bsa_problem* p, int64_t units) {
+  Shape s = make_shape(p, (int)units);
+  Layout L;
+  size_t off = 0;
+  L.krepr = off; off = align256(off + sizeof(float) * units * s.nb * s.D);
+  L.khi = off;   off = align256(off + 2 * (size_t)units * s.nb * s.D);
+  L.klo = off;   off = align256(off + 2 * (size_t)units * s.nb * s.D);
+  L.idx = off;   off = align256(off + sizeof(int32_t) * (size_t)units * s.N * s.k);
+  L.fine_bytes = fine_workspace_bytes(s, p->flags);
+  L.fine = off;  off = align256(off + L.fine_bytes);
+  L.total = off;
+  return L;
+}
+
+static int64_t total_units(const bsa_problem* p) { return (int64_t)p->batch * p->heads; }
+
+}  // namespace bsa
+
+using namespace bsa;
+
+extern "C" {
+
+int bsa_abi_version(void) { return BSA_ABI_VERSION; }
+
+const char* bsa_status_string(int status) {
+  switch (status) {
+    case BSA_OK: return "ok";
+    case BSA_ERR_INVALID: return "invalid problem";
+    case BSA_ERR_UNSUPPORTED: return "unsupported problem";
+    case BSA_ERR_ALIGNMENT: return "misaligned pointer";
+    case BSA_ERR_WORKSPACE: return "workspace too small";
+    case BSA_ERR_CUDA: return "CUDA error";
+    default: return "unknown status";
+  }
+}
+
+const char* bsa_last_error(void) { return g_last_error.c_str(); }
+
+int bsa_check_problem(const bsa_problem* p) {
+  g_last_error.clear();
+  return check(p);
+}
+
+size_t bsa_workspace_bytes(const bsa_problem* p, int64_t units_per_pass) {
+  if (check(p) != BSA_OK) return 0;
+  int64_t U = total_units(p);
+  int64_t g = (units_per_pass <= 0 || units_per_pass > U) ? U : units_per_pass;
+  return layout_for(p, g).total;
+}
+
+size_t bsa_fine_workspace_bytes(const bsa_problem* p) {
+  if (check(p) != BSA_OK) return 0;
+  return fine_workspace_bytes(make_shape(p, (int)total_units(p)), p->flags);
+}
+
+int bsa_forward_ex(const bsa_problem* p, const void* Q, const void* K, const void* V, void* O,
+                   void* workspace, size_t workspace_bytes, void* stream, void* const* events,
+                   int n_events, int* n_launches) {
+  g_last_error.clear();
+  int st = check(p);
+  if (st != BSA_OK) return st;
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O) || !aligned16(workspace))
+    return fail(BSA_ERR_ALIGNMENT, "Q, K, V, O and workspace must be 16-byte aligned");
+  const int64_t U = total_units(p);
+  // Largest number of units per pass whose workspace fits.
+  int64_t g = U;
+  while (g > 1 && layout_for(p, g).total > workspace_bytes) g = (g + 1) / 2;
+  Layout L = layout_for(p, g);
+  if (workspace == nullptr || L.total > workspace_bytes)
+    return fail(BSA_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu one unit needs",
+                workspace_bytes, L.total);
+  cudaStream_t s_ = (cudaStream_t)stream;
+  unsigned char* ws = (unsigned char*)workspace;
+  int launches = 0;
+  const size_t elems = (size_t)p->seq_len * p->head_dim;
+  for (int64_t u0 = 0; u0 < U; u0 += g) {
+    const int units = (int)((U - u0) < g ? (U - u0) : g);
+    Shape s = make_shape(p, units);
+    const __nv_bfloat16* q = (const __nv_bfloat16*)Q + u0 * elems;
+    const __nv_bfloat16* k = (const __nv_bfloat16*)K + u0 * elems;
+    const __nv_bfloat16* v = (const __nv_bfloat16*)V + u0 * elems;
+    __nv_bfloat16* o = (__nv_bfloat16*)O + u0 * elems;
+    float* krepr = (float*)(ws + L.krepr);
+    __nv_bfloat16* khi = (__nv_bfloat16*)(ws + L.khi);
+    __nv_bfloat16* klo = (__nv_bfloat16*)(ws + L.klo);
+    int32_t* idx = (int32_t*)(ws + L.idx);
+    const bool first = (u0 == 0);
+    auto mark = [&](int stage) {
+      if (first && events != nullptr && stage < n_events && events[stage] != nullptr)
+        cudaEventRecord((cudaEvent_t)events[stage], s_);
+    };
+    cudaError_t e = launch_pool_k(k, krepr, khi, klo, s, s_);
+    if (e != cudaSuccess) return cuda_fail(e, "pool_k launch");
+    ++launches;
+    mark(0);
+    int nl = 0;
+    e = launch_select(q, krepr, khi, klo, idx, s, p->flags, s_, &nl);
+    if (e != cudaSuccess) return cuda_fail(e, "select launch");
+    launches += nl;
+    mark(1);
+    nl = 0;
+    e = launch_fine(q, k, v, idx, o, ws + L.fine, L.fine_bytes, s, p->flags, s_, &nl,
+                    first ? events : nullptr, n_events);
+    if (e != cudaSuccess) return cuda_fail(e, "fine launch");
+    launches += nl;
+  }
+  if (n_launches) *n_launches = launches;
+  return BSA_OK;
+}
+
+int bsa_forward(const bsa_problem* p, const void* Q, const void* K, const void* V, void* O,
+                void* workspace, size_t workspace_bytes, void* stream) {
+  return bsa_forward_ex(p, Q, K, V, O, workspace, workspace_bytes, stream, nullptr, 0, nullptr);
+}
+
+int bsa_pool_k(const bsa_problem* p, const void* K, float* K_repr, void* K_split, void* stream) {
+  g_last_error.clear();
+  int st = check(p);
+  if (st != BSA_OK) return st;
+  if (!aligned16(K) || !aligned16(K_repr) || !aligned16(K_split))
+    return fail(BSA_ERR_ALIGNMENT, "K, K_repr and K_split must be 16-byte aligned");
+  Shape s = make_shape(p, (int)total_units(p));
+  __nv_bfloat16* hi = (__nv_bfloat16*)K_split;
+  __nv_bfloat16* lo = hi ? hi + (size_t)s.units * s.nb * s.D : nullptr;
+  cudaError_t e = launch_pool_k((const __nv_bfloat16*)K, K_repr, hi, lo, s, (cudaStream_t)stream);
+  return e == cudaSuccess ? BSA_OK : cuda_fail(e, "pool_k launch");
+}
+
+int bsa_select_blocks(const bsa_problem* p, const void* Q, const float* K_repr,
+                      const void* K_split, int32_t* idx, void* stream) {
+  g_last_error.clear();
+  int st = check(p);
+  if (st != BSA_OK) return st;
+  if (!aligned16(Q) || !aligned16(K_repr) || !aligned16(K_split) || !aligned16(idx))
+    return fail(BSA_ERR_ALIGNMENT, "Q, K_repr, K_split and idx must be 16-byte aligned");
+  Shape s = make_shape(p, (int)total_units(p));
+  const __nv_bfloat16* hi = (const __nv_bfloat16*)K_split;
+  const __nv_bfloat16* lo = hi ? hi + (size_t)s.units * s.nb * s.D : nullptr;
+  uint32_t flags = p->flags;
+  if (hi == nullptr && !(flags & BSA_FLAG_SIMT_SELECT) && select_uses_tensor_cores(s, flags))
+    return fail(BSA_ERR_INVALID, "K_split is required by the tensor-core scorer");
+  int nl = 0;
+  cudaError_t e = launch_select((const __nv_bfloat16*)Q, K_repr, hi, lo, idx, s, flags,
+                                (cudaStream_t)stream, &nl);
+  return e == cudaSuccess ? BSA_OK : cuda_fail(e, "select launch");
+}
+
+int bsa_fine(const bsa_problem* p, const void* Q, const void* K, const void* V, const int32_t* idx,
+             void* O, void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  int st = check(p);
+  if (st != BSA_OK) return st;
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O) || !aligned16(idx) ||
+      !aligned16(workspace))
+    return fail(BSA_ERR_ALIGNMENT, "Q, K, V, idx, O and workspace must be 16-byte aligned");
+  Shape s = make_shape(p, (int)total_units(p));
+  size_t need = fine_workspace_bytes(s, p->flags);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return fail(BSA_ERR_WORKSPACE, "fine stage needs %zu bytes of workspace, got %zu", need,
+                workspace_bytes);
+  int nl = 0;
+  cudaError_t e = launch_fine((const __nv_bfloat16*)Q, (const __nv_bfloat16*)K,
+                              (const __nv_bfloat16*)V, idx, (__nv_bfloat16*)O,
+                              (unsigned char*)workspace, need, s, p->flags, (cudaStream_t)stream,
+                              &nl, nullptr, 0);
+  return e == cudaSuccess ? BSA_OK : cuda_fail(e, "fine launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,56 @@
+// Shared helpers for the block-sparse attention kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/bsattn.h"
+
+namespace bsa {
+
+constexpr int kNumSMs = 148;  // B200
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Pack two floats to bf16x2 with round-to-nearest-even (low half = a).
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 1/ln(2): converts a natural-log-domain exponent to base 2.
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Problem shape derived once on the host and passed by value to kernels.
+struct Shape {
+  int32_t units;       // batch * heads processed by this launch
+  int32_t N;           // seq_len
+  int32_t D;           // head_dim
+  int32_t bs;          // block_size
+  int32_t nb;          // N / bs
+  int32_t k;           // top_k
+  int32_t causal;
+  float scale;
+};
+
+}  // namespace bsa

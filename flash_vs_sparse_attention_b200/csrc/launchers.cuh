@@ -1,0 +1,43 @@
+// Host-side launchers of every kernel, and the stage dispatchers.
+#pragma once
+
+#include "common.cuh"
+
+namespace bsa {
+
+// Stage 1 (pool.cu).
+cudaError_t launch_pool_k(const __nv_bfloat16* K, float* K_repr, __nv_bfloat16* K_hi,
+                          __nv_bfloat16* K_lo, const Shape& s, cudaStream_t st);
+
+// Stages 2-3 (select_simt.cu, select_tc.cu).
+cudaError_t launch_select_simt(const __nv_bfloat16* Q, const float* K_repr, int32_t* idx,
+                               const Shape& s, cudaStream_t st);
+bool select_tc_supported(const Shape& s);
+cudaError_t launch_select_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K_hi,
+                             const __nv_bfloat16* K_lo, int32_t* idx, const Shape& s,
+                             cudaStream_t st);
+
+// Stage 4 (fine_simt.cu, fine_kv.cu).
+cudaError_t launch_fine_simt(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                             const __nv_bfloat16* V, const int32_t* idx, __nv_bfloat16* O,
+                             const Shape& s, cudaStream_t st);
+bool fine_kv_supported(const Shape& s);
+size_t fine_kv_workspace_bytes(const Shape& s);
+cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                           const __nv_bfloat16* V, const int32_t* idx, __nv_bfloat16* O,
+                           unsigned char* ws, const Shape& s, cudaStream_t st, int* n_launches,
+                           void* const* events, int n_events);
+
+// Dispatchers (dispatch.cu).
+bool select_uses_tensor_cores(const Shape& s, uint32_t flags);
+bool fine_uses_tensor_cores(const Shape& s, uint32_t flags);
+cudaError_t launch_select(const __nv_bfloat16* Q, const float* K_repr, const __nv_bfloat16* K_hi,
+                          const __nv_bfloat16* K_lo, int32_t* idx, const Shape& s,
+                          uint32_t flags, cudaStream_t st, int* n_launches);
+size_t fine_workspace_bytes(const Shape& s, uint32_t flags);
+cudaError_t launch_fine(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
+                        const int32_t* idx, __nv_bfloat16* O, unsigned char* ws, size_t ws_bytes,
+                        const Shape& s, uint32_t flags, cudaStream_t st, int* n_launches,
+                        void* const* events, int n_events);
+
+}  // namespace bsa

@@ -1,0 +1,121 @@
+/*
+ * bsattn.h - C ABI of the B200 (sm_100a) two-stage content-adaptive
+ * block-sparse attention forward.
+ *
+ * The path replaces the reference's block-indexer variant
+ *   attention(Q, K, V, causal=False, block_size=64, top_k=16) -> O
+ * (attention/block_indexer_triton.py:86-146, same semantics as
+ *  attention/block_indexer.py:4-86):
+ *
+ *   1. K_repr[u, j, :] = mean of the block_size keys of block j   (pool)
+ *   2. coarse[u, i, j] = (Q[u, i, :] . K_repr[u, j, :]) * scale,
+ *      -inf when causal and j*block_size > i                        (score)
+ *   3. the top_k blocks of every query row i                        (select)
+ *   4. softmax attention of row i over the top_k*block_size keys of
+ *      its blocks, token-masked when causal                         (fine)
+ *
+ * Tensors are dense, row-major (batch, heads, seq_len, head_dim) bf16 in
+ * device memory (the reference's Triton path makes them contiguous too,
+ * block_indexer_triton.py:116-117,199).  Every entry point enqueues work on
+ * the given stream and returns without synchronising; none allocates device
+ * memory: scratch comes from the caller as a workspace of
+ * bsa_workspace_bytes() bytes.  No entry point throws; each returns a
+ * bsa_status.
+ */
+#ifndef BSATTN_H_
+#define BSATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BSA_ABI_VERSION 1
+
+typedef enum bsa_status {
+  BSA_OK = 0,
+  BSA_ERR_INVALID = 1,      /* contract violated: N % block_size, top_k > nb, ... */
+  BSA_ERR_UNSUPPORTED = 2,  /* valid but outside this build: head_dim % 8, top_k > 64 */
+  BSA_ERR_ALIGNMENT = 3,    /* a pointer is not 16-byte aligned */
+  BSA_ERR_WORKSPACE = 4,    /* workspace missing or smaller than required */
+  BSA_ERR_CUDA = 5          /* a CUDA runtime/driver call or launch failed */
+} bsa_status;
+
+/* Implementation choices a caller may force (tests compare the two). */
+#define BSA_FLAG_SIMT_SELECT 1u  /* CUDA-core coarse scoring + top-k */
+#define BSA_FLAG_SIMT_FINE 2u    /* query-stationary CUDA-core fine stage */
+
+typedef struct bsa_problem {
+  int32_t batch;       /* B */
+  int32_t heads;       /* H */
+  int32_t seq_len;     /* N, a multiple of block_size */
+  int32_t head_dim;    /* D, a multiple of 8, at most 256 */
+  int32_t block_size;  /* bs */
+  int32_t top_k;       /* k, 1 <= k <= min(64, N / bs) */
+  int32_t causal;      /* 0 or 1 */
+  float scale;         /* softmax scale; <= 0 selects head_dim ** -0.5 */
+  uint32_t flags;      /* BSA_FLAG_* (0 = fastest supported kernels) */
+} bsa_problem;
+
+/* ABI version of the loaded library (BSA_ABI_VERSION). */
+int bsa_abi_version(void);
+
+/* Static description of a status code. */
+const char* bsa_status_string(int status);
+
+/* Detail of the last error returned on the calling host thread ("" if none). */
+const char* bsa_last_error(void);
+
+/* Validate a problem without launching anything.  Mirrors the reference's
+ * asserts (block_indexer_triton.py:108-110; block_indexer.py:21-23). */
+int bsa_check_problem(const bsa_problem* p);
+
+/* Bytes of workspace bsa_forward needs to process `units_per_pass`
+ * (batch*head) units per pass (<= 0: all units in one pass). */
+size_t bsa_workspace_bytes(const bsa_problem* p, int64_t units_per_pass);
+
+/* One-shot forward: O = attention(Q, K, V).  Replaces
+ * block_indexer_triton.attention (block_indexer_triton.py:86-146).
+ * Units are processed in passes sized to fit `workspace_bytes`. */
+int bsa_forward(const bsa_problem* p, const void* Q, const void* K, const void* V,
+                void* O, void* workspace, size_t workspace_bytes, void* stream);
+
+/* bsa_forward with instrumentation: when `events` is non-NULL, records
+ * events[s] (cudaEvent_t) after stage s of the first pass (0 pool, 1 select,
+ * 2 bucket, 3 fine, 4 combine; n_events entries at most).  When
+ * `n_launches` is non-NULL it receives the number of kernels launched. */
+int bsa_forward_ex(const bsa_problem* p, const void* Q, const void* K, const void* V,
+                   void* O, void* workspace, size_t workspace_bytes, void* stream,
+                   void* const* events, int n_events, int* n_launches);
+
+/* Stage 1 alone (block_indexer_triton.py:120, block_indexer.py:33).
+ * K_repr: (B*H, nb, D) fp32 block means.  K_split: NULL, or (2, B*H, nb, D)
+ * bf16, the high and low bf16 parts of K_repr (hi + lo == K_repr to about
+ * 2^-17 relative) used by the tensor-core scorer. */
+int bsa_pool_k(const bsa_problem* p, const void* K, float* K_repr, void* K_split, void* stream);
+
+/* Stages 2-3 alone (block_indexer_triton.py:121-129, block_indexer.py:44-53):
+ * writes idx (B*H, N, top_k) int32, each row's selected blocks in ascending
+ * block order, -1 in slots left empty because fewer than top_k blocks are
+ * eligible.  Ties in the coarse score go to the lower block index.  Needs the
+ * outputs of bsa_pool_k (K_split may be NULL only with BSA_FLAG_SIMT_SELECT). */
+int bsa_select_blocks(const bsa_problem* p, const void* Q, const float* K_repr,
+                      const void* K_split, int32_t* idx, void* stream);
+
+/* Stage 4 alone (block_indexer_triton.py:132-145 and the Triton kernel
+ * _fine_attn_fwd, :12-83): O from Q, K, V and a selection `idx` laid out as
+ * bsa_select_blocks writes it (any order within a row; -1 = empty). */
+int bsa_fine(const bsa_problem* p, const void* Q, const void* K, const void* V,
+             const int32_t* idx, void* O, void* workspace, size_t workspace_bytes,
+             void* stream);
+
+/* Bytes of workspace bsa_fine needs for all units at once. */
+size_t bsa_fine_workspace_bytes(const bsa_problem* p);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BSATTN_H_ */

@@ -1,0 +1,56 @@
+"""Parity helpers shared by the GPU tests (test infrastructure: uses the oracle)."""
+
+import numpy as np
+import torch
+
+from oracle import CONFIGS, index_parity, make_inputs
+from oracle.block_indexer_np import _fine_rows, pool_k
+
+# Output tolerance of the bf16 path against the fp32 oracle.
+MAX_ABS = 2e-2
+MEAN_ABS = 2e-3
+TAU = 1e-5
+
+
+def to_gpu(*arrays):
+    return [torch.from_numpy(np.ascontiguousarray(a)).to("cuda", torch.bfloat16) for a in arrays]
+
+
+def config_inputs(c, units=None, seed=0):
+    cfg = CONFIGS[c]
+    Q, K, V = make_inputs(cfg, seed=seed, units=units)
+    return cfg, Q, K, V
+
+
+def oracle_scores(q, k, rows, block_size, causal):
+    """(len(rows), nb) masked coarse scores of one unit from the oracle."""
+    D = q.shape[1]
+    kr = pool_k(k, block_size)
+    s = (q[rows] @ kr.T) * np.float32(D ** -0.5)
+    if causal:
+        starts = np.arange(kr.shape[0]) * block_size
+        s = np.where(starts[None, :] > np.asarray(rows)[:, None], np.float32(-np.inf), s)
+    return s.astype(np.float32)
+
+
+def check_indices(q, k, idx_rows, rows, block_size, top_k, causal):
+    """Tie-aware index parity of one unit's rows; returns (n_bad, n_tie)."""
+    sc = oracle_scores(q, k, rows, block_size, causal)
+    n_bad, n_tie, bad = index_parity(sc, idx_rows, top_k, TAU)
+    return n_bad, n_tie, bad
+
+
+def oracle_fine(q, k, v, idx_rows, rows, block_size, causal):
+    """The oracle's fine stage fed a given selection (block_indexer.py:55-84)."""
+    N, D = q.shape
+    nb = N // block_size
+    return _fine_rows(q[rows], k.reshape(nb, block_size, D), v.reshape(nb, block_size, D),
+                      np.asarray(idx_rows, np.int64), np.asarray(rows), causal, D ** -0.5)
+
+
+def assert_close_out(got, want, what=""):
+    err = np.abs(np.asarray(got, np.float32) - np.asarray(want, np.float32))
+    assert np.isfinite(got).all(), f"{what}: non-finite output"
+    assert err.max() <= MAX_ABS, f"{what}: max-abs {err.max():.3e} > {MAX_ABS}"
+    assert err.mean() <= MEAN_ABS, f"{what}: mean-abs {err.mean():.3e} > {MEAN_ABS}"
+    return float(err.max()), float(err.mean())

@@ -1,0 +1,120 @@
+"""End-to-end parity of the variant API against the oracle on the benchmark
+workloads, plus the reference's own GPU tests restated (GPU only)."""
+
+import numpy as np
+import pytest
+import torch
+
+from flash_vs_sparse_attention_b200 import _lib, block_indexer_b200 as bi
+from oracle import CONFIGS, attention_unit, make_inputs
+from parity import assert_close_out, check_indices, config_inputs, to_gpu
+
+pytestmark = pytest.mark.gpu
+
+B, H, N, D = 1, 2, 64, 32   # test_correctness.py:6
+
+
+def make_ref_inputs(dtype=torch.bfloat16, device="cuda"):
+    torch.manual_seed(42)
+    return [torch.randn(B, H, N, D, dtype=dtype, device=device) for _ in range(3)]
+
+
+def dense(Q, K, V, causal=False):
+    s = (Q.float() @ K.float().transpose(-1, -2)) * Q.shape[-1] ** -0.5
+    if causal:
+        n = Q.shape[-2]
+        s = s.masked_fill(torch.triu(torch.ones(n, n, dtype=torch.bool, device=Q.device), 1), float("-inf"))
+    return torch.softmax(s, -1) @ V.float()
+
+
+def test_output_shape(cuda):
+    """test_correctness.py:110-115"""
+    Q, K, V = make_ref_inputs()
+    assert bi.attention(Q, K, V, block_size=8, top_k=4).shape == (B, H, N, D)
+
+
+def test_finite(cuda):
+    """test_correctness.py:118-123"""
+    Q, K, V = make_ref_inputs()
+    out = bi.attention(Q, K, V, causal=False, block_size=8, top_k=4)
+    assert torch.isfinite(out).all()
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_degenerate_matches_dense(cuda, causal):
+    """test_correctness.py:126-133: top_k == num_blocks is dense attention."""
+    Q, K, V = make_ref_inputs()
+    out = bi.attention(Q, K, V, causal=causal, block_size=8, top_k=8)
+    torch.testing.assert_close(dense(Q, K, V, causal).to(torch.bfloat16), out, atol=1e-2, rtol=0)
+
+
+def test_asserts_and_errors(cuda):
+    Q, K, V = make_ref_inputs()
+    with pytest.raises(AssertionError, match="divisible"):
+        bi.attention(Q, K, V, block_size=7, top_k=4)
+    with pytest.raises(AssertionError, match="exceeds num_blocks"):
+        bi.attention(Q, K, V, block_size=8, top_k=9)
+    with pytest.raises(TypeError):
+        bi.attention(Q.float(), K.float(), V.float(), block_size=8, top_k=4)
+    with pytest.raises(_lib.BsaError):
+        Qo = torch.randn(1, 1, 64, 60, dtype=torch.bfloat16, device="cuda")
+        bi.attention(Qo, Qo, Qo, block_size=8, top_k=4)
+
+
+def run_config(c, units, rows_per_unit=None, flags=0, seed=0):
+    cfg, Q, K, V = config_inputs(c, units=units, seed=seed)
+    Qg, Kg, Vg = to_gpu(Q, K, V)
+    out = bi.attention(Qg, Kg, Vg, causal=cfg["causal"], block_size=cfg["block_size"],
+                       top_k=cfg["top_k"], flags=flags).float().cpu().numpy()
+    idx = bi.select_blocks(Qg, Kg, causal=cfg["causal"], block_size=cfg["block_size"],
+                           top_k=cfg["top_k"], flags=flags).cpu().numpy()
+    n = cfg["N"]
+    errs = []
+    for i in range(len(units)):
+        if rows_per_unit is None:
+            rows = np.arange(n)
+        else:
+            rng = np.random.default_rng(i)
+            rows = np.unique(np.concatenate([np.arange(min(n, 2 * cfg["block_size"])),
+                                             rng.choice(n, rows_per_unit, replace=False), [n - 1]]))
+        want = attention_unit(Q[0, i], K[0, i], V[0, i], cfg["causal"], cfg["block_size"],
+                              cfg["top_k"], rows=rows)
+        n_bad, n_tie, bad = check_indices(Q[0, i], K[0, i], idx[0, i][rows], rows,
+                                          cfg["block_size"], cfg["top_k"], cfg["causal"])
+        assert n_bad == 0, f"config {c} unit {units[i]}: {n_bad} rows with other blocks {bad[:5]}"
+        # Output parity on rows whose selection is unambiguous.
+        errs.append(assert_close_out(out[0, i][rows], want, f"config {c} unit {units[i]}"))
+    return errs
+
+
+def test_config1_full(cuda):
+    run_config(1, units=list(range(8)))
+
+
+def test_config2_full(cuda):
+    run_config(2, units=list(range(8)), rows_per_unit=None)
+
+
+def test_config3_sampled(cuda):
+    run_config(3, units=[0, 5], rows_per_unit=1024)
+
+
+@pytest.mark.slow
+def test_config4_sampled(cuda):
+    run_config(4, units=[0, 37], rows_per_unit=512)
+
+
+@pytest.mark.slow
+def test_config5_sampled(cuda):
+    run_config(5, units=[0, 11], rows_per_unit=512)
+
+
+def test_flags_agree_on_config3_unit(cuda):
+    """The tensor-core and CUDA-core paths give the same output to bf16 noise."""
+    cfg, Q, K, V = config_inputs(3, units=[2])
+    Qg, Kg, Vg = to_gpu(Q, K, V)
+    a = bi.attention(Qg, Kg, Vg, causal=True).float()
+    simt = _lib.BSA_FLAG_SIMT_SELECT | _lib.BSA_FLAG_SIMT_FINE
+    b = bi.attention(Qg, Kg, Vg, causal=True, flags=simt).float()
+    d = (a - b).abs()
+    assert d.max().item() <= 2e-2 and d.mean().item() <= 1e-3

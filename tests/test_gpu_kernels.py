@@ -1,0 +1,80 @@
+"""Per-stage parity of the CUDA kernels against the CPU oracle (GPU only)."""
+
+import numpy as np
+import pytest
+import torch
+
+from flash_vs_sparse_attention_b200 import _lib, block_indexer_b200 as bi
+from oracle import pool_k as oracle_pool_k
+from parity import assert_close_out, check_indices, config_inputs, oracle_fine, to_gpu
+
+pytestmark = pytest.mark.gpu
+
+SIMT = _lib.BSA_FLAG_SIMT_SELECT | _lib.BSA_FLAG_SIMT_FINE
+
+# (B, H, N, D, block_size, top_k, causal)
+SHAPES = [
+    (1, 2, 64, 32, 8, 4, False),      # the reference's test shape (test_correctness.py:6,65-67)
+    (1, 2, 64, 32, 8, 4, True),
+    (1, 2, 64, 32, 8, 8, True),       # top_k == num_blocks
+    (1, 2, 2048, 64, 64, 16, True),
+    (2, 1, 2048, 64, 64, 1, False),   # top_k = 1
+    (1, 2, 4096, 128, 64, 32, True),
+    (1, 1, 8192, 64, 128, 16, True),
+    (1, 1, 1024, 96, 32, 5, True),    # odd head_dim / top_k
+]
+
+
+def rand_inputs(B, H, N, D, seed=0):
+    rng = np.random.default_rng(seed)
+    from oracle import round_to_bf16
+    return [round_to_bf16(rng.standard_normal((B, H, N, D), dtype=np.float32)) for _ in range(3)]
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+def test_pool_k(cuda, shape):
+    B, H, N, D, bs, k, causal = shape
+    _, K, _ = rand_inputs(B, H, N, D)
+    (Kg,) = to_gpu(K)
+    K_repr, K_split = bi.pool_k(Kg, bs)
+    want = oracle_pool_k(K, bs)
+    got = K_repr.cpu().numpy()
+    np.testing.assert_allclose(got, want, rtol=2e-6, atol=1e-7)
+    hi = K_split[0].float().cpu().numpy()
+    lo = K_split[1].float().cpu().numpy()
+    np.testing.assert_allclose(hi + lo, got, rtol=2 ** -15, atol=1e-30)
+
+
+@pytest.mark.parametrize("flags", [0, SIMT])
+@pytest.mark.parametrize("shape", SHAPES)
+def test_select_blocks_index_parity(cuda, shape, flags):
+    B, H, N, D, bs, k, causal = shape
+    Q, K, _ = rand_inputs(B, H, N, D, seed=1)
+    Qg, Kg = to_gpu(Q, K)
+    idx = bi.select_blocks(Qg, Kg, causal=causal, block_size=bs, top_k=k, flags=flags).cpu().numpy()
+    rows = np.arange(N)
+    for b in range(B):
+        for h in range(H):
+            n_bad, n_tie, bad = check_indices(Q[b, h], K[b, h], idx[b, h], rows, bs, k, causal)
+            assert n_bad == 0, f"unit ({b},{h}): {n_bad} rows differ, e.g. {bad[:5]}"
+            # the emitted order is ascending block order, -1 last
+            row = idx[b, h]
+            valid = np.where(row < 0, np.iinfo(np.int32).max, row)
+            assert np.all(np.diff(valid, axis=1) > 0)
+
+
+@pytest.mark.parametrize("flags", [0, SIMT])
+@pytest.mark.parametrize("shape", SHAPES)
+def test_fine_stage_given_indices(cuda, shape, flags):
+    """Fine stage fed the GPU's own selection vs the oracle's fine stage."""
+    B, H, N, D, bs, k, causal = shape
+    Q, K, V = rand_inputs(B, H, N, D, seed=2)
+    Qg, Kg, Vg = to_gpu(Q, K, V)
+    idx = bi.select_blocks(Qg, Kg, causal=causal, block_size=bs, top_k=k, flags=flags)
+    O = bi.fine(Qg, Kg, Vg, idx, causal=causal, block_size=bs, flags=flags).float().cpu().numpy()
+    idx = idx.cpu().numpy()
+    rows = np.arange(N)
+    for b in range(B):
+        for h in range(H):
+            want = oracle_fine(Q[b, h], K[b, h], V[b, h], idx[b, h], rows, bs, causal)
+            assert_close_out(O[b, h], want, f"unit ({b},{h})")
