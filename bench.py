@@ -239,6 +239,12 @@ def run_ours(args, cfg):
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     stage_ev = [[torch.cuda.Event(enable_timing=True) for _ in STAGES] for _ in range(args.steps)]
+    # torch creates the CUDA event on its first record; create them all now so
+    # the C ABI can record them by handle inside the timed region.
+    for evs in stage_ev:
+        for e in evs:
+            e.record(stream)
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
