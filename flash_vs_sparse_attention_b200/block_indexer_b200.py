@@ -79,8 +79,16 @@ def workspace_bytes(p, cap=DEFAULT_WORKSPACE_CAP):
     return L.bsa_workspace_bytes(pp, g)
 
 
+def _raise_on_kernel_error(L, p, ws, from_forward):
+    bits = ctypes.c_uint32(0)
+    _lib.check(L.bsa_workspace_error(ctypes.byref(p), _ptr(ws), ctypes.c_size_t(ws.numel()),
+                                     int(from_forward), ctypes.byref(bits)), VARIANT)
+    if bits.value:
+        raise RuntimeError(f"{VARIANT}: fine-stage kernel stopped early (error bits 0x{bits.value:x})")
+
+
 def attention(Q, K, V, causal=False, block_size=64, top_k=16, *, flags=0,
-              workspace_cap=DEFAULT_WORKSPACE_CAP):
+              workspace_cap=DEFAULT_WORKSPACE_CAP, check_errors=False):
     """
     Q, K, V: (batch, heads, seq_len, head_dim) bf16 CUDA tensors
     returns: (batch, heads, seq_len, head_dim) bf16
@@ -105,6 +113,8 @@ def attention(Q, K, V, causal=False, block_size=64, top_k=16, *, flags=0,
         st = L.bsa_forward(ctypes.byref(p), _ptr(Qc), _ptr(Kc), _ptr(Vc), _ptr(O), _ptr(ws),
                            ctypes.c_size_t(ws.numel()), _stream(Q.device))
         _lib.check(st, VARIANT)
+        if check_errors:
+            _raise_on_kernel_error(L, p, ws, True)
     return O
 
 
@@ -143,7 +153,7 @@ def select_blocks(Q, K, causal=False, block_size=64, top_k=16, *, flags=0):
     return idx
 
 
-def fine(Q, K, V, idx, causal=False, block_size=64, *, flags=0):
+def fine(Q, K, V, idx, causal=False, block_size=64, *, flags=0, check_errors=True):
     """Stage 4: attention of every query over the blocks ``idx`` lists."""
     L = _require_backend()
     B, H, N, D = Q.shape
@@ -158,4 +168,6 @@ def fine(Q, K, V, idx, causal=False, block_size=64, *, flags=0):
         ws = torch.empty(max(need, 16), dtype=torch.uint8, device=Q.device)
         _lib.check(L.bsa_fine(ctypes.byref(p), _ptr(Qc), _ptr(Kc), _ptr(Vc), _ptr(idxc), _ptr(O),
                               _ptr(ws), ctypes.c_size_t(ws.numel()), _stream(Q.device)), VARIANT)
+        if check_errors:
+            _raise_on_kernel_error(L, p, ws, False)
     return O

@@ -243,4 +243,31 @@ int bsa_fine(const bsa_problem* p, const void* Q, const void* K, const void* V, 
   return e == cudaSuccess ? BSA_OK : cuda_fail(e, "fine launch");
 }
 
+int bsa_workspace_error(const bsa_problem* p, const void* workspace, size_t workspace_bytes,
+                        int from_forward, uint32_t* error_bits) {
+  g_last_error.clear();
+  int st = check(p);
+  if (st != BSA_OK) return st;
+  if (error_bits == nullptr) return fail(BSA_ERR_INVALID, "error_bits is NULL");
+  *error_bits = 0;
+  int64_t units = total_units(p);
+  size_t base = 0;
+  if (from_forward) {
+    int64_t g = units;
+    while (g > 1 && layout_for(p, g).total > workspace_bytes) g = (g + 1) / 2;
+    Layout L = layout_for(p, g);
+    if (L.total > workspace_bytes) return fail(BSA_ERR_WORKSPACE, "workspace too small");
+    units = g;
+    base = L.fine;
+  }
+  Shape s = make_shape(p, (int)units);
+  if (!fine_uses_tensor_cores(s, p->flags)) return BSA_OK;
+  size_t off = base + fine_kv_error_offset(s);
+  if (workspace == nullptr || off + 4 > workspace_bytes)
+    return fail(BSA_ERR_WORKSPACE, "workspace too small");
+  cudaError_t e = cudaMemcpy(error_bits, (const unsigned char*)workspace + off, 4,
+                             cudaMemcpyDeviceToHost);
+  return e == cudaSuccess ? BSA_OK : cuda_fail(e, "reading the error word");
+}
+
 }  // extern "C"

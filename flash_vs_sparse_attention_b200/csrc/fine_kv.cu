@@ -1,0 +1,620 @@
+// Stage 4 on tcgen05 tensor cores, key-block-stationary.
+// (Replaces block_indexer.py:55-84 / the Triton kernel _fine_attn_fwd,
+//  block_indexer_triton.py:12-83, with the same arithmetic.)
+//
+// Per-token selections barely overlap on unstructured inputs: the 64 queries
+// of a query tile pick ~15x top_k distinct blocks between them, so a
+// query-stationary tile would do nearly dense work.  Turned around, every key
+// block is picked by ~N*top_k/num_blocks queries, which fills 128-row MMA
+// tiles.  The stage therefore runs as:
+//
+//  1. bucket_count   per-unit histogram of the selected block ids
+//  2. bucket_scan    per block: list offset and 128-query work items
+//  3. bucket_scatter list entries (query row << 6 | slot) grouped by block
+//  4. fine_kv        persistent kernel over work items.  For each item (one
+//                    key block, <= 128 queries that picked it): TMA loads the
+//                    block's K and V tiles, TMA gather4 loads the 128 query
+//                    rows, tcgen05 computes S = Q K^T into TMEM, a softmax
+//                    warpgroup turns its row of S into P (bf16, shared
+//                    memory) with the row's max m and sum l, tcgen05 computes
+//                    O = P V into TMEM, and the warpgroup writes the partial
+//                    (O / l as bf16, m, l) for that (query, slot).
+//  5. combine        per query: log-sum-exp merge of its top_k partials,
+//                    rounded to bf16 once.
+//
+// fine_kv warp roles (320 threads): warps 0-3 and 4-7 are two softmax /
+// epilogue warpgroups that take alternate work items (buffer g = item & 1), so
+// one group's exponentials overlap the other's MMAs and stores; warp 8 issues
+// TMA; one thread of warp 9 issues the MMAs.  All waits are bounded.
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+
+#include "common.cuh"
+#include "launchers.cuh"
+#include "sm100.cuh"
+
+namespace bsa {
+
+using namespace sm100;
+
+constexpr int kTileRows = 128;      // queries per work item (MMA M)
+constexpr int kRowsPerBucketCta = 1024;
+constexpr int kMaxNbKv = 32768;
+
+// Error codes ORed into the workspace error word.
+enum : uint32_t {
+  kErrWaitQ = 1u, kErrWaitS = 2u, kErrWaitP = 4u, kErrWaitO = 8u, kErrWaitFree = 16u,
+  kErrWaitDrain = 32u
+};
+
+struct FineWs {
+  int32_t* counts;     // units * nb
+  int32_t* cursors;    // units * nb
+  uint32_t* err;       // [0] error bits, [1] total work items
+  int32_t* offsets;    // units * nb
+  int4* items;         // units * max_items_per_unit
+  int32_t* lists;      // units * N * k
+  __nv_bfloat16* part_o;  // units * N * k * D
+  float2* part_ml;     // units * N * k
+  size_t zero_bytes;   // counts + cursors + err, contiguous from counts
+  size_t total;
+};
+
+static size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static int64_t max_items_per_unit(const Shape& s) {
+  return ((int64_t)s.N * s.k + kTileRows - 1) / kTileRows + s.nb;
+}
+
+static FineWs fine_ws_layout(const Shape& s, unsigned char* base) {
+  FineWs w;
+  size_t off = 0;
+  const size_t U = s.units, nb = s.nb, Nk = (size_t)s.N * s.k;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = a256(off + bytes);
+    return base ? base + o : nullptr;
+  };
+  w.counts = (int32_t*)take(4 * U * nb);
+  w.cursors = (int32_t*)take(4 * U * nb);
+  w.err = (uint32_t*)take(16);
+  w.zero_bytes = off;
+  w.offsets = (int32_t*)take(4 * U * nb);
+  w.items = (int4*)take(16 * U * (size_t)max_items_per_unit(s));
+  w.lists = (int32_t*)take(4 * U * Nk);
+  w.part_o = (__nv_bfloat16*)take(2 * U * Nk * s.D);
+  w.part_ml = (float2*)take(8 * U * Nk);
+  w.total = off;
+  return w;
+}
+
+bool fine_kv_supported(const Shape& s) {
+  const bool shape_ok = (s.bs == 64 && (s.D == 64 || s.D == 128)) || (s.bs == 128 && s.D == 64);
+  return shape_ok && s.k <= 64 && s.nb <= kMaxNbKv && s.N < (1 << 25) &&
+         (int64_t)s.units * s.N * s.k < (1LL << 31);
+}
+
+size_t fine_kv_workspace_bytes(const Shape& s) { return fine_ws_layout(s, nullptr).total; }
+
+size_t fine_kv_error_offset(const Shape& s) {
+  // counts and cursors precede the error word, each 256-byte aligned.
+  return 2 * a256(4 * (size_t)s.units * s.nb);
+}
+
+// ---------------------------------------------------------------------------
+// 1. Histogram of selected block ids per unit.
+__global__ void __launch_bounds__(256)
+bucket_count_kernel(const int32_t* __restrict__ idx, int32_t* __restrict__ counts, Shape s) {
+  extern __shared__ int32_t hist[];
+  const int u = blockIdx.y;
+  for (int j = threadIdx.x; j < s.nb; j += blockDim.x) hist[j] = 0;
+  __syncthreads();
+  const int64_t row0 = (int64_t)blockIdx.x * kRowsPerBucketCta;
+  const int64_t e0 = ((int64_t)u * s.N + row0) * s.k;
+  const int64_t ne = (int64_t)min((int64_t)kRowsPerBucketCta, s.N - row0) * s.k;
+  for (int64_t e = threadIdx.x; e < ne; e += blockDim.x) {
+    int j = idx[e0 + e];
+    if (j >= 0) atomicAdd(&hist[j], 1);
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < s.nb; j += blockDim.x)
+    if (hist[j]) atomicAdd(&counts[(int64_t)u * s.nb + j], hist[j]);
+}
+
+// 2. Per unit: exclusive scan of counts -> list offsets, and work items of at
+//    most 128 queries per block.  One CTA of 1024 threads per unit.
+__global__ void __launch_bounds__(1024)
+bucket_scan_kernel(const int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
+                   int4* __restrict__ items, uint32_t* __restrict__ err, Shape s,
+                   int64_t max_items) {
+  __shared__ int32_t wsum_c[32], wsum_t[32];
+  __shared__ int32_t item_base;
+  const int u = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (s.nb + blockDim.x - 1) / blockDim.x;
+  const int j0 = tid * per, j1 = min(s.nb, j0 + per);
+  const int32_t* c = counts + (int64_t)u * s.nb;
+  int sc = 0, st = 0;
+  for (int j = j0; j < j1; ++j) {
+    sc += c[j];
+    st += (c[j] + kTileRows - 1) / kTileRows;
+  }
+  // Block-wide exclusive scans of (sc, st).
+  int ic = sc, it = st;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int a = __shfl_up_sync(0xffffffffu, ic, o), b = __shfl_up_sync(0xffffffffu, it, o);
+    if (lane >= o) { ic += a; it += b; }
+  }
+  if (lane == 31) { wsum_c[warp] = ic; wsum_t[warp] = it; }
+  __syncthreads();
+  if (warp == 0) {
+    int a = wsum_c[lane], b = wsum_t[lane];
+    int ia = a, ib = b;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int x = __shfl_up_sync(0xffffffffu, ia, o), y = __shfl_up_sync(0xffffffffu, ib, o);
+      if (lane >= o) { ia += x; ib += y; }
+    }
+    wsum_c[lane] = ia - a;
+    wsum_t[lane] = ib - b;
+    if (lane == 31) item_base = (int)atomicAdd(&err[1], (uint32_t)ib);
+  }
+  __syncthreads();
+  int oc = wsum_c[warp] + ic - sc;   // exclusive prefix of this thread's chunk
+  int ot = wsum_t[warp] + it - st;
+  const int64_t list_base = (int64_t)u * s.N * s.k;
+  int4* out = items + item_base;
+  for (int j = j0; j < j1; ++j) {
+    const int cj = c[j];
+    offsets[(int64_t)u * s.nb + j] = oc;
+    for (int t = 0; t * kTileRows < cj; ++t) {
+      out[ot++] = make_int4(u, j, (int)(list_base + oc + t * kTileRows), min(kTileRows, cj - t * kTileRows));
+    }
+    oc += cj;
+  }
+  (void)max_items;
+}
+
+// 3. List entries grouped by block: entry = query_row << 6 | slot.
+__global__ void __launch_bounds__(256)
+bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ offsets,
+                      int32_t* __restrict__ cursors, int32_t* __restrict__ lists, Shape s) {
+  extern __shared__ int32_t hist[];
+  const int u = blockIdx.y;
+  for (int j = threadIdx.x; j < s.nb; j += blockDim.x) hist[j] = 0;
+  __syncthreads();
+  const int64_t row0 = (int64_t)blockIdx.x * kRowsPerBucketCta;
+  const int64_t e0 = ((int64_t)u * s.N + row0) * s.k;
+  const int64_t ne = (int64_t)min((int64_t)kRowsPerBucketCta, s.N - row0) * s.k;
+  for (int64_t e = threadIdx.x; e < ne; e += blockDim.x) {
+    int j = idx[e0 + e];
+    if (j >= 0) atomicAdd(&hist[j], 1);
+  }
+  __syncthreads();
+  // Reserve this CTA's range in every block's list.
+  for (int j = threadIdx.x; j < s.nb; j += blockDim.x) {
+    int n = hist[j];
+    if (n) {
+      int64_t g = (int64_t)u * s.nb + j;
+      hist[j] = offsets[g] + atomicAdd(&cursors[g], n);
+    }
+  }
+  __syncthreads();
+  int32_t* ul = lists + (int64_t)u * s.N * s.k;
+  for (int64_t e = threadIdx.x; e < ne; e += blockDim.x) {
+    int j = idx[e0 + e];
+    if (j >= 0) {
+      int pos = atomicAdd(&hist[j], 1);
+      int64_t le = row0 * s.k + e;  // entry index within the unit
+      int row = (int)(le / s.k), slot = (int)(le % s.k);
+      ul[pos] = (row << 6) | slot;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 4. The tensor-core fine kernel.
+template <int BS, int HD>
+struct KvCfg {
+  static constexpr int kQBytes = kTileRows * HD * 2;   // gathered queries
+  static constexpr int kKBytes = BS * HD * 2;          // key block
+  static constexpr int kVBytes = BS * HD * 2;          // value block
+  static constexpr int kPBytes = kTileRows * BS * 2;   // probabilities (bf16)
+  static constexpr int kBufBytes = kQBytes + kKBytes + kVBytes + kPBytes;
+  static constexpr int kSmem = 2 * kBufBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kTmemCols = (2 * (BS + HD) <= 256) ? 256 : 512;
+  static constexpr uint32_t kTxBytes = kQBytes + kKBytes + kVBytes;
+  static constexpr int kThreads = 320;
+};
+
+struct FineKvParams {
+  const int4* items;
+  const int32_t* lists;
+  const uint32_t* total_items;  // device word written by bucket_scan
+  __nv_bfloat16* part_o;
+  float2* part_ml;
+  uint32_t* err;
+  Shape s;
+};
+
+template <int BS, int HD>
+__global__ void __launch_bounds__(320, 1)
+fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+               const __grid_constant__ CUtensorMap tmap_v, FineKvParams prm) {
+  using C = KvCfg<BS, HD>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  // Barriers after the two buffers.
+  uint64_t* bars = (uint64_t*)(smem + 2 * C::kBufBytes);
+  uint64_t* q_full = bars + 0;   // [2] TMA landed (Q rows + K + V)
+  uint64_t* s_full = bars + 2;   // [2] S = QK^T in TMEM
+  uint64_t* p_full = bars + 4;   // [2] P in smem, S consumed (128 arrivals)
+  uint64_t* o_full = bars + 6;   // [2] O = PV in TMEM, smem buffer consumed
+  uint64_t* o_free = bars + 8;   // [2] O loaded by the warpgroup (128 arrivals)
+  uint64_t* drain = bars + 10;   // [1] final MMA completion
+  uint32_t* tmem_slot = (uint32_t*)(bars + 12);
+  volatile int* abort_flag = (volatile int*)(bars + 13);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Shape s = prm.s;
+  const uint32_t total = *prm.total_items;
+  const uint32_t G = gridDim.x;
+  const uint32_t t_begin = (uint32_t)(((uint64_t)total * blockIdx.x) / G);
+  const uint32_t t_end = (uint32_t)(((uint64_t)total * (blockIdx.x + 1)) / G);
+  const int T = (int)(t_end - t_begin);
+  if (T <= 0) return;
+
+  if (threadIdx.x == 0) {
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(&q_full[g], 1);
+      mbar_init(&s_full[g], 1);
+      mbar_init(&p_full[g], 128);
+      mbar_init(&o_full[g], 1);
+      mbar_init(&o_free[g], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8 && lane == 0) {
+    prefetch_tensormap(&tmap_q);
+    prefetch_tensormap(&tmap_k);
+    prefetch_tensormap(&tmap_v);
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  auto buf = [&](int g) { return smem + g * C::kBufBytes; };
+  auto q_s = [&](int g) { return buf(g); };
+  auto k_s = [&](int g) { return buf(g) + C::kQBytes; };
+  auto v_s = [&](int g) { return buf(g) + C::kQBytes + C::kKBytes; };
+  auto p_s = [&](int g) { return buf(g) + C::kQBytes + C::kKBytes + C::kVBytes; };
+  const float sc = s.scale * kLog2e;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    int issued = 0;
+    for (int t = 0; t < T; ++t) {
+      const int g = t & 1;
+      if (t >= 2) {
+        bool ok = mbar_wait(&o_free[g], ((t - 2) >> 1) & 1, prm.err, kErrWaitFree);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok || *abort_flag) { *abort_flag = 1; break; }
+      }
+      const int4 it = prm.items[t_begin + t];
+      const int u = it.x, j = it.y, start = it.z, cnt = it.w;
+      if (lane == 0) mbar_arrive_expect_tx(&q_full[g], C::kTxBytes);
+      __syncwarp();
+      // Four query rows per lane; rows past the item's count repeat its first.
+      int32_t ys[4];
+      const int32_t first = prm.lists[start] >> 6;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = lane * 4 + i;
+        const int32_t row = (r < cnt) ? (prm.lists[start + r] >> 6) : first;
+        ys[i] = u * s.N + row;
+      }
+#pragma unroll
+      for (int p = 0; p < HD / 64; ++p)
+        tma_gather4(q_s(g) + p * (kTileRows * 128) + lane * 4 * 128, &tmap_q, &q_full[g], p * 64,
+                    ys[0], ys[1], ys[2], ys[3]);
+      if (lane == 0) {
+        const int32_t y = u * s.N + j * BS;
+#pragma unroll
+        for (int p = 0; p < HD / 64; ++p) {
+          tma_load_2d(k_s(g) + p * (BS * 128), &tmap_k, &q_full[g], p * 64, y);
+          tma_load_2d(v_s(g) + p * (BS * 128), &tmap_v, &q_full[g], p * 64, y);
+        }
+      }
+      issued = t + 1;
+    }
+    // Drain: wait (bounded) for the loads this warp issued but nobody consumed.
+    if (*abort_flag && lane == 0) {
+      for (int t = (issued >= 2 ? issued - 2 : 0); t < issued; ++t)
+        mbar_wait(&q_full[t & 1], (t >> 1) & 1, nullptr, 0);
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_f32(kTileRows, BS, false);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(kTileRows, HD, true);
+      auto issue_s = [&](int t) -> bool {
+        const int g = t & 1;
+        if (!mbar_wait(&q_full[g], (t >> 1) & 1, prm.err, kErrWaitQ)) return false;
+        tc_fence_after();
+        const uint32_t d = tbase + g * (BS + HD);
+        const uint32_t qa = smem_u32(q_s(g)), ka = smem_u32(k_s(g));
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (kTileRows * 128) + (kk & 3) * 32;
+          const uint32_t offk = (kk >> 2) * (BS * 128) + (kk & 3) * 32;
+          mma_bf16(d, smem_desc_sw128(qa + off, 16, 1024), smem_desc_sw128(ka + offk, 16, 1024),
+                   idesc_s, kk > 0);
+        }
+        mma_commit(&s_full[g]);
+        return true;
+      };
+      auto issue_o = [&](int t) -> bool {
+        const int g = t & 1;
+        if (!mbar_wait(&p_full[g], (t >> 1) & 1, prm.err, kErrWaitP)) return false;
+        tc_fence_after();
+        const uint32_t d = tbase + g * (BS + HD) + BS;
+        const uint32_t pa = smem_u32(p_s(g)), va = smem_u32(v_s(g));
+#pragma unroll
+        for (int kk = 0; kk < BS / 16; ++kk) {
+          const uint32_t offp = (kk >> 2) * (kTileRows * 128) + (kk & 3) * 32;
+          const uint32_t offv = kk * 16 * 128;
+          mma_bf16(d, smem_desc_sw128(pa + offp, 16, 1024),
+                   smem_desc_sw128(va + offv, BS * 128, 1024), idesc_o, kk > 0);
+        }
+        mma_commit(&o_full[g]);
+        return true;
+      };
+      bool ok = issue_s(0);
+      for (int t = 0; ok && t < T; ++t) {
+        if (t + 1 < T) ok = issue_s(t + 1);
+        if (ok) ok = issue_o(t);
+        if (*abort_flag) ok = false;
+      }
+      if (!ok) *abort_flag = 1;
+      // Make sure no MMA is in flight when TMEM is released.
+      mma_commit(drain);
+      mbar_wait(drain, 0, prm.err, kErrWaitDrain);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax / epilogue
+    const int wg = warp >> 2;              // 0 or 1: takes items t with t & 1 == wg
+    const int quad = warp & 3;             // TMEM lane quadrant
+    const int r = quad * 32 + lane;        // row of the tile this thread owns
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    for (int t = wg; t < T; t += 2) {
+      const int g = wg;
+      const int n = t >> 1;
+      const int4 it = prm.items[t_begin + t];
+      const int u = it.x, j = it.y, start = it.z, cnt = it.w;
+      const bool valid = r < cnt;
+      const int32_t e = valid ? prm.lists[start + r] : 0;
+      const int qrow = e >> 6, slot = e & 63;
+
+      bool ok = mbar_wait(&s_full[g], n & 1, prm.err, kErrWaitS);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || *abort_flag) { *abort_flag = 1; break; }
+      tc_fence_after();
+      float sv[BS];
+      const uint32_t s_addr = tbase + lane_off + g * (BS + HD);
+#pragma unroll
+      for (int c = 0; c < BS; c += 64) tmem_ld64(s_addr + c, sv + c);
+      // Token-level causal mask (block_indexer.py:73-81): key > query -> -inf.
+      const int key0 = j * BS;
+      if (s.causal && key0 + BS - 1 > qrow) {
+#pragma unroll
+        for (int c = 0; c < BS; ++c)
+          if (key0 + c > qrow) sv[c] = -INFINITY;
+      }
+      float m0 = sv[0], m1 = sv[1], m2 = sv[2], m3 = sv[3];
+#pragma unroll
+      for (int c = 4; c < BS; c += 4) {
+        m0 = fmaxf(m0, sv[c]); m1 = fmaxf(m1, sv[c + 1]);
+        m2 = fmaxf(m2, sv[c + 2]); m3 = fmaxf(m3, sv[c + 3]);
+      }
+      const float m = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+      // Padding rows of a short item can be fully masked; keep them finite.
+      const float msc = (m == -INFINITY) ? 0.f : m * sc;
+      float l0 = 0.f, l1 = 0.f;
+      unsigned char* prow = p_s(g) + r * 128;
+#pragma unroll
+      for (int c = 0; c < BS; c += 8) {
+        float p[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) p[i] = fast_exp2(fmaf(sv[c + i], sc, -msc));
+        l0 += (p[0] + p[1]) + (p[2] + p[3]);
+        l1 += (p[4] + p[5]) + (p[6] + p[7]);
+        uint4 w = make_uint4(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]),
+                             pack_bf16x2(p[4], p[5]), pack_bf16x2(p[6], p[7]));
+        const int panel = c >> 6, chunk = (c & 63) >> 3;
+        *reinterpret_cast<uint4*>(prow + panel * (kTileRows * 128) + ((chunk ^ (r & 7)) << 4)) = w;
+      }
+      const float l = l0 + l1;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[g]);
+
+      ok = mbar_wait(&o_full[g], n & 1, prm.err, kErrWaitO);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || *abort_flag) { *abort_flag = 1; break; }
+      tc_fence_after();
+      float ov[HD];
+      const uint32_t o_addr = tbase + lane_off + g * (BS + HD) + BS;
+#pragma unroll
+      for (int c = 0; c < HD; c += 64) tmem_ld64(o_addr + c, ov + c);
+      tc_fence_before();
+      mbar_arrive(&o_free[g]);
+      if (valid) {
+        const float inv = 1.f / l;
+        const int64_t pe = ((int64_t)u * s.N + qrow) * s.k + slot;
+        uint4* dst = reinterpret_cast<uint4*>(prm.part_o + pe * HD);
+#pragma unroll
+        for (int c = 0; c < HD; c += 8) {
+          dst[c >> 3] = make_uint4(pack_bf16x2(ov[c] * inv, ov[c + 1] * inv),
+                                   pack_bf16x2(ov[c + 2] * inv, ov[c + 3] * inv),
+                                   pack_bf16x2(ov[c + 4] * inv, ov[c + 5] * inv),
+                                   pack_bf16x2(ov[c + 6] * inv, ov[c + 7] * inv));
+        }
+        prm.part_ml[pe] = make_float2(msc, l);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tbase, C::kTmemCols);
+}
+
+// 5. Per query: merge its partials (m in the base-2 domain, l, O / l).
+template <int HD>
+__global__ void __launch_bounds__(256)
+combine_kernel(const int32_t* __restrict__ idx, const __nv_bfloat16* __restrict__ part_o,
+               const float2* __restrict__ part_ml, __nv_bfloat16* __restrict__ O, Shape s) {
+  constexpr int CH = HD / 8;  // 16-byte chunks per row
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t R = gid / CH;  // global query row (unit * N + row)
+  const int c = (int)(gid % CH);
+  if (R >= (int64_t)s.units * s.N) return;
+  const int32_t* sel = idx + R * s.k;
+  float M = -INFINITY;
+  for (int q = 0; q < s.k; ++q)
+    if (__ldg(sel + q) >= 0) M = fmaxf(M, __ldg(&part_ml[R * s.k + q].x));
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float L = 0.f;
+  for (int q = 0; q < s.k; ++q) {
+    if (__ldg(sel + q) < 0) continue;
+    const float2 ml = __ldg(&part_ml[R * s.k + q]);
+    const float w = ml.y * fast_exp2(ml.x - M);
+    L += w;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(part_o + (R * s.k + q) * HD) + c);
+    acc[0] = fmaf(w, bf16_lo(v.x), acc[0]); acc[1] = fmaf(w, bf16_hi(v.x), acc[1]);
+    acc[2] = fmaf(w, bf16_lo(v.y), acc[2]); acc[3] = fmaf(w, bf16_hi(v.y), acc[3]);
+    acc[4] = fmaf(w, bf16_lo(v.z), acc[4]); acc[5] = fmaf(w, bf16_hi(v.z), acc[5]);
+    acc[6] = fmaf(w, bf16_lo(v.w), acc[6]); acc[7] = fmaf(w, bf16_hi(v.w), acc[7]);
+  }
+  const float inv = 1.f / L;
+  reinterpret_cast<uint4*>(O + R * HD)[c] =
+      make_uint4(pack_bf16x2(acc[0] * inv, acc[1] * inv), pack_bf16x2(acc[2] * inv, acc[3] * inv),
+                 pack_bf16x2(acc[4] * inv, acc[5] * inv), pack_bf16x2(acc[6] * inv, acc[7] * inv));
+}
+
+// ---------------------------------------------------------------------------
+// Host side.
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major (rows, cols) matrix, 128-byte swizzle,
+// box of 64 columns x box_rows rows.
+static bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols,
+                     uint32_t box_rows) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = kNumSMs;
+  }
+  return n;
+}
+
+template <int BS, int HD>
+static cudaError_t launch_kv_kernel(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                    const __nv_bfloat16* V, const FineWs& w, const Shape& s,
+                                    cudaStream_t st) {
+  using C = KvCfg<BS, HD>;
+  CUtensorMap mq, mk, mv;
+  const uint64_t rows = (uint64_t)s.units * s.N;
+  if (!make_map(&mq, Q, rows, HD, 1) || !make_map(&mk, K, rows, HD, BS) ||
+      !make_map(&mv, V, rows, HD, BS))
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(fine_kv_kernel<BS, HD>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  if (e != cudaSuccess) return e;
+  FineKvParams prm;
+  prm.items = w.items;
+  prm.lists = w.lists;
+  prm.total_items = w.err + 1;
+  prm.part_o = w.part_o;
+  prm.part_ml = w.part_ml;
+  prm.err = w.err;
+  prm.s = s;
+  fine_kv_kernel<BS, HD><<<num_sms(), C::kThreads, C::kSmem, st>>>(mq, mk, mv, prm);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                           const __nv_bfloat16* V, const int32_t* idx, __nv_bfloat16* O,
+                           unsigned char* ws, const Shape& s, cudaStream_t st, int* n_launches,
+                           void* const* events, int n_events) {
+  FineWs w = fine_ws_layout(s, ws);
+  auto mark = [&](int i) {
+    if (events != nullptr && i < n_events && events[i] != nullptr)
+      cudaEventRecord((cudaEvent_t)events[i], st);
+  };
+  cudaError_t e = cudaMemsetAsync(w.counts, 0, w.zero_bytes, st);
+  if (e != cudaSuccess) return e;
+  const size_t hist_smem = sizeof(int32_t) * s.nb;
+  dim3 bgrid((s.N + kRowsPerBucketCta - 1) / kRowsPerBucketCta, s.units);
+  if (hist_smem > 48 * 1024) {
+    cudaFuncSetAttribute(bucket_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)hist_smem);
+    cudaFuncSetAttribute(bucket_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)hist_smem);
+  }
+  bucket_count_kernel<<<bgrid, 256, hist_smem, st>>>(idx, w.counts, s);
+  bucket_scan_kernel<<<s.units, 1024, 0, st>>>(w.counts, w.offsets, w.items, w.err, s,
+                                               max_items_per_unit(s));
+  bucket_scatter_kernel<<<bgrid, 256, hist_smem, st>>>(idx, w.offsets, w.cursors, w.lists, s);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  mark(2);
+  if (s.bs == 64 && s.D == 64) e = launch_kv_kernel<64, 64>(Q, K, V, w, s, st);
+  else if (s.bs == 64 && s.D == 128) e = launch_kv_kernel<64, 128>(Q, K, V, w, s, st);
+  else if (s.bs == 128 && s.D == 64) e = launch_kv_kernel<128, 64>(Q, K, V, w, s, st);
+  else e = cudaErrorNotSupported;
+  if (e != cudaSuccess) return e;
+  mark(3);
+  const int64_t threads = (int64_t)s.units * s.N * (s.D / 8);
+  const unsigned blocks = (unsigned)((threads + 255) / 256);
+  if (s.D == 64) combine_kernel<64><<<blocks, 256, 0, st>>>(idx, w.part_o, w.part_ml, O, s);
+  else combine_kernel<128><<<blocks, 256, 0, st>>>(idx, w.part_o, w.part_ml, O, s);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  mark(4);
+  *n_launches = 5;
+  return cudaSuccess;
+}
+
+}  // namespace bsa

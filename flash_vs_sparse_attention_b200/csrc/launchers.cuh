@@ -23,6 +23,7 @@ cudaError_t launch_fine_simt(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                              const Shape& s, cudaStream_t st);
 bool fine_kv_supported(const Shape& s);
 size_t fine_kv_workspace_bytes(const Shape& s);
+size_t fine_kv_error_offset(const Shape& s);  // byte offset of the error word
 cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                            const __nv_bfloat16* V, const int32_t* idx, __nv_bfloat16* O,
                            unsigned char* ws, const Shape& s, cudaStream_t st, int* n_launches,

@@ -114,6 +114,13 @@ int bsa_fine(const bsa_problem* p, const void* Q, const void* K, const void* V,
 /* Bytes of workspace bsa_fine needs for all units at once. */
 size_t bsa_fine_workspace_bytes(const bsa_problem* p);
 
+/* Error bits the tensor-core fine stage left in a workspace (0 = clean; a
+ * set bit names a pipeline wait that timed out and made the kernel stop
+ * early).  `from_forward` selects a bsa_forward workspace (its last pass)
+ * rather than a bsa_fine one.  Synchronises with the device. */
+int bsa_workspace_error(const bsa_problem* p, const void* workspace, size_t workspace_bytes,
+                        int from_forward, uint32_t* error_bits);
+
 #ifdef __cplusplus
 }
 #endif

@@ -65,7 +65,7 @@ def run_config(c, units, rows_per_unit=None, flags=0, seed=0):
     cfg, Q, K, V = config_inputs(c, units=units, seed=seed)
     Qg, Kg, Vg = to_gpu(Q, K, V)
     out = bi.attention(Qg, Kg, Vg, causal=cfg["causal"], block_size=cfg["block_size"],
-                       top_k=cfg["top_k"], flags=flags).float().cpu().numpy()
+                       top_k=cfg["top_k"], flags=flags, check_errors=True).float().cpu().numpy()
     idx = bi.select_blocks(Qg, Kg, causal=cfg["causal"], block_size=cfg["block_size"],
                            top_k=cfg["top_k"], flags=flags).cpu().numpy()
     n = cfg["N"]
