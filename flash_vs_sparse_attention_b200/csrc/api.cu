@@ -166,18 +166,24 @@ int bsa_forward_ex(const bsa_problem* p, const void* Q, const void* K, const voi
       if (first && events != nullptr && stage < n_events && events[stage] != nullptr)
         cudaEventRecord((cudaEvent_t)events[stage], s_);
     };
-    cudaError_t e = launch_pool_k(k, krepr, khi, klo, s, s_);
+    // The pool kernel also clears the fine stage's counters and error word,
+    // and the scorer reports into that error word.
+    const bool kv = fine_uses_tensor_cores(s, p->flags);
+    void* zero = kv ? (void*)(ws + L.fine) : nullptr;
+    const size_t zero_bytes = kv ? fine_kv_zero_bytes(s) : 0;
+    uint32_t* err = kv ? (uint32_t*)(ws + L.fine + fine_kv_error_offset(s)) : nullptr;
+    cudaError_t e = launch_pool_k(k, krepr, khi, klo, s, s_, zero, zero_bytes);
     if (e != cudaSuccess) return cuda_fail(e, "pool_k launch");
     ++launches;
     mark(0);
     int nl = 0;
-    e = launch_select(q, krepr, khi, klo, idx, s, p->flags, s_, &nl);
+    e = launch_select(q, krepr, khi, klo, idx, err, s, p->flags, s_, &nl);
     if (e != cudaSuccess) return cuda_fail(e, "select launch");
     launches += nl;
     mark(1);
     nl = 0;
     e = launch_fine(q, k, v, idx, o, ws + L.fine, L.fine_bytes, s, p->flags, s_, &nl,
-                    first ? events : nullptr, n_events);
+                    first ? events : nullptr, n_events, kv);
     if (e != cudaSuccess) return cuda_fail(e, "fine launch");
     launches += nl;
   }
@@ -217,7 +223,7 @@ int bsa_select_blocks(const bsa_problem* p, const void* Q, const float* K_repr,
   if (hi == nullptr && !(flags & BSA_FLAG_SIMT_SELECT) && select_uses_tensor_cores(s, flags))
     return fail(BSA_ERR_INVALID, "K_split is required by the tensor-core scorer");
   int nl = 0;
-  cudaError_t e = launch_select((const __nv_bfloat16*)Q, K_repr, hi, lo, idx, s, flags,
+  cudaError_t e = launch_select((const __nv_bfloat16*)Q, K_repr, hi, lo, idx, nullptr, s, flags,
                                 (cudaStream_t)stream, &nl);
   return e == cudaSuccess ? BSA_OK : cuda_fail(e, "select launch");
 }
@@ -239,7 +245,7 @@ int bsa_fine(const bsa_problem* p, const void* Q, const void* K, const void* V, 
   cudaError_t e = launch_fine((const __nv_bfloat16*)Q, (const __nv_bfloat16*)K,
                               (const __nv_bfloat16*)V, idx, (__nv_bfloat16*)O,
                               (unsigned char*)workspace, need, s, p->flags, (cudaStream_t)stream,
-                              &nl, nullptr, 0);
+                              &nl, nullptr, 0, false);
   return e == cudaSuccess ? BSA_OK : cuda_fail(e, "fine launch");
 }
 

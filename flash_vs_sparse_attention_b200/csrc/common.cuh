@@ -5,7 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/bsattn.h"
+#include "bsattn.h"  // from include/ (-I)
 
 namespace bsa {
 

@@ -13,11 +13,11 @@ bool fine_uses_tensor_cores(const Shape& s, uint32_t flags) {
 }
 
 cudaError_t launch_select(const __nv_bfloat16* Q, const float* K_repr, const __nv_bfloat16* K_hi,
-                          const __nv_bfloat16* K_lo, int32_t* idx, const Shape& s,
+                          const __nv_bfloat16* K_lo, int32_t* idx, uint32_t* err, const Shape& s,
                           uint32_t flags, cudaStream_t st, int* n_launches) {
   *n_launches = 1;
   if (select_uses_tensor_cores(s, flags) && K_hi != nullptr)
-    return launch_select_tc(Q, K_hi, K_lo, idx, s, st);
+    return launch_select_tc(Q, K_hi, K_lo, idx, err, s, st);
   return launch_select_simt(Q, K_repr, idx, s, st);
 }
 
@@ -28,9 +28,9 @@ size_t fine_workspace_bytes(const Shape& s, uint32_t flags) {
 cudaError_t launch_fine(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
                         const int32_t* idx, __nv_bfloat16* O, unsigned char* ws, size_t ws_bytes,
                         const Shape& s, uint32_t flags, cudaStream_t st, int* n_launches,
-                        void* const* events, int n_events) {
+                        void* const* events, int n_events, bool pre_zeroed) {
   if (fine_uses_tensor_cores(s, flags) && ws_bytes >= fine_kv_workspace_bytes(s))
-    return launch_fine_kv(Q, K, V, idx, O, ws, s, st, n_launches, events, n_events);
+    return launch_fine_kv(Q, K, V, idx, O, ws, s, st, n_launches, events, n_events, pre_zeroed);
   // The CUDA-core path has no bucket or combine kernel: it is all "fine".
   *n_launches = 1;
   if (events != nullptr && n_events > 2 && events[2] != nullptr)

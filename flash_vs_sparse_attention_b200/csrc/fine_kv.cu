@@ -97,6 +97,8 @@ bool fine_kv_supported(const Shape& s) {
 
 size_t fine_kv_workspace_bytes(const Shape& s) { return fine_ws_layout(s, nullptr).total; }
 
+size_t fine_kv_zero_bytes(const Shape& s) { return fine_ws_layout(s, nullptr).zero_bytes; }
+
 size_t fine_kv_error_offset(const Shape& s) {
   // counts and cursors precede the error word, each 256-byte aligned.
   return 2 * a256(4 * (size_t)s.units * s.nb);
@@ -579,14 +581,14 @@ static cudaError_t launch_kv_kernel(const __nv_bfloat16* Q, const __nv_bfloat16*
 cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                            const __nv_bfloat16* V, const int32_t* idx, __nv_bfloat16* O,
                            unsigned char* ws, const Shape& s, cudaStream_t st, int* n_launches,
-                           void* const* events, int n_events) {
+                           void* const* events, int n_events, bool pre_zeroed) {
   FineWs w = fine_ws_layout(s, ws);
   auto mark = [&](int i) {
     if (events != nullptr && i < n_events && events[i] != nullptr)
       cudaEventRecord((cudaEvent_t)events[i], st);
   };
-  cudaError_t e = cudaMemsetAsync(w.counts, 0, w.zero_bytes, st);
-  if (e != cudaSuccess) return e;
+  cudaError_t e = cudaSuccess;
+  if (!pre_zeroed && (e = cudaMemsetAsync(w.counts, 0, w.zero_bytes, st)) != cudaSuccess) return e;
   const size_t hist_smem = sizeof(int32_t) * s.nb;
   dim3 bgrid((s.N + kRowsPerBucketCta - 1) / kRowsPerBucketCta, s.units);
   if (hist_smem > 48 * 1024) {

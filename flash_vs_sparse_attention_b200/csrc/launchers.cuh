@@ -6,16 +6,19 @@
 namespace bsa {
 
 // Stage 1 (pool.cu).
+// `zero`/`zero_bytes` (optional): a 16-byte-aligned region the kernel clears
+// on the way (the fine stage's counters), saving a memset launch.
 cudaError_t launch_pool_k(const __nv_bfloat16* K, float* K_repr, __nv_bfloat16* K_hi,
-                          __nv_bfloat16* K_lo, const Shape& s, cudaStream_t st);
+                          __nv_bfloat16* K_lo, const Shape& s, cudaStream_t st,
+                          void* zero = nullptr, size_t zero_bytes = 0);
 
 // Stages 2-3 (select_simt.cu, select_tc.cu).
 cudaError_t launch_select_simt(const __nv_bfloat16* Q, const float* K_repr, int32_t* idx,
                                const Shape& s, cudaStream_t st);
 bool select_tc_supported(const Shape& s);
 cudaError_t launch_select_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K_hi,
-                             const __nv_bfloat16* K_lo, int32_t* idx, const Shape& s,
-                             cudaStream_t st);
+                             const __nv_bfloat16* K_lo, int32_t* idx, uint32_t* err,
+                             const Shape& s, cudaStream_t st);
 
 // Stage 4 (fine_simt.cu, fine_kv.cu).
 cudaError_t launch_fine_simt(const __nv_bfloat16* Q, const __nv_bfloat16* K,
@@ -24,21 +27,22 @@ cudaError_t launch_fine_simt(const __nv_bfloat16* Q, const __nv_bfloat16* K,
 bool fine_kv_supported(const Shape& s);
 size_t fine_kv_workspace_bytes(const Shape& s);
 size_t fine_kv_error_offset(const Shape& s);  // byte offset of the error word
+size_t fine_kv_zero_bytes(const Shape& s);    // bytes to clear at the start of the region
 cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                            const __nv_bfloat16* V, const int32_t* idx, __nv_bfloat16* O,
                            unsigned char* ws, const Shape& s, cudaStream_t st, int* n_launches,
-                           void* const* events, int n_events);
+                           void* const* events, int n_events, bool pre_zeroed);
 
 // Dispatchers (dispatch.cu).
 bool select_uses_tensor_cores(const Shape& s, uint32_t flags);
 bool fine_uses_tensor_cores(const Shape& s, uint32_t flags);
 cudaError_t launch_select(const __nv_bfloat16* Q, const float* K_repr, const __nv_bfloat16* K_hi,
-                          const __nv_bfloat16* K_lo, int32_t* idx, const Shape& s,
+                          const __nv_bfloat16* K_lo, int32_t* idx, uint32_t* err, const Shape& s,
                           uint32_t flags, cudaStream_t st, int* n_launches);
 size_t fine_workspace_bytes(const Shape& s, uint32_t flags);
 cudaError_t launch_fine(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
                         const int32_t* idx, __nv_bfloat16* O, unsigned char* ws, size_t ws_bytes,
                         const Shape& s, uint32_t flags, cudaStream_t st, int* n_launches,
-                        void* const* events, int n_events);
+                        void* const* events, int n_events, bool pre_zeroed);
 
 }  // namespace bsa

@@ -4,9 +4,9 @@
 // 16-byte vectors (8 bf16 per lane, a full 128-byte line per 8 lanes when
 // D = 64), so a block of 64 keys is 16 fully coalesced vector loads per lane.
 // Sums are fp32; the mean is sum / bs as torch's mean computes it.  Besides
-// the fp32 means the kernel writes their split into two bf16 terms
-// (hi = bf16(mean), lo = bf16(mean - hi)) for the tensor-core scorer, whose
-// bf16 MMAs then reproduce fp32 coarse scores to ~2^-17 relative.
+// the fp32 means the kernel writes the split of mean * scale into two bf16
+// terms (hi = bf16(m), lo = bf16(m - hi)) for the tensor-core scorer, whose
+// bf16 MMAs then reproduce the scaled fp32 coarse scores to ~2^-17 relative.
 //
 // HBM-bound: reads N*D*2 bytes per unit, writes nb*D*(4+2+2).
 #include "common.cuh"
@@ -16,7 +16,12 @@ namespace bsa {
 __global__ void __launch_bounds__(256)
 pool_k_kernel(const __nv_bfloat16* __restrict__ K, float* __restrict__ K_repr,
               __nv_bfloat16* __restrict__ K_hi, __nv_bfloat16* __restrict__ K_lo,
-              Shape s, int lanes_per_row) {
+              Shape s, int lanes_per_row, uint4* __restrict__ zero, int64_t zero_words) {
+  {
+    const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < zero_words; i += nthreads)
+      zero[i] = make_uint4(0, 0, 0, 0);
+  }
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t total = (int64_t)s.units * s.nb;
@@ -63,10 +68,11 @@ pool_k_kernel(const __nv_bfloat16* __restrict__ K, float* __restrict__ K_repr,
       uint32_t hi[4], lo[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        __nv_bfloat16 h0 = __float2bfloat16_rn(m[2 * i]);
-        __nv_bfloat16 h1 = __float2bfloat16_rn(m[2 * i + 1]);
-        float r0 = m[2 * i] - __bfloat162float(h0);
-        float r1 = m[2 * i + 1] - __bfloat162float(h1);
+        const float a0 = m[2 * i] * s.scale, a1 = m[2 * i + 1] * s.scale;
+        __nv_bfloat16 h0 = __float2bfloat16_rn(a0);
+        __nv_bfloat16 h1 = __float2bfloat16_rn(a1);
+        float r0 = a0 - __bfloat162float(h0);
+        float r1 = a1 - __bfloat162float(h1);
         hi[i] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
         lo[i] = pack_bf16x2(r0, r1);
       }
@@ -77,14 +83,16 @@ pool_k_kernel(const __nv_bfloat16* __restrict__ K, float* __restrict__ K_repr,
 }
 
 cudaError_t launch_pool_k(const __nv_bfloat16* K, float* K_repr, __nv_bfloat16* K_hi,
-                          __nv_bfloat16* K_lo, const Shape& s, cudaStream_t st) {
+                          __nv_bfloat16* K_lo, const Shape& s, cudaStream_t st, void* zero,
+                          size_t zero_bytes) {
   int chunks = s.D >> 3;
   int lpr = 1;
   while (lpr < chunks) lpr <<= 1;
   const int64_t warps = (int64_t)s.units * s.nb;
   const int threads = 256;
   const int64_t blocks = (warps * 32 + threads - 1) / threads;
-  pool_k_kernel<<<(unsigned)blocks, threads, 0, st>>>(K, K_repr, K_hi, K_lo, s, lpr);
+  pool_k_kernel<<<(unsigned)blocks, threads, 0, st>>>(K, K_repr, K_hi, K_lo, s, lpr,
+                                                       (uint4*)zero, (int64_t)(zero_bytes / 16));
   return cudaGetLastError();
 }
 

@@ -29,8 +29,7 @@ select_simt_kernel(const __nv_bfloat16* __restrict__ Q, const float* __restrict_
 
   float* qT = reinterpret_cast<float*>(smem);                       // D x 64
   float* kt = qT + s.D * kSimtRows;                                 // 16 x D
-  float* bval = kt + kSimtTile * s.D;                               // cap x 64
-  int32_t* bidx = reinterpret_cast<int32_t*>(bval + cap * kSimtRows);
+  uint2* bbuf = reinterpret_cast<uint2*>(kt + kSimtTile * s.D);     // cap x 64
 
   // Stage Q rows (transposed).  Rows past N read as zero.
   const __nv_bfloat16* qbase = Q + ((int64_t)unit * s.N + row0) * s.D;
@@ -41,7 +40,7 @@ select_simt_kernel(const __nv_bfloat16* __restrict__ Q, const float* __restrict_
   }
 
   RowTopK<KCAP> sel;
-  sel.init(bval + t, bidx + t, kSimtRows, cap, s.k);
+  sel.init(bbuf + t, kSimtRows, cap, s.k);
 
   int last_row = min(row0 + kSimtRows, s.N) - 1;
   int nb_visit = s.causal ? min(s.nb, last_row / s.bs + 1) : s.nb;
@@ -79,7 +78,7 @@ select_simt_kernel(const __nv_bfloat16* __restrict__ Q, const float* __restrict_
 
 static size_t select_simt_smem(const Shape& s, int kcap) {
   return sizeof(float) * ((size_t)s.D * kSimtRows + (size_t)kSimtTile * s.D) +
-         (sizeof(float) + sizeof(int32_t)) * (size_t)topk_buffer_slots(kcap) * kSimtRows;
+         sizeof(uint2) * (size_t)topk_buffer_slots(kcap) * kSimtRows;
 }
 
 template <int KCAP>

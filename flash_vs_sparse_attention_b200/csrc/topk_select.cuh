@@ -1,9 +1,9 @@
 // Per-row streaming top-k with lowest-index tie break (block_indexer.py:53).
 //
 // One thread owns one query row.  Candidates arrive in ascending block order.
-// A candidate is appended to the thread's buffer (a column of shared memory,
-// so a warp's appends are bank-conflict free) only if it can still be in the
-// final top-k:
+// A candidate is appended to the thread's buffer -- a column of shared memory
+// holding packed (score bits, block index) pairs, so a warp's appends are
+// bank-conflict free -- only if it can still be in the final top-k:
 //   * x > theta_excl, the exact k-th largest value among the candidates seen
 //     so far (a later candidate equal to it loses the tie to the earlier,
 //     lower-index one), and
@@ -12,10 +12,12 @@
 // When the buffer is about to overflow it is compacted to its exact top-k
 // (values only, a 2*KCAP-op min/max insertion network per entry), which also
 // raises theta_excl.  Compaction keeps buffer order, so ties keep resolving
-// to the lowest index, and the final emission lists the selected blocks in
-// ascending block order.  -inf candidates (causally masked blocks) never
-// enter the buffer, so rows with fewer than k eligible blocks emit -1 in the
-// remaining slots.
+// to the lowest index.  The final emission sorts the surviving (score,
+// index) pairs as 64-bit keys with a bitonic network in registers and writes
+// the indices by descending score, ties by ascending index -- the order of
+// torch.topk(sorted=True) with its ties made deterministic.  -inf candidates
+// (causally masked blocks) never enter the buffer, so rows with fewer than k
+// eligible blocks emit -1 in the remaining slots.
 #pragma once
 
 #include "common.cuh"
@@ -24,8 +26,7 @@ namespace bsa {
 
 template <int KCAP>
 struct RowTopK {
-  float* bval;        // this thread's column: bval[slot * stride]
-  int32_t* bidx;
+  uint2* buf;         // this thread's column: buf[slot * stride]
   int stride;
   int cap;            // buffer slots
   int cnt;
@@ -33,9 +34,8 @@ struct RowTopK {
   float theta_excl;
   float theta_incl;
 
-  __device__ __forceinline__ void init(float* v, int32_t* i, int stride_, int cap_, int k_) {
-    bval = v;
-    bidx = i;
+  __device__ __forceinline__ void init(uint2* b, int stride_, int cap_, int k_) {
+    buf = b;
     stride = stride_;
     cap = cap_;
     cnt = 0;
@@ -44,12 +44,18 @@ struct RowTopK {
     theta_incl = -INFINITY;
   }
 
+  __device__ __forceinline__ bool passes(float x) const {
+    return x > theta_excl && x >= theta_incl;
+  }
+
+  // Append unconditionally (the caller checked passes()).
+  __device__ __forceinline__ void append(float x, int32_t j) {
+    buf[cnt * stride] = make_uint2(__float_as_uint(x), (uint32_t)j);
+    ++cnt;
+  }
+
   __device__ __forceinline__ void push(float x, int32_t j) {
-    if (x > theta_excl && x >= theta_incl) {
-      bval[cnt * stride] = x;
-      bidx[cnt * stride] = j;
-      ++cnt;
-    }
+    if (passes(x)) append(x, j);
   }
 
   // Make room for `incoming` more pushes.
@@ -61,41 +67,48 @@ struct RowTopK {
     theta_incl = fmaxf(theta_incl, lower_bound);
   }
 
-  // Reduce the buffer to its exact top-k, in buffer (= ascending index) order.
-  __device__ void compact() {
+  // Exact k-th largest value of the buffer: a descending min/max insertion
+  // network over KCAP registers (2 ops per cell and entry).  The entry loop
+  // is unrolled so the dependent chains of consecutive entries interleave.
+  __device__ __forceinline__ float kth_value(int* n_gt_out) const {
     float a[KCAP];
 #pragma unroll
     for (int p = 0; p < KCAP; ++p) a[p] = -INFINITY;
+#pragma unroll 4
     for (int e = 0; e < cnt; ++e) {
-      float x = bval[e * stride];
+      float x = __uint_as_float(buf[e * stride].x);
 #pragma unroll
       for (int p = 0; p < KCAP; ++p) {
-        float hi = fmaxf(a[p], x);
+        const float hi = fmaxf(a[p], x);
         x = fminf(a[p], x);
         a[p] = hi;
       }
     }
-    float T = -INFINITY;
+    float T = INFINITY;
     int n_gt = 0;
 #pragma unroll
-    for (int p = 0; p < KCAP; ++p) {
-      if (p == k - 1) T = a[p];
-    }
+    for (int p = 0; p < KCAP; ++p) T = fminf(T, p < k ? a[p] : INFINITY);
 #pragma unroll
     for (int p = 0; p < KCAP; ++p) n_gt += (p < k && a[p] > T) ? 1 : 0;
+    *n_gt_out = n_gt;
+    return T;
+  }
+
+  // Reduce the buffer to its exact top-k, in buffer (= ascending index) order.
+  __device__ __forceinline__ void compact() {
+    int n_gt;
+    const float T = kth_value(&n_gt);
     int keep_eq = k - n_gt;
     int w = 0;
+#pragma unroll 1
     for (int e = 0; e < cnt; ++e) {
-      float v = bval[e * stride];
-      int32_t j = bidx[e * stride];
-      bool take = v > T;
-      if (!take && v == T && keep_eq > 0) {
-        take = true;
-        --keep_eq;
-      }
+      const uint2 en = buf[e * stride];
+      const float v = __uint_as_float(en.x);
+      const bool eq = !(v > T) && (v == T) && keep_eq > 0;
+      const bool take = v > T || eq;
+      keep_eq -= eq ? 1 : 0;
       if (take) {
-        bval[w * stride] = v;
-        bidx[w * stride] = j;
+        buf[w * stride] = en;
         ++w;
       }
     }
@@ -103,15 +116,79 @@ struct RowTopK {
     theta_excl = fmaxf(theta_excl, T);
   }
 
-  // Final top-k, written as k int32 (ascending block order, -1 padded).
+  // Final top-k, written as k int32 by descending score (ties: ascending
+  // index), -1 padded.
   __device__ __forceinline__ void emit(int32_t* out) {
-    compact();
-    for (int s = 0; s < k; ++s) out[s] = s < cnt ? bidx[s * stride] : -1;
+    constexpr int SORTN = KCAP > 32 ? 64 : 32;
+    if (cnt > SORTN) compact();   // exact top-k, at most KCAP <= SORTN entries
+    uint64_t key[SORTN];
+#pragma unroll
+    for (int e = 0; e < SORTN; ++e) {
+      uint64_t kk = 0;
+      if (e < cnt) {
+        const uint2 en = buf[e * stride];
+        const uint32_t b = en.x;
+        const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+        kk = ((uint64_t)ord << 32) | (uint64_t)(0xFFFFFFFFu - en.y);
+      }
+      key[e] = kk;
+    }
+    bitonic_sort_desc<SORTN>(key);
+#pragma unroll
+    for (int e = 0; e < SORTN; ++e)
+      if (e < k) out[e] = e < cnt ? (int32_t)(0xFFFFFFFFu - (uint32_t)key[e]) : -1;
+    for (int e = SORTN; e < k; ++e) out[e] = -1;
+  }
+
+  template <int N>
+  __device__ __forceinline__ static void bitonic_sort_desc(uint64_t (&v)[N]) {
+#pragma unroll
+    for (int k2 = 2; k2 <= N; k2 <<= 1) {
+#pragma unroll
+      for (int j = k2 >> 1; j > 0; j >>= 1) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          const int l = i ^ j;
+          if (l > i) {
+            const uint64_t a = v[i], b = v[l];
+            const bool gt = a > b;
+            const uint64_t hi = gt ? a : b, lo = gt ? b : a;
+            if ((i & k2) == 0) { v[i] = hi; v[l] = lo; } else { v[i] = lo; v[l] = hi; }
+          }
+        }
+      }
+    }
   }
 };
 
 // Buffer slots per thread for a given KCAP: room for the top-k plus at least
 // two 32-candidate chunks between compactions.
-__host__ __device__ constexpr int topk_buffer_slots(int kcap) { return 2 * kcap + 32; }
+__host__ __device__ constexpr int topk_buffer_slots(int kcap) {
+  return kcap <= 32 ? 2 * kcap + 32 : kcap + 64;
+}
+
+// k-th largest of 32 values (1 <= k <= 32): bitonic sort, descending, in
+// registers; returns the min of the first k.
+__device__ __forceinline__ float kth_of_32(float (&v)[32], int k) {
+#pragma unroll
+  for (int k2 = 2; k2 <= 32; k2 <<= 1) {
+#pragma unroll
+    for (int j = k2 >> 1; j > 0; j >>= 1) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int l = i ^ j;
+        if (l > i) {
+          const float a = v[i], b = v[l];
+          const float hi = fmaxf(a, b), lo = fminf(a, b);
+          if ((i & k2) == 0) { v[i] = hi; v[l] = lo; } else { v[i] = lo; v[l] = hi; }
+        }
+      }
+    }
+  }
+  float T = INFINITY;
+#pragma unroll
+  for (int p = 0; p < 32; ++p) T = fminf(T, p < k ? v[p] : INFINITY);
+  return T;
+}
 
 }  // namespace bsa

@@ -6,7 +6,7 @@ import torch
 
 from flash_vs_sparse_attention_b200 import _lib, block_indexer_b200 as bi
 from oracle import pool_k as oracle_pool_k
-from parity import assert_close_out, check_indices, config_inputs, oracle_fine, to_gpu
+from parity import assert_close_out, check_indices, config_inputs, oracle_fine, oracle_scores, to_gpu
 
 pytestmark = pytest.mark.gpu
 
@@ -22,6 +22,10 @@ SHAPES = [
     (1, 2, 4096, 128, 64, 32, True),
     (1, 1, 8192, 64, 128, 16, True),
     (1, 1, 1024, 96, 32, 5, True),    # odd head_dim / top_k
+    (1, 1, 640, 64, 32, 12, True),    # partial 128-row tile, top_k not a multiple of 4
+    (1, 1, 256, 64, 16, 8, True),     # small blocks
+    (1, 1, 4096, 128, 64, 48, False), # top_k > 32 with head_dim 128
+    (1, 1, 4096, 64, 64, 64, True),   # top_k = 64
 ]
 
 
@@ -42,7 +46,9 @@ def test_pool_k(cuda, shape):
     np.testing.assert_allclose(got, want, rtol=2e-6, atol=1e-7)
     hi = K_split[0].float().cpu().numpy()
     lo = K_split[1].float().cpu().numpy()
-    np.testing.assert_allclose(hi + lo, got, rtol=2 ** -15, atol=1e-30)
+    scale = D ** -0.5
+    np.testing.assert_allclose(hi + lo, (got * np.float32(scale)).astype(np.float32), rtol=2 ** -15,
+                               atol=1e-30)
 
 
 @pytest.mark.parametrize("flags", [0, SIMT])
@@ -57,10 +63,13 @@ def test_select_blocks_index_parity(cuda, shape, flags):
         for h in range(H):
             n_bad, n_tie, bad = check_indices(Q[b, h], K[b, h], idx[b, h], rows, bs, k, causal)
             assert n_bad == 0, f"unit ({b},{h}): {n_bad} rows differ, e.g. {bad[:5]}"
-            # the emitted order is ascending block order, -1 only at the end
-            for row in idx[b, h]:
+            # emitted by descending coarse score, -1 only at the end
+            sc = oracle_scores(Q[b, h], K[b, h], rows, bs, causal)
+            for r, row in enumerate(idx[b, h]):
                 v = row[row >= 0]
-                assert np.all(np.diff(v) > 0) and np.all(row[len(v):] == -1), row
+                assert np.all(row[len(v):] == -1), row
+                s_row = sc[r, v]
+                assert np.all(np.diff(s_row) <= 1e-6), (r, row, s_row)
 
 
 @pytest.mark.parametrize("flags", [0, SIMT])
