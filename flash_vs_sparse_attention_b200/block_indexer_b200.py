@@ -137,8 +137,8 @@ def pool_k(K, block_size=64):
 
 def select_blocks(Q, K, causal=False, block_size=64, top_k=16, *, flags=0):
     """Stages 1-3: the selected blocks of every query row, (B, H, N, top_k)
-    int32 by descending coarse score (ties to the lower block index), -1 in
-    slots left empty (fewer than top_k eligible blocks)."""
+    int32 in ascending block order (ties in the coarse score go to the lower
+    block index), -1 in slots left empty (fewer than top_k eligible blocks)."""
     L = _require_backend()
     B, H, N, D = Q.shape
     assert N % block_size == 0, f"seq_len {N} must be divisible by block_size {block_size}"

@@ -218,20 +218,46 @@ bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict
 
 // ---------------------------------------------------------------------------
 // 4. The tensor-core fine kernel.
+//
+// 16 warps:
+//   0-3, 4-7  softmax/epilogue warpgroups; warpgroup g takes the items t with
+//             t % 2 == g and owns TMEM buffers S[g], O[g] and shared P[g]
+//   8-11      loader warpgroup: thread i gathers query row i of each item
+//             with 16-byte cp.async (the LSU path streams random 128-byte rows
+//             faster than TMA gather4 issues them) and stages the item's list
+//             entries for the softmax warpgroups
+//   12        TMA: the item's K and V tiles
+//   13        one thread issues the MMAs, S(t) and PV(t) each as soon as its
+//             inputs are ready
+// Shared memory holds a ring of NS load stages (Q rows, K, V, entries).  S
+// and O are read from TMEM 64 columns at a time, so every (block_size,
+// head_dim) pair fits in 128 registers per thread.
 template <int BS, int HD>
 struct KvCfg {
   static constexpr int kQBytes = kTileRows * HD * 2;   // gathered queries
   static constexpr int kKBytes = BS * HD * 2;          // key block
   static constexpr int kVBytes = BS * HD * 2;          // value block
   static constexpr int kPBytes = kTileRows * BS * 2;   // probabilities (bf16)
-  static constexpr int kBufBytes = kQBytes + kKBytes + kVBytes + kPBytes;
-  static constexpr int kSmem = 2 * kBufBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kStageBytes = kQBytes + kKBytes + kVBytes;
+  static constexpr int NS = (BS == 64 && HD == 64) ? 4 : (HD == 64 ? 3 : 2);
+  static constexpr int kMetaBytes = kTileRows * 4 + 16;      // entries + item
+  static constexpr int kRing = 256;          // staged work items per loader warp
+  static constexpr int kPOff = NS * kStageBytes;
+  static constexpr int kMetaOff = kPOff + 2 * kPBytes;
+  static constexpr int kRingOff = kMetaOff + NS * kMetaBytes;
+  static constexpr int kBarOff = kRingOff + 4 * kRing * 16;
+  static constexpr int kSmem = kBarOff + 256 + 1024 /*align*/;
   static constexpr int kTmemCols = (2 * (BS + HD) <= 256) ? 256 : 512;
-  static constexpr uint32_t kTxBytes = kQBytes + kKBytes + kVBytes;
-  static constexpr int kThreads = 320;
+  static constexpr uint32_t kKVBytes = kKBytes + kVBytes;
+  static constexpr int kLoaders = 128;
+  // ld_full completes on: each loader's entries-written arrive, each
+  // loader's cp.async-landed arrive, and the TMA warp's expect_tx arrive.
+  static constexpr int kLdFullCount = 2 * kLoaders + 1;
+  static constexpr int kThreads = 512;
 };
 
 struct FineKvParams {
+  const __nv_bfloat16* q;
   const int4* items;
   const int32_t* lists;
   const uint32_t* total_items;  // device word written by bucket_scan
@@ -242,22 +268,24 @@ struct FineKvParams {
 };
 
 template <int BS, int HD>
-__global__ void __launch_bounds__(320, 1)
-fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
-               const __grid_constant__ CUtensorMap tmap_v, FineKvParams prm) {
+__global__ void __launch_bounds__(512, 1)
+fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+               FineKvParams prm) {
   using C = KvCfg<BS, HD>;
+  constexpr int NS = C::NS;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  // Barriers after the two buffers.
-  uint64_t* bars = (uint64_t*)(smem + 2 * C::kBufBytes);
-  uint64_t* q_full = bars + 0;   // [2] TMA landed (Q rows + K + V)
-  uint64_t* s_full = bars + 2;   // [2] S = QK^T in TMEM
-  uint64_t* p_full = bars + 4;   // [2] P in smem, S consumed (128 arrivals)
-  uint64_t* o_full = bars + 6;   // [2] O = PV in TMEM, smem buffer consumed
-  uint64_t* o_free = bars + 8;   // [2] O loaded by the warpgroup (128 arrivals)
-  uint64_t* drain = bars + 10;   // [1] final MMA completion
-  uint32_t* tmem_slot = (uint32_t*)(bars + 12);
-  volatile int* abort_flag = (volatile int*)(bars + 13);
+  uint64_t* bars = (uint64_t*)(smem + C::kBarOff);
+  uint64_t* ld_full = bars;             // [NS] Q rows, K, V and entries of the stage's item landed
+  uint64_t* ld_empty = bars + NS;       // [NS] PV of the stage's item done
+  uint64_t* s_full = bars + 2 * NS;     // [2] S = QK^T in TMEM
+  uint64_t* p_full = bars + 2 * NS + 2; // [2] P in smem, S consumed (128 arrivals)
+  uint64_t* o_full = bars + 2 * NS + 4; // [2] O = PV in TMEM
+  uint64_t* o_free = bars + 2 * NS + 6; // [2] O loaded by the warpgroup (128 arrivals)
+  uint64_t* drain = bars + 2 * NS + 8;  // [1] final MMA completion
+  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * NS + 9);
+  volatile int* abort_flag = (volatile int*)(bars + 2 * NS + 10);
+  int4* ring = (int4*)(smem + C::kRingOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Shape s = prm.s;
@@ -269,8 +297,11 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
   if (T <= 0) return;
 
   if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&ld_full[i], C::kLdFullCount);
+      mbar_init(&ld_empty[i], 1);
+    }
     for (int g = 0; g < 2; ++g) {
-      mbar_init(&q_full[g], 1);
       mbar_init(&s_full[g], 1);
       mbar_init(&p_full[g], 128);
       mbar_init(&o_full[g], 1);
@@ -280,8 +311,7 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 8 && lane == 0) {
-    prefetch_tensormap(&tmap_q);
+  if (warp == 12 && lane == 0) {
     prefetch_tensormap(&tmap_k);
     prefetch_tensormap(&tmap_v);
   }
@@ -291,97 +321,156 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
-  auto buf = [&](int g) { return smem + g * C::kBufBytes; };
-  auto q_s = [&](int g) { return buf(g); };
-  auto k_s = [&](int g) { return buf(g) + C::kQBytes; };
-  auto v_s = [&](int g) { return buf(g) + C::kQBytes + C::kKBytes; };
-  auto p_s = [&](int g) { return buf(g) + C::kQBytes + C::kKBytes + C::kVBytes; };
+  auto q_s = [&](int st) { return smem + st * C::kStageBytes; };
+  auto k_s = [&](int st) { return smem + st * C::kStageBytes + C::kQBytes; };
+  auto v_s = [&](int st) { return smem + st * C::kStageBytes + C::kQBytes + C::kKBytes; };
+  auto p_s = [&](int g) { return smem + C::kPOff + g * C::kPBytes; };
+  auto meta = [&](int st) { return (int32_t*)(smem + C::kMetaOff + st * C::kMetaBytes); };
   const float sc = s.scale * kLog2e;
 
-  if (warp == 8) {
-    // ------------------------------------------------------------ producer
-    int issued = 0;
-    for (int t = 0; t < T; ++t) {
-      const int g = t & 1;
-      if (t >= 2) {
-        bool ok = mbar_wait(&o_free[g], ((t - 2) >> 1) & 1, prm.err, kErrWaitFree);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok || *abort_flag) { *abort_flag = 1; break; }
-      }
-      const int4 it = prm.items[t_begin + t];
-      const int u = it.x, j = it.y, start = it.z, cnt = it.w;
-      if (lane == 0) mbar_arrive_expect_tx(&q_full[g], C::kTxBytes);
+  if (warp >= 8 && warp < 12) {
+    // ------------------------------------------------------------ Q loaders
+    const int li = threadIdx.x - 256;          // query row of each item this thread gathers
+    // Each loader warp keeps its own copy of the next work items in a ring of
+    // kRing entries, refilled half a ring at a time with warp-level sync only
+    // (so one warp stopping early can never leave the others at a barrier).
+    int4* my_ring = ring + (warp - 8) * C::kRing;
+    auto fill = [&](int base, int count) {   // items base .. base + count - 1
+      for (int q = lane; q < count; q += 32)
+        if (base + q < T) my_ring[(base + q) % C::kRing] = prm.items[t_begin + base + q];
       __syncwarp();
-      // Four query rows per lane; rows past the item's count repeat its first.
-      int32_t ys[4];
-      const int32_t first = prm.lists[start] >> 6;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = lane * 4 + i;
-        const int32_t row = (r < cnt) ? (prm.lists[start + r] >> 6) : first;
-        ys[i] = u * s.N + row;
+    };
+    auto entry = [&](int t) -> int32_t {
+      if (t >= T) return 0;
+      const int4 it = my_ring[t % C::kRing];
+      return prm.lists[it.z + (li < it.w ? li : 0)];
+    };
+    fill(0, C::kRing);
+    int32_t E0 = entry(0), E1 = entry(1);
+    auto step = [&](int t, int32_t& E) -> bool {
+      const int st = t % NS, use = t / NS;
+      const int4 it = my_ring[t % C::kRing];
+      const int32_t e = E;
+      if (use >= 1) {
+        bool ok = mbar_wait(&ld_empty[st], (use - 1) & 1, prm.err, kErrWaitFree);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok || *abort_flag) { *abort_flag = 1; return false; }
       }
+      // Rows past the item's count gather its first query again (never stored).
+      int32_t* m = meta(st);
+      m[li] = e;
+      if (li == 0) reinterpret_cast<int4*>(m + kTileRows)[0] = it;
+      const unsigned char* src =
+          reinterpret_cast<const unsigned char*>(prm.q + ((int64_t)it.x * s.N + (e >> 6)) * HD);
+      unsigned char* dst = q_s(st) + li * 128;
 #pragma unroll
-      for (int p = 0; p < HD / 64; ++p)
-        tma_gather4(q_s(g) + p * (kTileRows * 128) + lane * 4 * 128, &tmap_q, &q_full[g], p * 64,
-                    ys[0], ys[1], ys[2], ys[3]);
-      if (lane == 0) {
-        const int32_t y = u * s.N + j * BS;
+      for (int c = 0; c < HD / 8; ++c) {
+        const int panel = c >> 3, cc = c & 7;
+        cp_async16(dst + panel * (kTileRows * 128) + ((cc ^ (li & 7)) << 4), src + c * 16);
+      }
+      mbar_arrive(&ld_full[st]);            // entries visible
+      cp_async_arrive_noinc(&ld_full[st]);  // row landed
+      // Entering a new half ring: the half before it is done, so refill that
+      // half with the items one ring ahead.  Then load the entry of item t + 2.
+      constexpr int H = C::kRing / 2;
+      if (t % H == H - 1 && t + 1 >= H) fill(t + 1 + H, H);
+      E = entry(t + 2);
+      return true;
+    };
+    for (int t = 0; t < T; t += 2) {
+      if (!step(t, E0)) break;
+      if (t + 1 < T && !step(t + 1, E1)) break;
+    }
+  } else if (warp == 12) {
+    // ------------------------------------------------------------ K/V TMA
+    if (lane == 0) {
+      int4 A = prm.items[t_begin], B = T > 1 ? prm.items[t_begin + 1] : A;
+      auto step = [&](int t, int4& X) -> bool {
+        const int st = t % NS, use = t / NS;
+        const int4 it = X;
+        if (t + 2 < T) X = prm.items[t_begin + t + 2];
+        if (use >= 1 && (!mbar_wait(&ld_empty[st], (use - 1) & 1, prm.err, kErrWaitFree) || *abort_flag)) {
+          *abort_flag = 1;
+          return false;
+        }
+        mbar_arrive_expect_tx(&ld_full[st], C::kKVBytes);
+        const int32_t y = it.x * s.N + it.y * BS;
 #pragma unroll
         for (int p = 0; p < HD / 64; ++p) {
-          tma_load_2d(k_s(g) + p * (BS * 128), &tmap_k, &q_full[g], p * 64, y);
-          tma_load_2d(v_s(g) + p * (BS * 128), &tmap_v, &q_full[g], p * 64, y);
+          tma_load_2d(k_s(st) + p * (BS * 128), &tmap_k, &ld_full[st], p * 64, y);
+          tma_load_2d(v_s(st) + p * (BS * 128), &tmap_v, &ld_full[st], p * 64, y);
         }
+        return true;
+      };
+      for (int t = 0; t < T; t += 2) {
+        if (!step(t, A)) break;
+        if (t + 1 < T && !step(t + 1, B)) break;
       }
-      issued = t + 1;
     }
-    // Drain: wait (bounded) for the loads this warp issued but nobody consumed.
-    if (*abort_flag && lane == 0) {
-      for (int t = (issued >= 2 ? issued - 2 : 0); t < issued; ++t)
-        mbar_wait(&q_full[t & 1], (t >> 1) & 1, nullptr, 0);
-    }
-  } else if (warp == 9) {
+    __syncwarp();
+  } else if (warp == 13) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(kTileRows, BS, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(kTileRows, HD, true);
-      auto issue_s = [&](int t) -> bool {
-        const int g = t & 1;
-        if (!mbar_wait(&q_full[g], (t >> 1) & 1, prm.err, kErrWaitQ)) return false;
-        tc_fence_after();
-        const uint32_t d = tbase + g * (BS + HD);
-        const uint32_t qa = smem_u32(q_s(g)), ka = smem_u32(k_s(g));
+      int ns = 0, no = 0;
+      uint64_t t_idle = globaltimer();
+      uint32_t spins = 0;
+      bool ok = true;
+      while (no < T) {
+        bool prog = false;
+        // S(ns) needs its stage loaded and TMEM S[ns & 1] consumed: the
+        // warpgroup has written P(ns - 2).  (PV(ns - 2) need not be issued.)
+        if (ns < T && (ns < 2 || mbar_test(&p_full[ns & 1], ((ns - 2) >> 1) & 1)) &&
+            mbar_test(&ld_full[ns % NS], (ns / NS) & 1)) {
+          tc_fence_after();
+          const int st = ns % NS;
+          const uint32_t d = tbase + (ns & 1) * (BS + HD);
+          const uint32_t qa = smem_u32(q_s(st)), ka = smem_u32(k_s(st));
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (kTileRows * 128) + (kk & 3) * 32;
-          const uint32_t offk = (kk >> 2) * (BS * 128) + (kk & 3) * 32;
-          mma_bf16(d, smem_desc_sw128(qa + off, 16, 1024), smem_desc_sw128(ka + offk, 16, 1024),
-                   idesc_s, kk > 0);
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (kTileRows * 128) + (kk & 3) * 32;
+            const uint32_t offk = (kk >> 2) * (BS * 128) + (kk & 3) * 32;
+            mma_bf16(d, smem_desc_sw128(qa + off, 16, 1024), smem_desc_sw128(ka + offk, 16, 1024),
+                     idesc_s, kk > 0);
+          }
+          mma_commit(&s_full[ns & 1]);
+          ++ns;
+          prog = true;
         }
-        mma_commit(&s_full[g]);
-        return true;
-      };
-      auto issue_o = [&](int t) -> bool {
-        const int g = t & 1;
-        if (!mbar_wait(&p_full[g], (t >> 1) & 1, prm.err, kErrWaitP)) return false;
-        tc_fence_after();
-        const uint32_t d = tbase + g * (BS + HD) + BS;
-        const uint32_t pa = smem_u32(p_s(g)), va = smem_u32(v_s(g));
+        // PV(no) needs P(no) written and O[no & 1] read out (item no - 2).
+        if (no < ns) {
+          const int g = no & 1;
+          if (mbar_test(&p_full[g], (no >> 1) & 1) &&
+              (no < 2 || mbar_test(&o_free[g], ((no - 2) >> 1) & 1))) {
+            tc_fence_after();
+            const int st = no % NS;
+            const uint32_t d = tbase + g * (BS + HD) + BS;
+            const uint32_t pa = smem_u32(p_s(g)), va = smem_u32(v_s(st));
 #pragma unroll
-        for (int kk = 0; kk < BS / 16; ++kk) {
-          const uint32_t offp = (kk >> 2) * (kTileRows * 128) + (kk & 3) * 32;
-          const uint32_t offv = kk * 16 * 128;
-          mma_bf16(d, smem_desc_sw128(pa + offp, 16, 1024),
-                   smem_desc_sw128(va + offv, BS * 128, 1024), idesc_o, kk > 0);
+            for (int kk = 0; kk < BS / 16; ++kk) {
+              const uint32_t offp = (kk >> 2) * (kTileRows * 128) + (kk & 3) * 32;
+              const uint32_t offv = kk * 16 * 128;
+              mma_bf16(d, smem_desc_sw128(pa + offp, 16, 1024),
+                       smem_desc_sw128(va + offv, BS * 128, 1024), idesc_o, kk > 0);
+            }
+            mma_commit(&o_full[g]);
+            mma_commit(&ld_empty[st]);
+            ++no;
+            prog = true;
+          }
         }
-        mma_commit(&o_full[g]);
-        return true;
-      };
-      bool ok = issue_s(0);
-      for (int t = 0; ok && t < T; ++t) {
-        if (t + 1 < T) ok = issue_s(t + 1);
-        if (ok) ok = issue_o(t);
-        if (*abort_flag) ok = false;
+        if (prog) {
+          spins = 0;
+        } else if (++spins % 256 == 0) {
+          const uint64_t now = globaltimer();
+          if (spins == 256) t_idle = now;
+          if (*abort_flag || now - t_idle > kWaitLimitNs) {
+            if (!*abort_flag) atomicOr(prm.err, kErrWaitP);
+            ok = false;
+            break;
+          }
+        }
       }
       if (!ok) *abort_flag = 1;
       // Make sure no MMA is in flight when TMEM is released.
@@ -389,58 +478,72 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
       mbar_wait(drain, 0, prm.err, kErrWaitDrain);
     }
     __syncwarp();
-  } else {
+  } else if (warp < 8) {
     // ------------------------------------------------------------ softmax / epilogue
     const int wg = warp >> 2;              // 0 or 1: takes items t with t & 1 == wg
     const int quad = warp & 3;             // TMEM lane quadrant
     const int r = quad * 32 + lane;        // row of the tile this thread owns
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     for (int t = wg; t < T; t += 2) {
-      const int g = wg;
-      const int n = t >> 1;
-      const int4 it = prm.items[t_begin + t];
-      const int u = it.x, j = it.y, start = it.z, cnt = it.w;
+      const int g = wg, n = t >> 1, st = t % NS;
+      bool ok = mbar_wait(&ld_full[st], (t / NS) & 1, prm.err, kErrWaitQ);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || *abort_flag) { *abort_flag = 1; break; }
+      const int32_t* m = meta(st);
+      const int4 it = reinterpret_cast<const int4*>(m + kTileRows)[0];
+      const int u = it.x, j = it.y, cnt = it.w;
       const bool valid = r < cnt;
-      const int32_t e = valid ? prm.lists[start + r] : 0;
+      const int32_t e = m[r];
       const int qrow = e >> 6, slot = e & 63;
 
-      bool ok = mbar_wait(&s_full[g], n & 1, prm.err, kErrWaitS);
+      ok = mbar_wait(&s_full[g], n & 1, prm.err, kErrWaitS);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok || *abort_flag) { *abort_flag = 1; break; }
       tc_fence_after();
-      float sv[BS];
       const uint32_t s_addr = tbase + lane_off + g * (BS + HD);
-#pragma unroll
-      for (int c = 0; c < BS; c += 64) tmem_ld64(s_addr + c, sv + c);
-      // Token-level causal mask (block_indexer.py:73-81): key > query -> -inf.
       const int key0 = j * BS;
-      if (s.causal && key0 + BS - 1 > qrow) {
+      const bool diag = s.causal && key0 + BS - 1 > qrow;
+      float sv[64];
+      auto load_s = [&](int c0) {
+        tmem_ld64(s_addr + c0, sv);
+        // Token-level causal mask (block_indexer.py:73-81): key > query -> -inf.
+        if (diag) {
 #pragma unroll
-        for (int c = 0; c < BS; ++c)
-          if (key0 + c > qrow) sv[c] = -INFINITY;
-      }
-      float m0 = sv[0], m1 = sv[1], m2 = sv[2], m3 = sv[3];
+          for (int c = 0; c < 64; ++c)
+            if (key0 + c0 + c > qrow) sv[c] = -INFINITY;
+        }
+      };
+      float mx = -INFINITY;
 #pragma unroll
-      for (int c = 4; c < BS; c += 4) {
-        m0 = fmaxf(m0, sv[c]); m1 = fmaxf(m1, sv[c + 1]);
-        m2 = fmaxf(m2, sv[c + 2]); m3 = fmaxf(m3, sv[c + 3]);
+      for (int c0 = 0; c0 < BS; c0 += 64) {
+        load_s(c0);
+        float m0 = sv[0], m1 = sv[1], m2 = sv[2], m3 = sv[3];
+#pragma unroll
+        for (int c = 4; c < 64; c += 4) {
+          m0 = fmaxf(m0, sv[c]); m1 = fmaxf(m1, sv[c + 1]);
+          m2 = fmaxf(m2, sv[c + 2]); m3 = fmaxf(m3, sv[c + 3]);
+        }
+        mx = fmaxf(mx, fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)));
       }
-      const float m = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
       // Padding rows of a short item can be fully masked; keep them finite.
-      const float msc = (m == -INFINITY) ? 0.f : m * sc;
+      const float msc = (mx == -INFINITY) ? 0.f : mx * sc;
       float l0 = 0.f, l1 = 0.f;
       unsigned char* prow = p_s(g) + r * 128;
 #pragma unroll
-      for (int c = 0; c < BS; c += 8) {
-        float p[8];
+      for (int c0 = 0; c0 < BS; c0 += 64) {
+        if (BS > 64) load_s(c0);   // with one chunk the values are still in sv
 #pragma unroll
-        for (int i = 0; i < 8; ++i) p[i] = fast_exp2(fmaf(sv[c + i], sc, -msc));
-        l0 += (p[0] + p[1]) + (p[2] + p[3]);
-        l1 += (p[4] + p[5]) + (p[6] + p[7]);
-        uint4 w = make_uint4(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]),
-                             pack_bf16x2(p[4], p[5]), pack_bf16x2(p[6], p[7]));
-        const int panel = c >> 6, chunk = (c & 63) >> 3;
-        *reinterpret_cast<uint4*>(prow + panel * (kTileRows * 128) + ((chunk ^ (r & 7)) << 4)) = w;
+        for (int c = 0; c < 64; c += 8) {
+          float p[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) p[i] = fast_exp2(fmaf(sv[c + i], sc, -msc));
+          l0 += (p[0] + p[1]) + (p[2] + p[3]);
+          l1 += (p[4] + p[5]) + (p[6] + p[7]);
+          uint4 w = make_uint4(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]),
+                               pack_bf16x2(p[4], p[5]), pack_bf16x2(p[6], p[7]));
+          const int chunk = c >> 3;
+          *reinterpret_cast<uint4*>(prow + (c0 >> 6) * (kTileRows * 128) + ((chunk ^ (r & 7)) << 4)) = w;
+        }
       }
       const float l = l0 + l1;
       fence_proxy_async_smem();
@@ -451,25 +554,29 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
       ok = __all_sync(0xffffffffu, ok);
       if (!ok || *abort_flag) { *abort_flag = 1; break; }
       tc_fence_after();
-      float ov[HD];
       const uint32_t o_addr = tbase + lane_off + g * (BS + HD) + BS;
+      const float inv = 1.f / l;
+      const int64_t pe = ((int64_t)u * s.N + qrow) * s.k + slot;
+      uint4* dst = reinterpret_cast<uint4*>(prm.part_o + pe * HD);
 #pragma unroll
-      for (int c = 0; c < HD; c += 64) tmem_ld64(o_addr + c, ov + c);
-      tc_fence_before();
-      mbar_arrive(&o_free[g]);
-      if (valid) {
-        const float inv = 1.f / l;
-        const int64_t pe = ((int64_t)u * s.N + qrow) * s.k + slot;
-        uint4* dst = reinterpret_cast<uint4*>(prm.part_o + pe * HD);
-#pragma unroll
-        for (int c = 0; c < HD; c += 8) {
-          dst[c >> 3] = make_uint4(pack_bf16x2(ov[c] * inv, ov[c + 1] * inv),
-                                   pack_bf16x2(ov[c + 2] * inv, ov[c + 3] * inv),
-                                   pack_bf16x2(ov[c + 4] * inv, ov[c + 5] * inv),
-                                   pack_bf16x2(ov[c + 6] * inv, ov[c + 7] * inv));
+      for (int c0 = 0; c0 < HD; c0 += 64) {
+        float ov[64];
+        tmem_ld64(o_addr + c0, ov);
+        if (c0 + 64 >= HD) {
+          tc_fence_before();
+          mbar_arrive(&o_free[g]);
         }
-        prm.part_ml[pe] = make_float2(msc, l);
+        if (valid) {
+#pragma unroll
+          for (int c = 0; c < 64; c += 8) {
+            dst[(c0 + c) >> 3] = make_uint4(pack_bf16x2(ov[c] * inv, ov[c + 1] * inv),
+                                            pack_bf16x2(ov[c + 2] * inv, ov[c + 3] * inv),
+                                            pack_bf16x2(ov[c + 4] * inv, ov[c + 5] * inv),
+                                            pack_bf16x2(ov[c + 6] * inv, ov[c + 7] * inv));
+          }
+        }
       }
+      if (valid) prm.part_ml[pe] = make_float2(msc, l);
     }
   }
   tc_fence_before();
@@ -558,15 +665,15 @@ static cudaError_t launch_kv_kernel(const __nv_bfloat16* Q, const __nv_bfloat16*
                                     const __nv_bfloat16* V, const FineWs& w, const Shape& s,
                                     cudaStream_t st) {
   using C = KvCfg<BS, HD>;
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mk, mv;
   const uint64_t rows = (uint64_t)s.units * s.N;
-  if (!make_map(&mq, Q, rows, HD, 1) || !make_map(&mk, K, rows, HD, BS) ||
-      !make_map(&mv, V, rows, HD, BS))
+  if (!make_map(&mk, K, rows, HD, BS) || !make_map(&mv, V, rows, HD, BS))
     return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(fine_kv_kernel<BS, HD>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   if (e != cudaSuccess) return e;
   FineKvParams prm;
+  prm.q = Q;
   prm.items = w.items;
   prm.lists = w.lists;
   prm.total_items = w.err + 1;
@@ -574,7 +681,7 @@ static cudaError_t launch_kv_kernel(const __nv_bfloat16* Q, const __nv_bfloat16*
   prm.part_ml = w.part_ml;
   prm.err = w.err;
   prm.s = s;
-  fine_kv_kernel<BS, HD><<<num_sms(), C::kThreads, C::kSmem, st>>>(mq, mk, mv, prm);
+  fine_kv_kernel<BS, HD><<<num_sms(), C::kThreads, C::kSmem, st>>>(mk, mv, prm);
   return cudaGetLastError();
 }
 

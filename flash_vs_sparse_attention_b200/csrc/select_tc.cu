@@ -38,17 +38,25 @@ constexpr int kSelRows = 128;
 
 template <int KCAP, int HD>
 struct SelCfg {
-  // Window width (blocks per MMA N tile): as wide as shared memory allows.
-  static constexpr int W = (HD == 64) ? (KCAP <= 32 ? 128 : 64) : (KCAP <= 16 ? 64 : 32);
-  static constexpr int kCap = topk_buffer_slots(KCAP);
+  // The head_dim-64 shapes run two CTAs per SM (two selection warps per
+  // scheduler hide each other's latency), which caps shared memory near
+  // 100 KB: 64-block windows, one Q buffer and a candidate buffer of k + 32
+  // slots (the row floor leaves ~20 candidates per row; the buffer compacts
+  // itself if a row sends more).  Wider problems use one CTA per SM.
+  static constexpr int kCtasPerSm = (HD == 64 && KCAP <= 32) ? 2 : 1;
+  static constexpr int W = (HD == 64) ? (KCAP <= 16 ? 64 : (KCAP <= 32 ? 32 : 64))
+                                      : (KCAP <= 16 ? 64 : 32);
+  static constexpr int kQBufs = kCtasPerSm == 2 ? 1 : 2;
+  static constexpr int kCap = kCtasPerSm == 2 ? KCAP + 32 : topk_buffer_slots(KCAP);
   static constexpr int kQBytes = kSelRows * HD * 2;
   static constexpr int kTermBytes = W * HD * 2;          // one bf16 term of a window
   static constexpr int kWinBytes = 2 * kTermBytes;       // hi + lo
-  static constexpr int kBufOff = 2 * kQBytes + 2 * kWinBytes;
+  static constexpr int kBufOff = kQBufs * kQBytes + 2 * kWinBytes;
   static constexpr int kBufBytes = kCap * kSelRows * 8;
   static constexpr int kSmem = kBufOff + kBufBytes + 256 + 1024;
   static constexpr int kTmemCols = (2 * W <= 32) ? 32 : (2 * W <= 64 ? 64 : (2 * W <= 128 ? 128 : 256));
   static constexpr int kThreads = 192;
+  static_assert(kCap >= KCAP + 32, "the buffer must hold the top-k plus one 32-candidate chunk");
 };
 
 struct SelectTcParams {
@@ -59,7 +67,7 @@ struct SelectTcParams {
 };
 
 template <int KCAP, int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, SelCfg<KCAP, HD>::kCtasPerSm)
 select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                  const __grid_constant__ CUtensorMap tmap_hi,
                  const __grid_constant__ CUtensorMap tmap_lo, SelectTcParams prm) {
@@ -67,9 +75,9 @@ select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
   constexpr int W = C::W;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  auto q_s = [&](int b) { return smem + b * C::kQBytes; };
+  auto q_s = [&](int b) { return smem + (b % C::kQBufs) * C::kQBytes; };
   auto win = [&](int b, int term) {
-    return smem + 2 * C::kQBytes + b * C::kWinBytes + term * C::kTermBytes;
+    return smem + C::kQBufs * C::kQBytes + b * C::kWinBytes + term * C::kTermBytes;
   };
   uint2* cbuf = reinterpret_cast<uint2*>(smem + C::kBufOff);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBufOff + C::kBufBytes);
@@ -129,8 +137,9 @@ select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
       int kw = 0;  // windows loaded so far
       for (int n = 0; n < n_items; ++n) {
         const int unit = item_unit(n), tile = item_tile(n);
-        const int qb = n & 1;
-        if (n >= 2 && (!mbar_wait(&q_empty[qb], ((n - 2) >> 1) & 1, prm.err, 1u) || *abort_flag)) {
+        const int qb = n % C::kQBufs;
+        const int qn = n / C::kQBufs;   // use count of this Q buffer
+        if (qn >= 1 && (!mbar_wait(&q_empty[qb], (qn - 1) & 1, prm.err, 1u) || *abort_flag)) {
           *abort_flag = 1;
           break;
         }
@@ -167,8 +176,8 @@ select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
       bool ok = true;
       int kw = 0;
       for (int n = 0; ok && n < n_items; ++n) {
-        const int qb = n & 1;
-        ok = mbar_wait(&q_full[qb], (n >> 1) & 1, prm.err, 2u);
+        const int qb = n % C::kQBufs;
+        ok = mbar_wait(&q_full[qb], (n / C::kQBufs) & 1, prm.err, 2u);
         const uint32_t qa = smem_u32(q_s(qb));
         const int nw = (visible_blocks(item_tile(n)) + W - 1) / W;
         for (int ww = 0; ok && ww < 2 * nw; ++ww, ++kw) {
@@ -327,7 +336,7 @@ static cudaError_t launch_tc(const __nv_bfloat16* Q, const __nv_bfloat16* K_hi,
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int items = s.units * prm.tiles;
-  const int grid = items < sms ? items : sms;
+  const int grid = items < sms * C::kCtasPerSm ? items : sms * C::kCtasPerSm;
   select_tc_kernel<KCAP, HD><<<grid, C::kThreads, C::kSmem, st>>>(mq, mh, ml, prm);
   return cudaGetLastError();
 }

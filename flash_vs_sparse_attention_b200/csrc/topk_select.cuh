@@ -12,12 +12,10 @@
 // When the buffer is about to overflow it is compacted to its exact top-k
 // (values only, a 2*KCAP-op min/max insertion network per entry), which also
 // raises theta_excl.  Compaction keeps buffer order, so ties keep resolving
-// to the lowest index.  The final emission sorts the surviving (score,
-// index) pairs as 64-bit keys with a bitonic network in registers and writes
-// the indices by descending score, ties by ascending index -- the order of
-// torch.topk(sorted=True) with its ties made deterministic.  -inf candidates
-// (causally masked blocks) never enter the buffer, so rows with fewer than k
-// eligible blocks emit -1 in the remaining slots.
+// to the lowest index, and the final emission lists the selected blocks in
+// ascending block order (the fine stage needs no particular order).  -inf
+// candidates (causally masked blocks) never enter the buffer, so rows with
+// fewer than k eligible blocks emit -1 in the remaining slots.
 #pragma once
 
 #include "common.cuh"
@@ -116,48 +114,10 @@ struct RowTopK {
     theta_excl = fmaxf(theta_excl, T);
   }
 
-  // Final top-k, written as k int32 by descending score (ties: ascending
-  // index), -1 padded.
+  // Final top-k, written as k int32 in ascending block order, -1 padded.
   __device__ __forceinline__ void emit(int32_t* out) {
-    constexpr int SORTN = KCAP > 32 ? 64 : 32;
-    if (cnt > SORTN) compact();   // exact top-k, at most KCAP <= SORTN entries
-    uint64_t key[SORTN];
-#pragma unroll
-    for (int e = 0; e < SORTN; ++e) {
-      uint64_t kk = 0;
-      if (e < cnt) {
-        const uint2 en = buf[e * stride];
-        const uint32_t b = en.x;
-        const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-        kk = ((uint64_t)ord << 32) | (uint64_t)(0xFFFFFFFFu - en.y);
-      }
-      key[e] = kk;
-    }
-    bitonic_sort_desc<SORTN>(key);
-#pragma unroll
-    for (int e = 0; e < SORTN; ++e)
-      if (e < k) out[e] = e < cnt ? (int32_t)(0xFFFFFFFFu - (uint32_t)key[e]) : -1;
-    for (int e = SORTN; e < k; ++e) out[e] = -1;
-  }
-
-  template <int N>
-  __device__ __forceinline__ static void bitonic_sort_desc(uint64_t (&v)[N]) {
-#pragma unroll
-    for (int k2 = 2; k2 <= N; k2 <<= 1) {
-#pragma unroll
-      for (int j = k2 >> 1; j > 0; j >>= 1) {
-#pragma unroll
-        for (int i = 0; i < N; ++i) {
-          const int l = i ^ j;
-          if (l > i) {
-            const uint64_t a = v[i], b = v[l];
-            const bool gt = a > b;
-            const uint64_t hi = gt ? a : b, lo = gt ? b : a;
-            if ((i & k2) == 0) { v[i] = hi; v[l] = lo; } else { v[i] = lo; v[l] = hi; }
-          }
-        }
-      }
-    }
+    compact();
+    for (int e = 0; e < k; ++e) out[e] = e < cnt ? (int32_t)buf[e * stride].y : -1;
   }
 };
 

@@ -97,10 +97,9 @@ int bsa_forward_ex(const bsa_problem* p, const void* Q, const void* K, const voi
 int bsa_pool_k(const bsa_problem* p, const void* K, float* K_repr, void* K_split, void* stream);
 
 /* Stages 2-3 alone (block_indexer_triton.py:121-129, block_indexer.py:44-53):
- * writes idx (B*H, N, top_k) int32, each row's selected blocks by descending
- * coarse score (the order of torch.topk(sorted=True)), ties to the lower
- * block index, then -1 in slots left empty because fewer than top_k blocks
- * are eligible.  Needs the outputs of bsa_pool_k (K_split may be NULL only
+ * writes idx (B*H, N, top_k) int32, each row's selected blocks in ascending
+ * block order, then -1 in slots left empty because fewer than top_k blocks
+ * are eligible.  Ties in the coarse score go to the lower block index.  Needs the outputs of bsa_pool_k (K_split may be NULL only
  * with BSA_FLAG_SIMT_SELECT). */
 int bsa_select_blocks(const bsa_problem* p, const void* Q, const float* K_repr,
                       const void* K_split, int32_t* idx, void* stream);

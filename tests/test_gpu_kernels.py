@@ -63,13 +63,10 @@ def test_select_blocks_index_parity(cuda, shape, flags):
         for h in range(H):
             n_bad, n_tie, bad = check_indices(Q[b, h], K[b, h], idx[b, h], rows, bs, k, causal)
             assert n_bad == 0, f"unit ({b},{h}): {n_bad} rows differ, e.g. {bad[:5]}"
-            # emitted by descending coarse score, -1 only at the end
-            sc = oracle_scores(Q[b, h], K[b, h], rows, bs, causal)
-            for r, row in enumerate(idx[b, h]):
+            # emitted in ascending block order, -1 only at the end
+            for row in idx[b, h]:
                 v = row[row >= 0]
-                assert np.all(row[len(v):] == -1), row
-                s_row = sc[r, v]
-                assert np.all(np.diff(s_row) <= 1e-6), (r, row, s_row)
+                assert np.all(np.diff(v) > 0) and np.all(row[len(v):] == -1), row
 
 
 @pytest.mark.parametrize("flags", [0, SIMT])
