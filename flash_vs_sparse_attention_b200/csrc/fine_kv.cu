@@ -222,13 +222,13 @@ bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict
 // 16 warps:
 //   0-3, 4-7  softmax/epilogue warpgroups; warpgroup g takes the items t with
 //             t % 2 == g and owns TMEM buffers S[g], O[g] and shared P[g]
-//   8-11      loader warpgroup: thread i gathers query row i of each item
-//             with 16-byte cp.async (the LSU path streams random 128-byte rows
+//   8         loader: each lane gathers four query rows of each item with
+//             16-byte cp.async (the LSU path streams random 128-byte rows
 //             faster than TMA gather4 issues them) and stages the item's list
 //             entries for the softmax warpgroups
 //   12        TMA: the item's K and V tiles
-//   13        one thread issues the MMAs, S(t) and PV(t) each as soon as its
-//             inputs are ready
+//   13        one thread issues the MMAs in the order S0 S1 PV0 S2 PV1 S3 ...
+//             (S(t + 2) reuses the TMEM buffer PV(t)'s softmax just freed)
 // Shared memory holds a ring of NS load stages (Q rows, K, V, entries).  S
 // and O are read from TMEM 64 columns at a time, so every (block_size,
 // head_dim) pair fits in 128 registers per thread.
@@ -245,14 +245,15 @@ struct KvCfg {
   static constexpr int kPOff = NS * kStageBytes;
   static constexpr int kMetaOff = kPOff + 2 * kPBytes;
   static constexpr int kRingOff = kMetaOff + NS * kMetaBytes;
-  static constexpr int kBarOff = kRingOff + 4 * kRing * 16;
+  static constexpr int kBarOff = kRingOff + kRing * 16;
   static constexpr int kSmem = kBarOff + 256 + 1024 /*align*/;
   static constexpr int kTmemCols = (2 * (BS + HD) <= 256) ? 256 : 512;
   static constexpr uint32_t kKVBytes = kKBytes + kVBytes;
-  static constexpr int kLoaders = 128;
-  // ld_full completes on: each loader's entries-written arrive, each
-  // loader's cp.async-landed arrive, and the TMA warp's expect_tx arrive.
-  static constexpr int kLdFullCount = 2 * kLoaders + 1;
+  static constexpr int kLoaders = 32;
+  // ld_full completes on: the loader warp's entries-written arrive (lane 0),
+  // each loader lane's cp.async-landed arrive, and the TMA warp's expect_tx
+  // arrive.  Few arrivals keep the barrier's atomics off the critical path.
+  static constexpr int kLdFullCount = kLoaders + 2;
   static constexpr int kThreads = 512;
 };
 
@@ -328,29 +329,35 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant
   auto meta = [&](int st) { return (int32_t*)(smem + C::kMetaOff + st * C::kMetaBytes); };
   const float sc = s.scale * kLog2e;
 
-  if (warp >= 8 && warp < 12) {
-    // ------------------------------------------------------------ Q loaders
-    const int li = threadIdx.x - 256;          // query row of each item this thread gathers
-    // Each loader warp keeps its own copy of the next work items in a ring of
-    // kRing entries, refilled half a ring at a time with warp-level sync only
-    // (so one warp stopping early can never leave the others at a barrier).
-    int4* my_ring = ring + (warp - 8) * C::kRing;
+  if (warp == 8) {
+    // ------------------------------------------------------------ Q loader
+    // Lane l gathers rows 4l .. 4l+3 of each item.  The warp keeps the next
+    // work items in a ring of kRing entries, refilled half a ring at a time.
     auto fill = [&](int base, int count) {   // items base .. base + count - 1
       for (int q = lane; q < count; q += 32)
-        if (base + q < T) my_ring[(base + q) % C::kRing] = prm.items[t_begin + base + q];
+        if (base + q < T) ring[(base + q) % C::kRing] = prm.items[t_begin + base + q];
       __syncwarp();
     };
-    auto entry = [&](int t) -> int32_t {
-      if (t >= T) return 0;
-      const int4 it = my_ring[t % C::kRing];
-      return prm.lists[it.z + (li < it.w ? li : 0)];
+    struct Ent { int32_t e[4]; };
+    auto entries = [&](int t, Ent& E) {
+      if (t >= T) return;
+      const int4 it = ring[t % C::kRing];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = lane * 4 + i;
+        E.e[i] = prm.lists[it.z + (r < it.w ? r : 0)];
+      }
     };
     fill(0, C::kRing);
-    int32_t E0 = entry(0), E1 = entry(1);
-    auto step = [&](int t, int32_t& E) -> bool {
+    Ent E0, E1;
+    entries(0, E0);
+    entries(1, E1);
+    auto step = [&](int t, Ent& E) -> bool {
       const int st = t % NS, use = t / NS;
-      const int4 it = my_ring[t % C::kRing];
-      const int32_t e = E;
+      const int4 it = ring[t % C::kRing];
+      int32_t e[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) e[i] = E.e[i];
       if (use >= 1) {
         bool ok = mbar_wait(&ld_empty[st], (use - 1) & 1, prm.err, kErrWaitFree);
         ok = __all_sync(0xffffffffu, ok);
@@ -358,23 +365,28 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant
       }
       // Rows past the item's count gather its first query again (never stored).
       int32_t* m = meta(st);
-      m[li] = e;
-      if (li == 0) reinterpret_cast<int4*>(m + kTileRows)[0] = it;
-      const unsigned char* src =
-          reinterpret_cast<const unsigned char*>(prm.q + ((int64_t)it.x * s.N + (e >> 6)) * HD);
-      unsigned char* dst = q_s(st) + li * 128;
 #pragma unroll
-      for (int c = 0; c < HD / 8; ++c) {
-        const int panel = c >> 3, cc = c & 7;
-        cp_async16(dst + panel * (kTileRows * 128) + ((cc ^ (li & 7)) << 4), src + c * 16);
+      for (int i = 0; i < 4; ++i) {
+        const int r = lane * 4 + i;
+        m[r] = e[i];
+        const unsigned char* src =
+            reinterpret_cast<const unsigned char*>(prm.q + ((int64_t)it.x * s.N + (e[i] >> 6)) * HD);
+        unsigned char* dst = q_s(st) + r * 128;
+#pragma unroll
+        for (int c = 0; c < HD / 8; ++c) {
+          const int panel = c >> 3, cc = c & 7;
+          cp_async16(dst + panel * (kTileRows * 128) + ((cc ^ (r & 7)) << 4), src + c * 16);
+        }
       }
-      mbar_arrive(&ld_full[st]);            // entries visible
-      cp_async_arrive_noinc(&ld_full[st]);  // row landed
+      if (lane == 0) reinterpret_cast<int4*>(m + kTileRows)[0] = it;
+      cp_async_arrive_noinc(&ld_full[st]);   // this lane's rows landed
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ld_full[st]);  // entries visible
       // Entering a new half ring: the half before it is done, so refill that
-      // half with the items one ring ahead.  Then load the entry of item t + 2.
+      // half with the items one ring ahead.  Then load item t + 2's entries.
       constexpr int H = C::kRing / 2;
-      if (t % H == H - 1 && t + 1 >= H) fill(t + 1 + H, H);
-      E = entry(t + 2);
+      if (t % H == H - 1) fill(t + 1 + H, H);
+      entries(t + 2, E);
       return true;
     };
     for (int t = 0; t < T; t += 2) {
@@ -413,64 +425,49 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(kTileRows, BS, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(kTileRows, HD, true);
-      int ns = 0, no = 0;
-      uint64_t t_idle = globaltimer();
-      uint32_t spins = 0;
-      bool ok = true;
-      while (no < T) {
-        bool prog = false;
-        // S(ns) needs its stage loaded and TMEM S[ns & 1] consumed: the
-        // warpgroup has written P(ns - 2).  (PV(ns - 2) need not be issued.)
-        if (ns < T && (ns < 2 || mbar_test(&p_full[ns & 1], ((ns - 2) >> 1) & 1)) &&
-            mbar_test(&ld_full[ns % NS], (ns / NS) & 1)) {
-          tc_fence_after();
-          const int st = ns % NS;
-          const uint32_t d = tbase + (ns & 1) * (BS + HD);
-          const uint32_t qa = smem_u32(q_s(st)), ka = smem_u32(k_s(st));
+      // Descriptors at stage / buffer 0; the start-address field (bits 0-13,
+      // address >> 4) is advanced by adding byte offsets >> 4.
+      const uint64_t dq0 = smem_desc_sw128(smem_u32(q_s(0)), 16, 1024);
+      const uint64_t dk0 = smem_desc_sw128(smem_u32(k_s(0)), 16, 1024);
+      const uint64_t dp0 = smem_desc_sw128(smem_u32(p_s(0)), 16, 1024);
+      const uint64_t dv0 = smem_desc_sw128(smem_u32(v_s(0)), BS * 128, 1024);
+      auto issue_s = [&](int t) -> bool {
+        const int st = t % NS;
+        if (!mbar_wait(&ld_full[st], (t / NS) & 1, prm.err, kErrWaitQ)) return false;
+        tc_fence_after();
+        const uint32_t d = tbase + (t & 1) * (BS + HD);
+        const uint64_t dq = dq0 + ((st * C::kStageBytes) >> 4), dk = dk0 + ((st * C::kStageBytes) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * (kTileRows * 128) + (kk & 3) * 32;
-            const uint32_t offk = (kk >> 2) * (BS * 128) + (kk & 3) * 32;
-            mma_bf16(d, smem_desc_sw128(qa + off, 16, 1024), smem_desc_sw128(ka + offk, 16, 1024),
-                     idesc_s, kk > 0);
-          }
-          mma_commit(&s_full[ns & 1]);
-          ++ns;
-          prog = true;
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (kTileRows * 128) + (kk & 3) * 32;
+          const uint32_t offk = (kk >> 2) * (BS * 128) + (kk & 3) * 32;
+          mma_bf16(d, dq + (off >> 4), dk + (offk >> 4), idesc_s, kk > 0);
         }
-        // PV(no) needs P(no) written and O[no & 1] read out (item no - 2).
-        if (no < ns) {
-          const int g = no & 1;
-          if (mbar_test(&p_full[g], (no >> 1) & 1) &&
-              (no < 2 || mbar_test(&o_free[g], ((no - 2) >> 1) & 1))) {
-            tc_fence_after();
-            const int st = no % NS;
-            const uint32_t d = tbase + g * (BS + HD) + BS;
-            const uint32_t pa = smem_u32(p_s(g)), va = smem_u32(v_s(st));
+        mma_commit(&s_full[t & 1]);
+        return true;
+      };
+      auto issue_o = [&](int t) -> bool {
+        const int g = t & 1, st = t % NS;
+        if (!mbar_wait(&p_full[g], (t >> 1) & 1, prm.err, kErrWaitP)) return false;
+        if (t >= 2 && !mbar_wait(&o_free[g], ((t - 2) >> 1) & 1, prm.err, kErrWaitFree)) return false;
+        tc_fence_after();
+        const uint32_t d = tbase + g * (BS + HD) + BS;
+        const uint64_t dp = dp0 + ((g * C::kPBytes) >> 4), dv = dv0 + ((st * C::kStageBytes) >> 4);
 #pragma unroll
-            for (int kk = 0; kk < BS / 16; ++kk) {
-              const uint32_t offp = (kk >> 2) * (kTileRows * 128) + (kk & 3) * 32;
-              const uint32_t offv = kk * 16 * 128;
-              mma_bf16(d, smem_desc_sw128(pa + offp, 16, 1024),
-                       smem_desc_sw128(va + offv, BS * 128, 1024), idesc_o, kk > 0);
-            }
-            mma_commit(&o_full[g]);
-            mma_commit(&ld_empty[st]);
-            ++no;
-            prog = true;
-          }
+        for (int kk = 0; kk < BS / 16; ++kk) {
+          const uint32_t offp = (kk >> 2) * (kTileRows * 128) + (kk & 3) * 32;
+          mma_bf16(d, dp + (offp >> 4), dv + ((kk * 16 * 128) >> 4), idesc_o, kk > 0);
         }
-        if (prog) {
-          spins = 0;
-        } else if (++spins % 256 == 0) {
-          const uint64_t now = globaltimer();
-          if (spins == 256) t_idle = now;
-          if (*abort_flag || now - t_idle > kWaitLimitNs) {
-            if (!*abort_flag) atomicOr(prm.err, kErrWaitP);
-            ok = false;
-            break;
-          }
-        }
+        mma_commit(&o_full[g]);
+        mma_commit(&ld_empty[st]);
+        return true;
+      };
+      bool ok = issue_s(0);
+      if (ok && T > 1) ok = issue_s(1);
+      for (int t = 0; ok && t < T; ++t) {
+        ok = issue_o(t);
+        if (ok && t + 2 < T) ok = issue_s(t + 2);
+        if (*abort_flag) ok = false;
       }
       if (!ok) *abort_flag = 1;
       // Make sure no MMA is in flight when TMEM is released.
