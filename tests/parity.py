@@ -6,8 +6,14 @@ import torch
 from oracle import CONFIGS, index_parity, make_inputs
 from oracle.block_indexer_np import _fine_rows, pool_k
 
-# Output tolerance of the bf16 path against the fp32 oracle.
+# Output tolerance of the bf16 path against the fp32 oracle: max-abs 2e-2 and
+# mean-abs 2e-3, where the max-abs bound widens to two bf16 units in the last
+# place (2**-7 * |O|) for |O| above ~2.6.  A bf16 output alone is off by up to
+# half an ulp (2**-9 * |O|), so at |O| in [8, 16) -- early causal rows of the
+# block-scaled workload -- no bf16 result, the reference's Triton variant's
+# included (block_indexer_triton.py:167), can meet a fixed 2e-2.
 MAX_ABS = 2e-2
+MAX_REL = 2.0 ** -7
 MEAN_ABS = 2e-3
 TAU = 1e-5
 
@@ -49,8 +55,13 @@ def oracle_fine(q, k, v, idx_rows, rows, block_size, causal):
 
 
 def assert_close_out(got, want, what=""):
-    err = np.abs(np.asarray(got, np.float32) - np.asarray(want, np.float32))
+    got = np.asarray(got, np.float32)
+    want = np.asarray(want, np.float32)
+    err = np.abs(got - want)
     assert np.isfinite(got).all(), f"{what}: non-finite output"
-    assert err.max() <= MAX_ABS, f"{what}: max-abs {err.max():.3e} > {MAX_ABS}"
+    bound = np.maximum(MAX_ABS, MAX_REL * np.abs(want))
+    worst = np.unravel_index(np.argmax(err - bound), err.shape) if err.size else ()
+    assert np.all(err <= bound), (f"{what}: error {err[worst]:.3e} at |O| = {abs(want[worst]):.3f} "
+                                  f"exceeds max(2e-2, 2^-7 |O|)")
     assert err.mean() <= MEAN_ABS, f"{what}: mean-abs {err.mean():.3e} > {MEAN_ABS}"
     return float(err.max()), float(err.mean())
