@@ -23,6 +23,8 @@ static int fail(int status, const char* fmt, ...) {
   return status;
 }
 
+void set_last_error_message(const char* msg) { g_last_error = msg; }
+
 static int cuda_fail(cudaError_t e, const char* what) {
   return fail(BSA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }

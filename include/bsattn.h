@@ -121,6 +121,25 @@ size_t bsa_fine_workspace_bytes(const bsa_problem* p);
 int bsa_workspace_error(const bsa_problem* p, const void* workspace, size_t workspace_bytes,
                         int from_forward, uint32_t* error_bits);
 
+/* bsa_forward without a workspace argument, for callers that cannot allocate
+ * device memory where they run the attention (a memory pool they do not
+ * own, an allocator locked while they dispatch, fixed buffers handed to an
+ * embedded integration).  No counterpart in the reference: its variants
+ * allocate through torch.
+ * Scratch comes from a 64 MiB device array built into the library; a
+ * problem whose single (batch, head) unit needs more is rejected with
+ * BSA_ERR_WORKSPACE (one unit needs about N*top_k*(2*D + 16) bytes, e.g.
+ * N <= 16384 at D = 64, top_k = 16).  No cudaMalloc or other allocation.
+ * The first call on a device looks up the array's device address (host-side
+ * set-up): make it before any stream capture.  All calls on a device share
+ * the array: each call clears what must start at zero, but calls whose GPU
+ * work overlaps (unordered streams) race on it.  Every GPU that loads this
+ * library's device code holds the array until the process exits (with
+ * CUDA's default lazy module loading, from this entry point's first call on
+ * that GPU). */
+int bsa_forward_noalloc(const bsa_problem* p, const void* Q, const void* K, const void* V,
+                        void* O, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
