@@ -219,42 +219,54 @@ bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict
 // ---------------------------------------------------------------------------
 // 4. The tensor-core fine kernel.
 //
-// 16 warps:
-//   0-3, 4-7  softmax/epilogue warpgroups; warpgroup g takes the items t with
-//             t % 2 == g and owns TMEM buffers S[g], O[g] and shared P[g]
-//   8         loader: each lane gathers four query rows of each item with
-//             16-byte cp.async (the LSU path streams random 128-byte rows
-//             faster than TMA gather4 issues them) and stages the item's list
-//             entries for the softmax warpgroups
-//   12        TMA: the item's K and V tiles
-//   13        one thread issues the MMAs in the order S0 S1 PV0 S2 PV1 S3 ...
-//             (S(t + 2) reuses the TMEM buffer PV(t)'s softmax just freed)
-// Shared memory holds a ring of NS load stages (Q rows, K, V, entries).  S
-// and O are read from TMEM 64 columns at a time, so every (block_size,
-// head_dim) pair fits in 128 registers per thread.
+// Warps (NWG = 3 softmax warpgroups when TMEM holds three (S, O) pairs, else 2):
+//   0 .. 4*NWG-1  softmax/epilogue: warpgroup w takes the items t with
+//                 t % NWG == w and owns TMEM S[w] (P overwrites it as bf16)
+//                 and O[w]; several items in flight hide each one's latency
+//   4*NWG .. +2   three loader warps: gather the item's 128 query rows with
+//                 16-byte cp.async, HD/8 lanes per row so each instruction
+//                 moves whole rows (random 128-byte rows stream faster through
+//                 the LSU path than TMA gather4 issues them, and three warps
+//                 keep enough of them in flight), and stage the item's list
+//                 entries (and the item) for the other warps.  The first
+//                 loader's lane 0 also issues the TMA loads of K and V, once
+//                 per run of consecutive items on the same key block (items
+//                 are sorted by block), into one of NKV >= NWG slots.  After
+//                 S(t) the stage holds the item's output rows, which the
+//                 warpgroup stores row-coalesced before releasing the stage
+//   4*NWG+3       one thread issues the MMAs: S(0..NWG-1), then PV(t) followed
+//                 by S(t + NWG), which reuses the TMEM PV(t) has just read
+// Shared memory: NQ query stages (gathered rows + entries), NKV K/V slots.
 template <int BS, int HD>
 struct KvCfg {
+  static constexpr int NWG = (BS + HD <= 128) ? 3 : 2;
   static constexpr int kQBytes = kTileRows * HD * 2;   // gathered queries
-  static constexpr int kKBytes = BS * HD * 2;          // key block
-  static constexpr int kVBytes = BS * HD * 2;          // value block
-  static constexpr int kPBytes = kTileRows * BS * 2;   // probabilities (bf16)
-  static constexpr int kStageBytes = kQBytes + kKBytes + kVBytes;
-  static constexpr int NS = (BS == 64 && HD == 64) ? 4 : (HD == 64 ? 3 : 2);
-  static constexpr int kMetaBytes = kTileRows * 4 + 16;      // entries + item
-  static constexpr int kRing = 256;          // staged work items per loader warp
-  static constexpr int kPOff = NS * kStageBytes;
-  static constexpr int kMetaOff = kPOff + 2 * kPBytes;
-  static constexpr int kRingOff = kMetaOff + NS * kMetaBytes;
-  static constexpr int kBarOff = kRingOff + kRing * 16;
-  static constexpr int kSmem = kBarOff + 256 + 1024 /*align*/;
-  static constexpr int kTmemCols = (2 * (BS + HD) <= 256) ? 256 : 512;
-  static constexpr uint32_t kKVBytes = kKBytes + kVBytes;
-  static constexpr int kLoaders = 32;
-  // ld_full completes on: the loader warp's entries-written arrive (lane 0),
-  // each loader lane's cp.async-landed arrive, and the TMA warp's expect_tx
-  // arrive.  Few arrivals keep the barrier's atomics off the critical path.
-  static constexpr int kLdFullCount = kLoaders + 2;
-  static constexpr int kThreads = 512;
+  static constexpr int NQ = (HD == 64) ? 8 : 4;          // query stages
+  static constexpr int kKBytes = BS * HD * 2;
+  static constexpr int kKVBytes = 2 * kKBytes;           // one block's K and V
+  // K/V slots.  Items t .. t+NWG-1 (the S MMAs issued ahead of PV(t)) can
+  // belong to NWG different block runs that must all be resident while PV(t)
+  // is pending, so NKV >= NWG is required (fewer slots deadlock); one more
+  // lets the next run load early when shared memory allows.
+  static constexpr int NKV =
+      (NQ * kQBytes + (NWG + 1) * kKVBytes + 24 * 1024 <= 220 * 1024) ? NWG + 1 : NWG;
+  static constexpr int kMetaBytes = kTileRows * 4 + 16;  // entries + item
+  static constexpr int kRing = 256;                      // staged work items per loader warp
+  static constexpr int kLoaderWarps = 3;
+  static constexpr int kKVOff = NQ * kQBytes;
+  static constexpr int kMetaOff = kKVOff + NKV * kKVBytes;
+  static constexpr int kRingOff = kMetaOff + NQ * kMetaBytes;
+  static constexpr int kGenOff = kRingOff + kLoaderWarps * kRing * 16;   // MMA's block-run ids
+  static constexpr int kGenRing = 16;
+  static constexpr int kBarOff = kGenOff + kGenRing * 4;
+  static constexpr int kSmem = kBarOff + 512 + 1024 /*align*/;
+  static constexpr int kTmemCols = 512;
+  static constexpr int kThreads = (4 * NWG + kLoaderWarps + 1) * 32;
+  // q_full completes on each loader thread's cp.async-landed arrive plus one
+  // entries-written arrive per loader warp.
+  static constexpr int kQFullCount = kLoaderWarps * 33;
+  static_assert(NWG * (BS + HD) <= 512, "TMEM holds NWG (S, O) pairs");
+  static_assert(kGenRing > NWG + 1, "the MMA thread looks one item ahead");
 };
 
 struct FineKvParams {
@@ -269,26 +281,31 @@ struct FineKvParams {
 };
 
 template <int BS, int HD>
-__global__ void __launch_bounds__(512, 1)
+__global__ void __launch_bounds__(KvCfg<BS, HD>::kThreads, 1)
 fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                FineKvParams prm) {
   using C = KvCfg<BS, HD>;
-  constexpr int NS = C::NS;
+  constexpr int NQ = C::NQ, NWG = C::NWG;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = (uint64_t*)(smem + C::kBarOff);
-  uint64_t* ld_full = bars;             // [NS] Q rows, K, V and entries of the stage's item landed
-  uint64_t* ld_empty = bars + NS;       // [NS] PV of the stage's item done
-  uint64_t* s_full = bars + 2 * NS;     // [2] S = QK^T in TMEM
-  uint64_t* p_full = bars + 2 * NS + 2; // [2] P in smem, S consumed (128 arrivals)
-  uint64_t* o_full = bars + 2 * NS + 4; // [2] O = PV in TMEM
-  uint64_t* o_free = bars + 2 * NS + 6; // [2] O loaded by the warpgroup (128 arrivals)
-  uint64_t* drain = bars + 2 * NS + 8;  // [1] final MMA completion
-  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * NS + 9);
-  volatile int* abort_flag = (volatile int*)(bars + 2 * NS + 10);
+  uint64_t* q_full = bars;                      // [NQ] rows + entries of the stage's item landed
+  uint64_t* q_empty = q_full + NQ;              // [NQ] stage free: the item's epilogue, which
+                                                //      stages its output rows there, is done
+  uint64_t* kv_full = q_empty + NQ;             // [NKV] K, V of a block run landed
+  uint64_t* kv_empty = kv_full + C::NKV;        // [NKV] last PV of a block run done
+  uint64_t* s_full = kv_empty + C::NKV;         // [NWG] S in TMEM
+  uint64_t* p_full = s_full + NWG;              // [NWG] P in TMEM (128 arrivals)
+  uint64_t* o_full = p_full + NWG;              // [NWG] O in TMEM
+  uint64_t* o_free = o_full + NWG;              // [NWG] O read out (128 arrivals)
+  uint64_t* drain = o_free + NWG;
+  uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+  volatile int* abort_flag = (volatile int*)(drain + 2);
   int4* ring = (int4*)(smem + C::kRingOff);
+  int* gen_ring = (int*)(smem + C::kGenOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int w_load = 4 * NWG, w_mma = 4 * NWG + C::kLoaderWarps;
   const Shape s = prm.s;
   const uint32_t total = *prm.total_items;
   const uint32_t G = gridDim.x;
@@ -298,11 +315,15 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant
   if (T <= 0) return;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < NS; ++i) {
-      mbar_init(&ld_full[i], C::kLdFullCount);
-      mbar_init(&ld_empty[i], 1);
+    for (int i = 0; i < NQ; ++i) {
+      mbar_init(&q_full[i], C::kQFullCount);
+      mbar_init(&q_empty[i], 128);
     }
-    for (int g = 0; g < 2; ++g) {
+    for (int i = 0; i < C::NKV; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int g = 0; g < NWG; ++g) {
       mbar_init(&s_full[g], 1);
       mbar_init(&p_full[g], 128);
       mbar_init(&o_full[g], 1);
@@ -312,7 +333,7 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 12 && lane == 0) {
+  if (warp == w_load && lane == 0) {
     prefetch_tensormap(&tmap_k);
     prefetch_tensormap(&tmap_v);
   }
@@ -322,66 +343,93 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
-  auto q_s = [&](int st) { return smem + st * C::kStageBytes; };
-  auto k_s = [&](int st) { return smem + st * C::kStageBytes + C::kQBytes; };
-  auto v_s = [&](int st) { return smem + st * C::kStageBytes + C::kQBytes + C::kKBytes; };
-  auto p_s = [&](int g) { return smem + C::kPOff + g * C::kPBytes; };
+  auto q_s = [&](int st) { return smem + st * C::kQBytes; };
+  auto k_s = [&](int slot) { return smem + C::kKVOff + slot * C::kKVBytes; };
+  auto v_s = [&](int slot) { return smem + C::kKVOff + slot * C::kKVBytes + C::kKBytes; };
   auto meta = [&](int st) { return (int32_t*)(smem + C::kMetaOff + st * C::kMetaBytes); };
   const float sc = s.scale * kLog2e;
 
-  if (warp == 8) {
-    // ------------------------------------------------------------ Q loader
-    // Lane l gathers rows 4l .. 4l+3 of each item.  The warp keeps the next
-    // work items in a ring of kRing entries, refilled half a ring at a time.
+  if (warp >= w_load && warp < w_mma) {
+    // ------------------------------------------------------------ Q loaders (+ K/V TMA)
+    // Loader L handles rows r = i*3*RPI + L*RPI + lane/CPR: CPR = HD/8 lanes
+    // per row, RPI = 32/CPR whole rows per instruction.  Each warp keeps its
+    // own ring of the next work items, refilled half a ring at a time.
+    constexpr int CPR = HD / 8, RPI = 32 / CPR, NLW = C::kLoaderWarps;
+    constexpr int ROWS = (kTileRows + NLW * RPI - 1) / (NLW * RPI);   // rows per lane
+    const int L = warp - w_load;
+    const int chunk = lane % CPR, panel = chunk >> 3, cc = chunk & 7;
+    int4* my_ring = ring + L * C::kRing;
     auto fill = [&](int base, int count) {   // items base .. base + count - 1
       for (int q = lane; q < count; q += 32)
-        if (base + q < T) ring[(base + q) % C::kRing] = prm.items[t_begin + base + q];
+        if (base + q < T) my_ring[(base + q) % C::kRing] = prm.items[t_begin + base + q];
       __syncwarp();
     };
-    struct Ent { int32_t e[4]; };
+    auto row_of = [&](int i) { return i * NLW * RPI + L * RPI + lane / CPR; };
+    struct Ent { int32_t e[ROWS]; };
     auto entries = [&](int t, Ent& E) {
       if (t >= T) return;
-      const int4 it = ring[t % C::kRing];
+      const int4 it = my_ring[t % C::kRing];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = lane * 4 + i;
-        E.e[i] = prm.lists[it.z + (r < it.w ? r : 0)];
+      for (int i = 0; i < ROWS; ++i) {
+        const int r = row_of(i);
+        E.e[i] = (r < kTileRows) ? prm.lists[it.z + (r < it.w ? r : 0)] : 0;
       }
     };
     fill(0, C::kRing);
     Ent E0, E1;
     entries(0, E0);
     entries(1, E1);
+    int gen = -1, px = -1, py = -1;   // K/V runs (first loader, lane 0)
     auto step = [&](int t, Ent& E) -> bool {
-      const int st = t % NS, use = t / NS;
-      const int4 it = ring[t % C::kRing];
-      int32_t e[4];
+      const int st = t % NQ, use = t / NQ;
+      const int4 it = my_ring[t % C::kRing];
+      int32_t e[ROWS];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) e[i] = E.e[i];
+      for (int i = 0; i < ROWS; ++i) e[i] = E.e[i];
       if (use >= 1) {
-        bool ok = mbar_wait(&ld_empty[st], (use - 1) & 1, prm.err, kErrWaitFree);
+        bool ok = mbar_wait(&q_empty[st], (use - 1) & 1, prm.err, kErrWaitFree);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok || *abort_flag) { *abort_flag = 1; return false; }
       }
       // Rows past the item's count gather its first query again (never stored).
       int32_t* m = meta(st);
+      const unsigned char* qbase = reinterpret_cast<const unsigned char*>(prm.q) +
+                                   (int64_t)it.x * s.N * (HD * 2) + chunk * 16;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = lane * 4 + i;
-        m[r] = e[i];
-        const unsigned char* src =
-            reinterpret_cast<const unsigned char*>(prm.q + ((int64_t)it.x * s.N + (e[i] >> 6)) * HD);
-        unsigned char* dst = q_s(st) + r * 128;
-#pragma unroll
-        for (int c = 0; c < HD / 8; ++c) {
-          const int panel = c >> 3, cc = c & 7;
-          cp_async16(dst + panel * (kTileRows * 128) + ((cc ^ (r & 7)) << 4), src + c * 16);
+      for (int i = 0; i < ROWS; ++i) {
+        const int r = row_of(i);
+        if (r < kTileRows) {
+          if (chunk == 0) m[r] = e[i];
+          cp_async16(q_s(st) + panel * (kTileRows * 128) + r * 128 + ((cc ^ (r & 7)) << 4),
+                     qbase + (int64_t)(e[i] >> 6) * (HD * 2));
         }
       }
-      if (lane == 0) reinterpret_cast<int4*>(m + kTileRows)[0] = it;
-      cp_async_arrive_noinc(&ld_full[st]);   // this lane's rows landed
+      if (L == 0 && lane == 0) reinterpret_cast<int4*>(m + kTileRows)[0] = it;
+      cp_async_arrive_noinc(&q_full[st]);   // this lane's rows landed
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ld_full[st]);  // entries visible
+      if (lane == 0) mbar_arrive(&q_full[st]);  // this warp's entries (and the item) visible
+      // K and V of a new block run, into slot run % NKV once that slot's
+      // previous run is done.
+      if (L == 0 && lane == 0 && (it.x != px || it.y != py)) {
+        px = it.x;
+        py = it.y;
+        ++gen;
+        const int slot = gen % C::NKV, kuse = gen / C::NKV;
+        if (kuse >= 1 && (!mbar_wait(&kv_empty[slot], (kuse - 1) & 1, prm.err, kErrWaitFree) ||
+                          *abort_flag)) {
+          *abort_flag = 1;
+        } else {
+          mbar_arrive_expect_tx(&kv_full[slot], C::kKVBytes);
+          const int32_t y = it.x * s.N + it.y * BS;
+#pragma unroll
+          for (int p = 0; p < HD / 64; ++p) {
+            tma_load_2d(k_s(slot) + p * (BS * 128), &tmap_k, &kv_full[slot], p * 64, y);
+            tma_load_2d(v_s(slot) + p * (BS * 128), &tmap_v, &kv_full[slot], p * 64, y);
+          }
+        }
+      }
+      __syncwarp();
+      if (*abort_flag) return false;
       // Entering a new half ring: the half before it is done, so refill that
       // half with the items one ring ahead.  Then load item t + 2's entries.
       constexpr int H = C::kRing / 2;
@@ -393,80 +441,66 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant
       if (!step(t, E0)) break;
       if (t + 1 < T && !step(t + 1, E1)) break;
     }
-  } else if (warp == 12) {
-    // ------------------------------------------------------------ K/V TMA
-    if (lane == 0) {
-      int4 A = prm.items[t_begin], B = T > 1 ? prm.items[t_begin + 1] : A;
-      auto step = [&](int t, int4& X) -> bool {
-        const int st = t % NS, use = t / NS;
-        const int4 it = X;
-        if (t + 2 < T) X = prm.items[t_begin + t + 2];
-        if (use >= 1 && (!mbar_wait(&ld_empty[st], (use - 1) & 1, prm.err, kErrWaitFree) || *abort_flag)) {
-          *abort_flag = 1;
-          return false;
-        }
-        mbar_arrive_expect_tx(&ld_full[st], C::kKVBytes);
-        const int32_t y = it.x * s.N + it.y * BS;
-#pragma unroll
-        for (int p = 0; p < HD / 64; ++p) {
-          tma_load_2d(k_s(st) + p * (BS * 128), &tmap_k, &ld_full[st], p * 64, y);
-          tma_load_2d(v_s(st) + p * (BS * 128), &tmap_v, &ld_full[st], p * 64, y);
-        }
-        return true;
-      };
-      for (int t = 0; t < T; t += 2) {
-        if (!step(t, A)) break;
-        if (t + 1 < T && !step(t + 1, B)) break;
-      }
-    }
-    __syncwarp();
-  } else if (warp == 13) {
+  } else if (warp == w_mma) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(kTileRows, BS, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(kTileRows, HD, true);
-      // Descriptors at stage / buffer 0; the start-address field (bits 0-13,
+      // Descriptors at stage / slot 0; the start-address field (bits 0-13,
       // address >> 4) is advanced by adding byte offsets >> 4.
       const uint64_t dq0 = smem_desc_sw128(smem_u32(q_s(0)), 16, 1024);
       const uint64_t dk0 = smem_desc_sw128(smem_u32(k_s(0)), 16, 1024);
-      const uint64_t dp0 = smem_desc_sw128(smem_u32(p_s(0)), 16, 1024);
       const uint64_t dv0 = smem_desc_sw128(smem_u32(v_s(0)), BS * 128, 1024);
+      int gen = -1, px = -1, py = -1;
       auto issue_s = [&](int t) -> bool {
-        const int st = t % NS;
-        if (!mbar_wait(&ld_full[st], (t / NS) & 1, prm.err, kErrWaitQ)) return false;
+        const int st = t % NQ;
+        if (!mbar_wait(&q_full[st], (t / NQ) & 1, prm.err, kErrWaitQ)) return false;
+        const int4 it = reinterpret_cast<const int4*>(meta(st) + kTileRows)[0];
+        if (it.x != px || it.y != py) {
+          ++gen;
+          px = it.x;
+          py = it.y;
+        }
+        gen_ring[t % C::kGenRing] = gen;
+        const int slot = gen % C::NKV;
+        if (!mbar_wait(&kv_full[slot], (gen / C::NKV) & 1, prm.err, kErrWaitQ)) return false;
         tc_fence_after();
-        const uint32_t d = tbase + (t & 1) * (BS + HD);
-        const uint64_t dq = dq0 + ((st * C::kStageBytes) >> 4), dk = dk0 + ((st * C::kStageBytes) >> 4);
+        const uint32_t d = tbase + (t % NWG) * (BS + HD);
+        const uint64_t dq = dq0 + ((st * C::kQBytes) >> 4);
+        const uint64_t dk = dk0 + ((slot * C::kKVBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (kTileRows * 128) + (kk & 3) * 32;
           const uint32_t offk = (kk >> 2) * (BS * 128) + (kk & 3) * 32;
           mma_bf16(d, dq + (off >> 4), dk + (offk >> 4), idesc_s, kk > 0);
         }
-        mma_commit(&s_full[t & 1]);
+        mma_commit(&s_full[t % NWG]);
         return true;
       };
       auto issue_o = [&](int t) -> bool {
-        const int g = t & 1, st = t % NS;
-        if (!mbar_wait(&p_full[g], (t >> 1) & 1, prm.err, kErrWaitP)) return false;
-        if (t >= 2 && !mbar_wait(&o_free[g], ((t - 2) >> 1) & 1, prm.err, kErrWaitFree)) return false;
+        const int w = t % NWG, n = t / NWG;
+        if (!mbar_wait(&p_full[w], n & 1, prm.err, kErrWaitP)) return false;
+        if (n >= 1 && !mbar_wait(&o_free[w], (n - 1) & 1, prm.err, kErrWaitFree)) return false;
         tc_fence_after();
-        const uint32_t d = tbase + g * (BS + HD) + BS;
-        const uint64_t dp = dp0 + ((g * C::kPBytes) >> 4), dv = dv0 + ((st * C::kStageBytes) >> 4);
+        const int g = gen_ring[t % C::kGenRing];
+        const int slot = g % C::NKV;
+        const uint32_t d = tbase + w * (BS + HD) + BS;
+        const uint32_t pa = tbase + w * (BS + HD);   // P: bf16 pairs over S's first BS/2 columns
+        const uint64_t dv = dv0 + ((slot * C::kKVBytes) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < BS / 16; ++kk) {
-          const uint32_t offp = (kk >> 2) * (kTileRows * 128) + (kk & 3) * 32;
-          mma_bf16(d, dp + (offp >> 4), dv + ((kk * 16 * 128) >> 4), idesc_o, kk > 0);
-        }
-        mma_commit(&o_full[g]);
-        mma_commit(&ld_empty[st]);
+        for (int kk = 0; kk < BS / 16; ++kk)
+          mma_bf16_ts(d, pa + kk * 8, dv + ((kk * 16 * 128) >> 4), idesc_o, kk > 0);
+        mma_commit(&o_full[w]);
+        // The run's last item frees its K/V slot.  S(t + 1) is already
+        // issued (NWG >= 2), so its run id is known.
+        if (t + 1 == T || gen_ring[(t + 1) % C::kGenRing] != g) mma_commit(&kv_empty[slot]);
         return true;
       };
-      bool ok = issue_s(0);
-      if (ok && T > 1) ok = issue_s(1);
+      bool ok = true;
+      for (int t = 0; ok && t < NWG && t < T; ++t) ok = issue_s(t);
       for (int t = 0; ok && t < T; ++t) {
         ok = issue_o(t);
-        if (ok && t + 2 < T) ok = issue_s(t + 2);
+        if (ok && t + NWG < T) ok = issue_s(t + NWG);
         if (*abort_flag) ok = false;
       }
       if (!ok) *abort_flag = 1;
@@ -475,15 +509,17 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant
       mbar_wait(drain, 0, prm.err, kErrWaitDrain);
     }
     __syncwarp();
-  } else if (warp < 8) {
+  } else if (warp < 4 * NWG) {
     // ------------------------------------------------------------ softmax / epilogue
-    const int wg = warp >> 2;              // 0 or 1: takes items t with t & 1 == wg
+    const int wg = warp >> 2;              // takes items t with t % NWG == wg
     const int quad = warp & 3;             // TMEM lane quadrant
     const int r = quad * 32 + lane;        // row of the tile this thread owns
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    for (int t = wg; t < T; t += 2) {
-      const int g = wg, n = t >> 1, st = t % NS;
-      bool ok = mbar_wait(&ld_full[st], (t / NS) & 1, prm.err, kErrWaitQ);
+    const uint32_t s_addr = tbase + lane_off + wg * (BS + HD);
+    const uint32_t o_addr = s_addr + BS;
+    for (int t = wg; t < T; t += NWG) {
+      const int n = t / NWG, st = t % NQ;
+      bool ok = mbar_wait(&q_full[st], (t / NQ) & 1, prm.err, kErrWaitQ);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok || *abort_flag) { *abort_flag = 1; break; }
       const int32_t* m = meta(st);
@@ -493,11 +529,10 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant
       const int32_t e = m[r];
       const int qrow = e >> 6, slot = e & 63;
 
-      ok = mbar_wait(&s_full[g], n & 1, prm.err, kErrWaitS);
+      ok = mbar_wait(&s_full[wg], n & 1, prm.err, kErrWaitS);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok || *abort_flag) { *abort_flag = 1; break; }
       tc_fence_after();
-      const uint32_t s_addr = tbase + lane_off + g * (BS + HD);
       const int key0 = j * BS;
       const bool diag = s.causal && key0 + BS - 1 > qrow;
       float sv[64];
@@ -525,55 +560,74 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant
       // Padding rows of a short item can be fully masked; keep them finite.
       const float msc = (mx == -INFINITY) ? 0.f : mx * sc;
       float l0 = 0.f, l1 = 0.f;
-      unsigned char* prow = p_s(g) + r * 128;
 #pragma unroll
       for (int c0 = 0; c0 < BS; c0 += 64) {
         if (BS > 64) load_s(c0);   // with one chunk the values are still in sv
+        uint32_t pk[32];
 #pragma unroll
-        for (int c = 0; c < 64; c += 8) {
-          float p[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) p[i] = fast_exp2(fmaf(sv[c + i], sc, -msc));
-          l0 += (p[0] + p[1]) + (p[2] + p[3]);
-          l1 += (p[4] + p[5]) + (p[6] + p[7]);
-          uint4 w = make_uint4(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]),
-                               pack_bf16x2(p[4], p[5]), pack_bf16x2(p[6], p[7]));
-          const int chunk = c >> 3;
-          *reinterpret_cast<uint4*>(prow + (c0 >> 6) * (kTileRows * 128) + ((chunk ^ (r & 7)) << 4)) = w;
+        for (int c = 0; c < 64; c += 2) {
+          const float p0 = fast_exp2(fmaf(sv[c], sc, -msc));
+          const float p1 = fast_exp2(fmaf(sv[c + 1], sc, -msc));
+          l0 += p0;
+          l1 += p1;
+          pk[c >> 1] = pack_bf16x2(p0, p1);
         }
+        // P (bf16 pairs) overwrites the S columns this chunk has consumed.
+        tmem_st32(s_addr + (c0 >> 1), pk);
       }
       const float l = l0 + l1;
-      fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&p_full[g]);
+      mbar_arrive(&p_full[wg]);
 
-      ok = mbar_wait(&o_full[g], n & 1, prm.err, kErrWaitO);
+      ok = mbar_wait(&o_full[wg], n & 1, prm.err, kErrWaitO);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok || *abort_flag) { *abort_flag = 1; break; }
       tc_fence_after();
-      const uint32_t o_addr = tbase + lane_off + g * (BS + HD) + BS;
       const float inv = 1.f / l;
-      const int64_t pe = ((int64_t)u * s.N + qrow) * s.k + slot;
-      uint4* dst = reinterpret_cast<uint4*>(prm.part_o + pe * HD);
+      // The item's query rows are consumed (S(t) is done), so its stage holds
+      // the output rows for a coalesced store: row r, chunk c at the same
+      // swizzled place a gathered query chunk occupied.
+      unsigned char* stage = q_s(st);
 #pragma unroll
       for (int c0 = 0; c0 < HD; c0 += 64) {
         float ov[64];
         tmem_ld64(o_addr + c0, ov);
         if (c0 + 64 >= HD) {
           tc_fence_before();
-          mbar_arrive(&o_free[g]);
+          mbar_arrive(&o_free[wg]);
         }
-        if (valid) {
 #pragma unroll
-          for (int c = 0; c < 64; c += 8) {
-            dst[(c0 + c) >> 3] = make_uint4(pack_bf16x2(ov[c] * inv, ov[c + 1] * inv),
-                                            pack_bf16x2(ov[c + 2] * inv, ov[c + 3] * inv),
-                                            pack_bf16x2(ov[c + 4] * inv, ov[c + 5] * inv),
-                                            pack_bf16x2(ov[c + 6] * inv, ov[c + 7] * inv));
+        for (int c = 0; c < 64; c += 8) {
+          const int ch = c >> 3;
+          *reinterpret_cast<uint4*>(stage + (c0 >> 6) * (kTileRows * 128) + r * 128 +
+                                    ((ch ^ (r & 7)) << 4)) =
+              make_uint4(pack_bf16x2(ov[c] * inv, ov[c + 1] * inv),
+                         pack_bf16x2(ov[c + 2] * inv, ov[c + 3] * inv),
+                         pack_bf16x2(ov[c + 4] * inv, ov[c + 5] * inv),
+                         pack_bf16x2(ov[c + 6] * inv, ov[c + 7] * inv));
+        }
+      }
+      const int64_t pe = ((int64_t)u * s.N + qrow) * s.k + slot;
+      if (valid) prm.part_ml[pe] = make_float2(msc, l);
+      __syncwarp();
+      {
+        // This warp's 32 rows, 32 / CPR whole rows per instruction.
+        constexpr int CPR = HD / 8, RPI = 32 / CPR;
+        const int chunk = lane % CPR, panel = chunk >> 3, cc = chunk & 7;
+#pragma unroll 4
+        for (int i = 0; i < 32 / RPI; ++i) {
+          const int rr = quad * 32 + i * RPI + lane / CPR;
+          if (rr < cnt) {
+            const int32_t er = m[rr];
+            const int64_t pr = ((int64_t)u * s.N + (er >> 6)) * s.k + (er & 63);
+            const uint4 v = *reinterpret_cast<const uint4*>(
+                stage + panel * (kTileRows * 128) + rr * 128 + ((cc ^ (rr & 7)) << 4));
+            reinterpret_cast<uint4*>(prm.part_o + pr * HD)[chunk] = v;
           }
         }
       }
-      if (valid) prm.part_ml[pe] = make_float2(msc, l);
+      __syncwarp();
+      mbar_arrive(&q_empty[st]);   // this thread is done with the stage
     }
   }
   tc_fence_before();
