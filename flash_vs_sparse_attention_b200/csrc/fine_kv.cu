@@ -9,23 +9,25 @@
 // tiles.  The stage therefore runs as:
 //
 //  1. bucket_count   per-unit histogram of the selected block ids
-//  2. bucket_scan    per block: list offset and 128-query work items
-//  3. bucket_scatter list entries (query row << 6 | slot) grouped by block
+//  2. bucket_scan    per block: list offset, first work item, and work items
+//                    of at most 128 queries
+//  3. bucket_scatter per block, the query rows that picked it (its list), and
+//                    for every (query, slot) the partial row its result goes
+//                    to: work item i owns partial rows [128 i, 128 i + 128)
 //  4. fine_kv        persistent kernel over work items.  For each item (one
-//                    key block, <= 128 queries that picked it): TMA loads the
-//                    block's K and V tiles, TMA gather4 loads the 128 query
-//                    rows, tcgen05 computes S = Q K^T into TMEM, a softmax
-//                    warpgroup turns its row of S into P (bf16, shared
-//                    memory) with the row's max m and sum l, tcgen05 computes
-//                    O = P V into TMEM, and the warpgroup writes the partial
-//                    (O / l as bf16, m, l) for that (query, slot).
+//                    key block, <= 128 queries that picked it): TMA gather4
+//                    loads the 128 query rows, TMA loads the block's K and V
+//                    (once per run of items on the same block), tcgen05
+//                    computes S = Q K^T into TMEM, a softmax warpgroup turns
+//                    it into P (bf16, TMEM) with each row's max m and sum l,
+//                    tcgen05 computes O = P V into TMEM, and the warpgroup
+//                    stores the item's partial tile (O as bf16, m, l) with
+//                    TMA stores: 128 contiguous rows per item.
 //  5. combine        per query: log-sum-exp merge of its top_k partials,
 //                    rounded to bf16 once.
 //
-// fine_kv warp roles (320 threads): warps 0-3 and 4-7 are two softmax /
-// epilogue warpgroups that take alternate work items (buffer g = item & 1), so
-// one group's exponentials overlap the other's MMAs and stores; warp 8 issues
-// TMA; one thread of warp 9 issues the MMAs.  All waits are bounded.
+// All waits are bounded (a stuck pipeline ends with an error word, not a
+// hang).  Warp roles and the barrier discipline are described at KvCfg.
 #include <cudaTypedefs.h>
 
 #include <cstdio>
@@ -45,19 +47,22 @@ constexpr int kMaxNbKv = 32768;
 // Error codes ORed into the workspace error word.
 enum : uint32_t {
   kErrWaitQ = 1u, kErrWaitS = 2u, kErrWaitP = 4u, kErrWaitO = 8u, kErrWaitFree = 16u,
-  kErrWaitDrain = 32u
+  kErrWaitDrain = 32u, kErrWaitStaged = 64u, kErrWaitKV = 128u, kErrWaitEnt = 256u
 };
 
 struct FineWs {
   int32_t* counts;     // units * nb
   int32_t* cursors;    // units * nb
   uint32_t* err;       // [0] error bits, [1] total work items
-  int32_t* offsets;    // units * nb
+  int32_t* offsets;    // units * nb: a block's first position in its unit's list
+  int32_t* item_off;   // units * nb: a block's first work item (global item index)
   int4* items;         // units * max_items_per_unit
-  int32_t* lists;      // units * N * k
-  __nv_bfloat16* part_o;  // units * N * k * D
-  float2* part_ml;     // units * N * k
+  int32_t* lists;      // units * N * k: query rows grouped by block
+  int32_t* inv;        // units * N * k: (query, slot) -> partial row
+  __nv_bfloat16* part_o;  // 128 rows per work item, D columns
+  float2* part_ml;     // 128 rows per work item
   size_t zero_bytes;   // counts + cursors + err, contiguous from counts
+  int64_t part_rows;   // rows of part_o / part_ml
   size_t total;
 };
 
@@ -76,22 +81,27 @@ static FineWs fine_ws_layout(const Shape& s, unsigned char* base) {
     off = a256(off + bytes);
     return base ? base + o : nullptr;
   };
+  w.part_rows = (int64_t)U * max_items_per_unit(s) * kTileRows;
   w.counts = (int32_t*)take(4 * U * nb);
   w.cursors = (int32_t*)take(4 * U * nb);
   w.err = (uint32_t*)take(16);
   w.zero_bytes = off;
   w.offsets = (int32_t*)take(4 * U * nb);
+  w.item_off = (int32_t*)take(4 * U * nb);
   w.items = (int4*)take(16 * U * (size_t)max_items_per_unit(s));
-  w.lists = (int32_t*)take(4 * U * Nk);
-  w.part_o = (__nv_bfloat16*)take(2 * U * Nk * s.D);
-  w.part_ml = (float2*)take(8 * U * Nk);
+  w.lists = (int32_t*)take(4 * (U * Nk + 256));   // slack for aligned list-slice copies
+  w.inv = (int32_t*)take(4 * U * Nk);
+  w.part_o = (__nv_bfloat16*)take(2 * (size_t)w.part_rows * s.D);
+  w.part_ml = (float2*)take(8 * (size_t)w.part_rows);
   w.total = off;
   return w;
 }
 
 bool fine_kv_supported(const Shape& s) {
   const bool shape_ok = (s.bs == 64 && (s.D == 64 || s.D == 128)) || (s.bs == 128 && s.D == 64);
-  return shape_ok && s.k <= 64 && s.nb <= kMaxNbKv && s.N < (1 << 25) &&
+  // Partial rows (128 per work item) are addressed with int32.
+  const int64_t part_rows = (int64_t)s.units * max_items_per_unit(s) * kTileRows;
+  return shape_ok && s.k <= 64 && s.nb <= kMaxNbKv && part_rows < (1LL << 31) &&
          (int64_t)s.units * s.N * s.k < (1LL << 31);
 }
 
@@ -128,8 +138,8 @@ bucket_count_kernel(const int32_t* __restrict__ idx, int32_t* __restrict__ count
 //    most 128 queries per block.  One CTA of 1024 threads per unit.
 __global__ void __launch_bounds__(1024)
 bucket_scan_kernel(const int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
-                   int4* __restrict__ items, uint32_t* __restrict__ err, Shape s,
-                   int64_t max_items) {
+                   int32_t* __restrict__ item_off, int4* __restrict__ items,
+                   uint32_t* __restrict__ err, Shape s) {
   __shared__ int32_t wsum_c[32], wsum_t[32];
   __shared__ int32_t item_base;
   const int u = blockIdx.x;
@@ -171,18 +181,21 @@ bucket_scan_kernel(const int32_t* __restrict__ counts, int32_t* __restrict__ off
   for (int j = j0; j < j1; ++j) {
     const int cj = c[j];
     offsets[(int64_t)u * s.nb + j] = oc;
+    item_off[(int64_t)u * s.nb + j] = item_base + ot;
     for (int t = 0; t * kTileRows < cj; ++t) {
       out[ot++] = make_int4(u, j, (int)(list_base + oc + t * kTileRows), min(kTileRows, cj - t * kTileRows));
     }
     oc += cj;
   }
-  (void)max_items;
 }
 
-// 3. List entries grouped by block: entry = query_row << 6 | slot.
+// 3. Per block, the query rows that picked it (its list), and for every
+//    (query, slot) the partial row its result lands in: work item i owns
+//    partial rows [128 i, 128 i + 128), one per list entry of the item.
 __global__ void __launch_bounds__(256)
 bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ offsets,
-                      int32_t* __restrict__ cursors, int32_t* __restrict__ lists, Shape s) {
+                      const int32_t* __restrict__ item_off, int32_t* __restrict__ cursors,
+                      int32_t* __restrict__ lists, int32_t* __restrict__ inv, Shape s) {
   extern __shared__ int32_t hist[];
   const int u = blockIdx.y;
   for (int j = threadIdx.x; j < s.nb; j += blockDim.x) hist[j] = 0;
@@ -195,23 +208,21 @@ bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict
     if (j >= 0) atomicAdd(&hist[j], 1);
   }
   __syncthreads();
-  // Reserve this CTA's range in every block's list.
+  // Reserve this CTA's range within every block's list.
   for (int j = threadIdx.x; j < s.nb; j += blockDim.x) {
     int n = hist[j];
-    if (n) {
-      int64_t g = (int64_t)u * s.nb + j;
-      hist[j] = offsets[g] + atomicAdd(&cursors[g], n);
-    }
+    if (n) hist[j] = atomicAdd(&cursors[(int64_t)u * s.nb + j], n);
   }
   __syncthreads();
   int32_t* ul = lists + (int64_t)u * s.N * s.k;
   for (int64_t e = threadIdx.x; e < ne; e += blockDim.x) {
     int j = idx[e0 + e];
     if (j >= 0) {
-      int pos = atomicAdd(&hist[j], 1);
-      int64_t le = row0 * s.k + e;  // entry index within the unit
-      int row = (int)(le / s.k), slot = (int)(le % s.k);
-      ul[pos] = (row << 6) | slot;
+      const int64_t g = (int64_t)u * s.nb + j;
+      const int pos = atomicAdd(&hist[j], 1);   // position within block j's list
+      const int64_t le = row0 * s.k + e;        // entry index within the unit
+      ul[offsets[g] + pos] = (int)(le / s.k);
+      inv[e0 + e] = item_off[g] * kTileRows + pos;
     }
   }
 }
@@ -220,61 +231,108 @@ bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict
 // 4. The tensor-core fine kernel.
 //
 // Warps (NWG = 3 softmax warpgroups when TMEM holds three (S, O) pairs, else 2):
-//   0 .. 4*NWG-1  softmax/epilogue: warpgroup w takes the items t with
-//                 t % NWG == w and owns TMEM S[w] (P overwrites it as bf16)
-//                 and O[w]; several items in flight hide each one's latency
-//   4*NWG .. +2   three loader warps: gather the item's 128 query rows with
-//                 16-byte cp.async, HD/8 lanes per row so each instruction
-//                 moves whole rows (random 128-byte rows stream faster through
-//                 the LSU path than TMA gather4 issues them, and three warps
-//                 keep enough of them in flight), and stage the item's list
-//                 entries (and the item) for the other warps.  The first
-//                 loader's lane 0 also issues the TMA loads of K and V, once
-//                 per run of consecutive items on the same key block (items
-//                 are sorted by block), into one of NKV >= NWG slots.  After
-//                 S(t) the stage holds the item's output rows, which the
-//                 warpgroup stores row-coalesced before releasing the stage
-//   4*NWG+3       one thread issues the MMAs: S(0..NWG-1), then PV(t) followed
-//                 by S(t + NWG), which reuses the TMEM PV(t) has just read
-// Shared memory: NQ query stages (gathered rows + entries), NKV K/V slots.
+//   0 .. 4*NWG-1  warpgroup w takes the items t with t % NWG == w and owns
+//                 TMEM columns S[w] (P overwrites them as bf16 pairs) and
+//                 O[w].  Per item: softmax of S(t) into P(t); the group's
+//                 first warp then issues PV(t) and, right behind it,
+//                 S(t + NWG) for the group's next item, so the tensor core
+//                 works on the next tile while the group writes this one's
+//                 output.  Each warp stores its own 32 output rows.  Each warpgroup issues its own MMAs: one thread's
+//                 chain of commit-and-wait steps is latency-bound (~500
+//                 cycles per commit at these tile sizes), and independent
+//                 issuers overlap.
+//   4*NWG .. +NG-1  NG gather warps, item t to warp t % NG: one bulk copy
+//                 brings the item's list slice (query rows) into a small
+//                 per-warp ring two of the warp's items ahead; the warp then
+//                 writes the rows into the stage's entries and issues one TMA
+//                 gather4 (four 128-byte rows) per lane.  TMA keeps the
+//                 gathers off the load/store pipe, which the softmax warps'
+//                 instruction stream would otherwise starve.
+//   4*NWG+NG      the K/V warp: for every item in order, writes the item and
+//                 its K/V slot into the stage, and issues the TMA loads of K
+//                 and V once per run of consecutive items on the same key
+//                 block (items are sorted by block), into one of NKV >= NWG
+//                 slots.  A slot is reloaded once every warpgroup has seen
+//                 the O of all its items up to the old run's last one (the
+//                 groups publish that progress in shared memory), since the
+//                 run's items are spread over all groups' MMA streams.
+// A query stage is handed back as soon as S of its item is done; each warp
+// stages its 32 output rows in its group's buffer and stores them with TMA.
+// Shared memory: NQ query stages (gathered rows + entries), NWG output tiles,
+// NKV K/V slots.
+//
+// Every mbarrier here is waited by phase parity, which is only sound if no
+// waiter can run two phases ahead of the barrier.  Hence: stage st serves
+// items st, st + NQ, ..., and NQ is a multiple of both NWG and NG, so one
+// warpgroup consumes and one gather warp fills every use of a stage, each in
+// order; the K/V warp visits every item in order; and K/V loads complete on
+// 2 * NKV barriers (run % (2 NKV)), so a barrier's previous use (2 NKV runs
+// back) has always completed before anyone waits for its next one.
 template <int BS, int HD>
 struct KvCfg {
   static constexpr int NWG = (BS + HD <= 128) ? 3 : 2;
-  static constexpr int kQBytes = kTileRows * HD * 2;   // gathered queries
-  static constexpr int NQ = (HD == 64) ? 8 : 4;          // query stages
+  static constexpr int NG = NWG;                         // gather warps
+  static constexpr int kQBytes = kTileRows * HD * 2;     // gathered queries of one item
+  // Query stages.  A stage is released as soon as S of its item is done, so
+  // two per warpgroup keep the next item of every group loaded ahead (one
+  // per group at head_dim 128, where K/V slots need the room).
+  static constexpr int NQ = (HD == 64) ? 2 * NWG : NWG;
+  static constexpr int kOutBytes = kTileRows * HD * 2;   // a group's output tile (bf16)
   static constexpr int kKBytes = BS * HD * 2;
   static constexpr int kKVBytes = 2 * kKBytes;           // one block's K and V
-  // K/V slots.  Items t .. t+NWG-1 (the S MMAs issued ahead of PV(t)) can
-  // belong to NWG different block runs that must all be resident while PV(t)
-  // is pending, so NKV >= NWG is required (fewer slots deadlock); one more
-  // lets the next run load early when shared memory allows.
-  static constexpr int NKV =
-      (NQ * kQBytes + (NWG + 1) * kKVBytes + 24 * 1024 <= 220 * 1024) ? NWG + 1 : NWG;
-  static constexpr int kMetaBytes = kTileRows * 4 + 16;  // entries + item
-  static constexpr int kRing = 256;                      // staged work items per loader warp
-  static constexpr int kLoaderWarps = 3;
-  static constexpr int kKVOff = NQ * kQBytes;
+  // Per stage: 128 list entries, the item (int4), its K/V word.
+  static constexpr int kMetaBytes = kTileRows * 4 + 32;
+  static constexpr int kRing = 128;                      // staged work items per loader warp
+  static constexpr int kLoaderWarps = NG + 1;            // + the K/V warp
+  static constexpr int kEntSlots = 3;                    // list slices in flight per gather warp
+  // A list slice copy starts at the 16-byte boundary at or below the item's
+  // first entry: up to 3 leading entries, 128 entries, padded to 16 bytes.
+  static constexpr int kEntBytes = (kTileRows + 4) * 4;
+  static constexpr int kSmemLimit = 227 * 1024;
+  static constexpr int kFixed = NQ * kQBytes + NWG * kOutBytes + NQ * kMetaBytes +
+                                kLoaderWarps * kRing * 16 + NG * kEntSlots * kEntBytes +
+                                512 /*barriers*/ + 1024 /*alignment*/;
+  // K/V slots.  Reloading the slot of the run NKV runs back waits for the
+  // O of every item up to that run's last one, which is at least NKV items
+  // back; with NKV >= NWG those items' S MMAs never wait for the run being
+  // loaded, so NKV >= NWG slots suffice.  More let later runs load early:
+  // as many as shared memory allows, up to 8.
+  static constexpr int kKVFit = (kSmemLimit - kFixed) / kKVBytes;
+  static constexpr int NKV = kKVFit > 8 ? 8 : kKVFit;
+  static constexpr int kOutOff = NQ * kQBytes;
+  static constexpr int kKVOff = kOutOff + NWG * kOutBytes;
   static constexpr int kMetaOff = kKVOff + NKV * kKVBytes;
   static constexpr int kRingOff = kMetaOff + NQ * kMetaBytes;
-  static constexpr int kGenOff = kRingOff + kLoaderWarps * kRing * 16;   // MMA's block-run ids
-  static constexpr int kGenRing = 16;
-  static constexpr int kBarOff = kGenOff + kGenRing * 4;
+  static constexpr int kEntOff = kRingOff + kLoaderWarps * kRing * 16;
+  static constexpr int kBarOff = kEntOff + NG * kEntSlots * kEntBytes;
   static constexpr int kSmem = kBarOff + 512 + 1024 /*align*/;
   static constexpr int kTmemCols = 512;
-  static constexpr int kThreads = (4 * NWG + kLoaderWarps + 1) * 32;
-  // q_full completes on each loader thread's cp.async-landed arrive plus one
-  // entries-written arrive per loader warp.
-  static constexpr int kQFullCount = kLoaderWarps * 33;
-  static_assert(NWG * (BS + HD) <= 512, "TMEM holds NWG (S, O) pairs");
-  static_assert(kGenRing > NWG + 1, "the MMA thread looks one item ahead");
+  static constexpr int kThreads = (4 * NWG + kLoaderWarps) * 32;
+  // q_full completes on two arrivals (the gather warp's, with the gathered
+  // bytes, and the K/V warp's) plus the gathered bytes; q_empty on one
+  // arrival per warp of the consuming group once S of the item is done.
+  static constexpr int kQFullCount = 2;
+  static constexpr int kQEmptyCount = 4;
+  static constexpr int kGroupCols = BS + BS / 2 + HD;    // TMEM: S, P, O of one group
+  static_assert(NWG * kGroupCols <= 512, "TMEM holds NWG (S, P, O) sets");
+  static_assert(NKV >= NWG && NKV <= 8, "K/V slots");
+  static_assert(NQ % NWG == 0 && NQ % NG == 0, "one consumer and one producer per stage");
+  static_assert(kSmem <= kSmemLimit, "shared memory");
+  static_assert(kOutOff % 1024 == 0 && kKVOff % 1024 == 0, "swizzled tiles 1024-byte aligned");
+  static_assert(kEntBytes % 16 == 0 && kMetaBytes % 16 == 0 && kRingOff % 16 == 0 &&
+                    kEntOff % 16 == 0,
+                "alignment");
+  static_assert((2 * NQ + 2 * NKV + 5 * NWG + NG * kEntSlots) * 8 + 8 + 4 * (NWG + NKV) <= 512,
+                "barrier area");
 };
 
+// K/V word of a staged item: slot | kv_full barrier << 8 | its phase parity << 16.
+constexpr int kMetaKv = kTileRows + 4;   // int offset of the word in the stage meta
+
 struct FineKvParams {
-  const __nv_bfloat16* q;
   const int4* items;
   const int32_t* lists;
   const uint32_t* total_items;  // device word written by bucket_scan
-  __nv_bfloat16* part_o;
   float2* part_ml;
   uint32_t* err;
   Shape s;
@@ -282,7 +340,8 @@ struct FineKvParams {
 
 template <int BS, int HD>
 __global__ void __launch_bounds__(KvCfg<BS, HD>::kThreads, 1)
-fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+               const __grid_constant__ CUtensorMap tmap_v, const __grid_constant__ CUtensorMap tmap_o,
                FineKvParams prm) {
   using C = KvCfg<BS, HD>;
   constexpr int NQ = C::NQ, NWG = C::NWG;
@@ -290,22 +349,24 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = (uint64_t*)(smem + C::kBarOff);
   uint64_t* q_full = bars;                      // [NQ] rows + entries of the stage's item landed
-  uint64_t* q_empty = q_full + NQ;              // [NQ] stage free: the item's epilogue, which
-                                                //      stages its output rows there, is done
-  uint64_t* kv_full = q_empty + NQ;             // [NKV] K, V of a block run landed
-  uint64_t* kv_empty = kv_full + C::NKV;        // [NKV] last PV of a block run done
-  uint64_t* s_full = kv_empty + C::NKV;         // [NWG] S in TMEM
-  uint64_t* p_full = s_full + NWG;              // [NWG] P in TMEM (128 arrivals)
+  uint64_t* q_empty = q_full + NQ;              // [NQ] stage free: S of its item is done
+  uint64_t* kv_full = q_empty + NQ;             // [2 NKV] K, V of a block run landed
+                                                //         (run % (2 NKV))
+  uint64_t* s_full = kv_full + 2 * C::NKV;      // [NWG] S in TMEM
+  uint64_t* s_free = s_full + NWG;              // [NWG] S read out (128 arrivals)
+  uint64_t* p_full = s_free + NWG;              // [NWG] P in TMEM and the previous O read
+                                                //       out (128 arrivals)
   uint64_t* o_full = p_full + NWG;              // [NWG] O in TMEM
-  uint64_t* o_free = o_full + NWG;              // [NWG] O read out (128 arrivals)
-  uint64_t* drain = o_free + NWG;
-  uint32_t* tmem_slot = (uint32_t*)(drain + 1);
-  volatile int* abort_flag = (volatile int*)(drain + 2);
+  uint64_t* drain = o_full + NWG;               // [NWG] the group's MMAs are complete
+  uint64_t* ent_full = drain + NWG;             // [NG * kEntSlots] a list slice landed
+  uint32_t* tmem_slot = (uint32_t*)(ent_full + C::NG * C::kEntSlots);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  int* o_done = (int*)(tmem_slot + 2);          // [NWG] last item whose O the group has seen
+  int* run_last = o_done + NWG;                 // [NKV] last item of the slot's current run
   int4* ring = (int4*)(smem + C::kRingOff);
-  int* gen_ring = (int*)(smem + C::kGenOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int w_load = 4 * NWG, w_mma = 4 * NWG + C::kLoaderWarps;
+  const int w_load = 4 * NWG;
   const Shape s = prm.s;
   const uint32_t total = *prm.total_items;
   const uint32_t G = gridDim.x;
@@ -317,25 +378,26 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant
   if (threadIdx.x == 0) {
     for (int i = 0; i < NQ; ++i) {
       mbar_init(&q_full[i], C::kQFullCount);
-      mbar_init(&q_empty[i], 128);
+      mbar_init(&q_empty[i], C::kQEmptyCount);
     }
-    for (int i = 0; i < C::NKV; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
-    }
+    for (int i = 0; i < 2 * C::NKV; ++i) mbar_init(&kv_full[i], 1);
     for (int g = 0; g < NWG; ++g) {
       mbar_init(&s_full[g], 1);
+      mbar_init(&s_free[g], 128);
       mbar_init(&p_full[g], 128);
       mbar_init(&o_full[g], 1);
-      mbar_init(&o_free[g], 128);
+      mbar_init(&drain[g], 2);   // one commit from each issuing warp
+      o_done[g] = g - NWG;
     }
-    mbar_init(drain, 1);
+    for (int i = 0; i < C::NG * C::kEntSlots; ++i) mbar_init(&ent_full[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == w_load && lane == 0) {
+    prefetch_tensormap(&tmap_q);
     prefetch_tensormap(&tmap_k);
     prefetch_tensormap(&tmap_v);
+    prefetch_tensormap(&tmap_o);
   }
   if (warp == 0) tmem_alloc(tmem_slot, C::kTmemCols);
   tc_fence_before();
@@ -349,190 +411,287 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant
   auto meta = [&](int st) { return (int32_t*)(smem + C::kMetaOff + st * C::kMetaBytes); };
   const float sc = s.scale * kLog2e;
 
-  if (warp >= w_load && warp < w_mma) {
-    // ------------------------------------------------------------ Q loaders (+ K/V TMA)
-    // Loader L handles rows r = i*3*RPI + L*RPI + lane/CPR: CPR = HD/8 lanes
-    // per row, RPI = 32/CPR whole rows per instruction.  Each warp keeps its
-    // own ring of the next work items, refilled half a ring at a time.
-    constexpr int CPR = HD / 8, RPI = 32 / CPR, NLW = C::kLoaderWarps;
-    constexpr int ROWS = (kTileRows + NLW * RPI - 1) / (NLW * RPI);   // rows per lane
+  if (warp >= w_load) {
+    // ------------------------------------------------------------ loaders
+    // Each loader warp keeps its own ring of the work items, refilled half a
+    // ring at a time once it is within a few items of the filled end.
+    constexpr int H = C::kRing / 2;
     const int L = warp - w_load;
-    const int chunk = lane % CPR, panel = chunk >> 3, cc = chunk & 7;
     int4* my_ring = ring + L * C::kRing;
-    auto fill = [&](int base, int count) {   // items base .. base + count - 1
+    int filled = 0;                          // items [filled - kRing, filled) are in the ring
+    auto fill = [&](int count) {
       for (int q = lane; q < count; q += 32)
-        if (base + q < T) my_ring[(base + q) % C::kRing] = prm.items[t_begin + base + q];
+        if (filled + q < T) my_ring[(filled + q) % C::kRing] = prm.items[t_begin + filled + q];
+      filled += count;
       __syncwarp();
     };
-    auto row_of = [&](int i) { return i * NLW * RPI + L * RPI + lane / CPR; };
-    struct Ent { int32_t e[ROWS]; };
-    auto entries = [&](int t, Ent& E) {
-      if (t >= T) return;
-      const int4 it = my_ring[t % C::kRing];
-#pragma unroll
-      for (int i = 0; i < ROWS; ++i) {
-        const int r = row_of(i);
-        E.e[i] = (r < kTileRows) ? prm.lists[it.z + (r < it.w ? r : 0)] : 0;
-      }
-    };
-    fill(0, C::kRing);
-    Ent E0, E1;
-    entries(0, E0);
-    entries(1, E1);
-    int gen = -1, px = -1, py = -1;   // K/V runs (first loader, lane 0)
-    auto step = [&](int t, Ent& E) -> bool {
-      const int st = t % NQ, use = t / NQ;
-      const int4 it = my_ring[t % C::kRing];
-      int32_t e[ROWS];
-#pragma unroll
-      for (int i = 0; i < ROWS; ++i) e[i] = E.e[i];
-      if (use >= 1) {
-        bool ok = mbar_wait(&q_empty[st], (use - 1) & 1, prm.err, kErrWaitFree);
+    fill(C::kRing);
+    if (L < C::NG) {
+      // ---------------------------------------------------------- gather warp
+      constexpr int NG = C::NG, ES = C::kEntSlots;
+      const uint64_t pol_q = policy_evict_last();   // rows are gathered ~top_k times each
+      auto ent_buf = [&](int es) {
+        return (int32_t*)(smem + C::kEntOff + (L * ES + es) * C::kEntBytes);
+      };
+      // Lane 0: the list slice of the warp's k-th item (t = L + k * NG) into
+      // ring slot k % ES.  Reading up to 3 entries before the item's first
+      // keeps the copy 16-byte aligned; the lists end with enough slack.
+      auto fetch_entries = [&](int k) {
+        const int t = L + k * NG;
+        if (t >= T) return;
+        const int4 it = my_ring[t % C::kRing];
+        uint64_t* bar = &ent_full[L * ES + k % ES];
+        mbar_arrive_expect_tx(bar, C::kEntBytes);
+        bulk_copy_g2s(ent_buf(k % ES), prm.lists + (it.z & ~3), C::kEntBytes, bar);
+      };
+      if (lane == 0)
+        for (int k = 0; k < ES - 1; ++k) fetch_entries(k);
+      int k = 0;
+      for (int t = L; t < T; t += NG, ++k) {
+        if (t + 2 * ES * NG >= filled) fill(H);
+        const int st = t % NQ, use = t / NQ;
+        if (use >= 1) {
+          bool ok = mbar_wait(&q_empty[st], (use - 1) & 1, prm.err, kErrWaitFree);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok || *abort_flag) { *abort_flag = 1; break; }
+        }
+        if (lane == 0) fetch_entries(k + ES - 1);   // its slot's previous slice is consumed
+        bool ok = mbar_wait(&ent_full[L * ES + k % ES], (k / ES) & 1, prm.err, kErrWaitEnt);
         ok = __all_sync(0xffffffffu, ok);
-        if (!ok || *abort_flag) { *abort_flag = 1; return false; }
-      }
-      // Rows past the item's count gather its first query again (never stored).
-      int32_t* m = meta(st);
-      const unsigned char* qbase = reinterpret_cast<const unsigned char*>(prm.q) +
-                                   (int64_t)it.x * s.N * (HD * 2) + chunk * 16;
+        if (!ok || *abort_flag) { *abort_flag = 1; break; }
+        const int4 it = my_ring[t % C::kRing];
+        // Lane l takes tile rows 4l .. 4l + 3; rows past the item's count
+        // repeat its first query (their results are never read).
+        const int32_t* ent = ent_buf(k % ES) + (it.z & 3);
+        int32_t rr[4];
 #pragma unroll
-      for (int i = 0; i < ROWS; ++i) {
-        const int r = row_of(i);
-        if (r < kTileRows) {
-          if (chunk == 0) m[r] = e[i];
-          cp_async16(q_s(st) + panel * (kTileRows * 128) + r * 128 + ((cc ^ (r & 7)) << 4),
-                     qbase + (int64_t)(e[i] >> 6) * (HD * 2));
+        for (int j = 0; j < 4; ++j) {
+          const int r = 4 * lane + j;
+          rr[j] = ent[r < it.w ? r : 0];
+        }
+        int32_t* m = meta(st);
+        reinterpret_cast<int4*>(m)[lane] = make_int4(rr[0], rr[1], rr[2], rr[3]);
+        // The slice has been read; the async proxy may overwrite it next.
+        fence_proxy_async_smem();
+        const int ngroups = (it.w + 3) >> 2;   // 4-row groups holding valid rows
+        __syncwarp();
+        if (lane == 0)
+          mbar_arrive_expect_tx(&q_full[st], (uint32_t)ngroups * 512u * (HD / 64));
+        if (lane < ngroups) {
+          const int32_t y0 = it.x * s.N;
+#pragma unroll
+          for (int p = 0; p < HD / 64; ++p)
+            tma_gather4_hint(q_s(st) + p * (kTileRows * 128) + lane * 512, &tmap_q, &q_full[st],
+                             p * 64, y0 + rr[0], y0 + rr[1], y0 + rr[2], y0 + rr[3], pol_q);
         }
       }
-      if (L == 0 && lane == 0) reinterpret_cast<int4*>(m + kTileRows)[0] = it;
-      cp_async_arrive_noinc(&q_full[st]);   // this lane's rows landed
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&q_full[st]);  // this warp's entries (and the item) visible
-      // K and V of a new block run, into slot run % NKV once that slot's
-      // previous run is done.
-      if (L == 0 && lane == 0 && (it.x != px || it.y != py)) {
-        px = it.x;
-        py = it.y;
-        ++gen;
-        const int slot = gen % C::NKV, kuse = gen / C::NKV;
-        if (kuse >= 1 && (!mbar_wait(&kv_empty[slot], (kuse - 1) & 1, prm.err, kErrWaitFree) ||
-                          *abort_flag)) {
-          *abort_flag = 1;
-        } else {
-          mbar_arrive_expect_tx(&kv_full[slot], C::kKVBytes);
-          const int32_t y = it.x * s.N + it.y * BS;
+    } else {
+      // ---------------------------------------------------------- K/V warp
+      const uint64_t pol_kv = policy_evict_first();   // a block's K, V are read once per run
+      int gen = -1, px = -1, py = -1;
+      // Every group has seen the O of all its items <= tl (bounded wait).
+      auto wait_o_done = [&](int tl) -> bool {
+        uint64_t t0 = 0;
+        for (uint32_t i = 0;; ++i) {
+          bool all = true;
 #pragma unroll
-          for (int p = 0; p < HD / 64; ++p) {
-            tma_load_2d(k_s(slot) + p * (BS * 128), &tmap_k, &kv_full[slot], p * 64, y);
-            tma_load_2d(v_s(slot) + p * (BS * 128), &tmap_v, &kv_full[slot], p * 64, y);
+          for (int w = 0; w < NWG; ++w) all = all && ld_acquire_shared(&o_done[w]) + NWG > tl;
+          if (all) return true;
+          if (*abort_flag) return false;
+          __nanosleep(64);
+          if ((i & 255) == 0) {
+            if (i == 0) {
+              t0 = globaltimer();
+            } else if (globaltimer() - t0 > kWaitLimitNs) {
+              atomicOr(prm.err, kErrWaitFree);
+              return false;
+            }
           }
         }
-      }
-      __syncwarp();
-      if (*abort_flag) return false;
-      // Entering a new half ring: the half before it is done, so refill that
-      // half with the items one ring ahead.  Then load item t + 2's entries.
-      constexpr int H = C::kRing / 2;
-      if (t % H == H - 1) fill(t + 1 + H, H);
-      entries(t + 2, E);
-      return true;
-    };
-    for (int t = 0; t < T; t += 2) {
-      if (!step(t, E0)) break;
-      if (t + 1 < T && !step(t + 1, E1)) break;
-    }
-  } else if (warp == w_mma) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_bf16_f32(kTileRows, BS, false);
-      constexpr uint32_t idesc_o = idesc_bf16_f32(kTileRows, HD, true);
-      // Descriptors at stage / slot 0; the start-address field (bits 0-13,
-      // address >> 4) is advanced by adding byte offsets >> 4.
-      const uint64_t dq0 = smem_desc_sw128(smem_u32(q_s(0)), 16, 1024);
-      const uint64_t dk0 = smem_desc_sw128(smem_u32(k_s(0)), 16, 1024);
-      const uint64_t dv0 = smem_desc_sw128(smem_u32(v_s(0)), BS * 128, 1024);
-      int gen = -1, px = -1, py = -1;
-      auto issue_s = [&](int t) -> bool {
-        const int st = t % NQ;
-        if (!mbar_wait(&q_full[st], (t / NQ) & 1, prm.err, kErrWaitQ)) return false;
-        const int4 it = reinterpret_cast<const int4*>(meta(st) + kTileRows)[0];
-        if (it.x != px || it.y != py) {
-          ++gen;
-          px = it.x;
-          py = it.y;
-        }
-        gen_ring[t % C::kGenRing] = gen;
-        const int slot = gen % C::NKV;
-        if (!mbar_wait(&kv_full[slot], (gen / C::NKV) & 1, prm.err, kErrWaitQ)) return false;
-        tc_fence_after();
-        const uint32_t d = tbase + (t % NWG) * (BS + HD);
-        const uint64_t dq = dq0 + ((st * C::kQBytes) >> 4);
-        const uint64_t dk = dk0 + ((slot * C::kKVBytes) >> 4);
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (kTileRows * 128) + (kk & 3) * 32;
-          const uint32_t offk = (kk >> 2) * (BS * 128) + (kk & 3) * 32;
-          mma_bf16(d, dq + (off >> 4), dk + (offk >> 4), idesc_s, kk > 0);
-        }
-        mma_commit(&s_full[t % NWG]);
-        return true;
       };
-      auto issue_o = [&](int t) -> bool {
-        const int w = t % NWG, n = t / NWG;
-        if (!mbar_wait(&p_full[w], n & 1, prm.err, kErrWaitP)) return false;
-        if (n >= 1 && !mbar_wait(&o_free[w], (n - 1) & 1, prm.err, kErrWaitFree)) return false;
-        tc_fence_after();
-        const int g = gen_ring[t % C::kGenRing];
-        const int slot = g % C::NKV;
-        const uint32_t d = tbase + w * (BS + HD) + BS;
-        const uint32_t pa = tbase + w * (BS + HD);   // P: bf16 pairs over S's first BS/2 columns
-        const uint64_t dv = dv0 + ((slot * C::kKVBytes) >> 4);
+      for (int t = 0; t < T; ++t) {
+        if (t + 8 >= filled) fill(H);
+        const int st = t % NQ, use = t / NQ;
+        if (use >= 1) {
+          bool ok = mbar_wait(&q_empty[st], (use - 1) & 1, prm.err, kErrWaitFree);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok || *abort_flag) { *abort_flag = 1; break; }
+        }
+        if (lane == 0) {
+          const int4 it = my_ring[t % C::kRing];
+          bool new_run = false;
+          if (it.x != px || it.y != py) {
+            px = it.x;
+            py = it.y;
+            ++gen;
+            new_run = true;
+          }
+          const int slot = gen % C::NKV, kb = gen % (2 * C::NKV);
+          int32_t* m = meta(st);
+          reinterpret_cast<int4*>(m + kTileRows)[0] = it;
+          m[kMetaKv] = slot | (kb << 8) | (((gen / (2 * C::NKV)) & 1) << 16);
+          mbar_arrive(&q_full[st]);
+          if (new_run) {
+            // K and V into the run's slot once the slot's previous run is done.
+            if (gen >= C::NKV && !wait_o_done(run_last[slot])) {
+              *abort_flag = 1;
+            } else {
+              mbar_arrive_expect_tx(&kv_full[kb], C::kKVBytes);
+              const int32_t y = it.x * s.N + it.y * BS;
 #pragma unroll
-        for (int kk = 0; kk < BS / 16; ++kk)
-          mma_bf16_ts(d, pa + kk * 8, dv + ((kk * 16 * 128) >> 4), idesc_o, kk > 0);
-        mma_commit(&o_full[w]);
-        // The run's last item frees its K/V slot.  S(t + 1) is already
-        // issued (NWG >= 2), so its run id is known.
-        if (t + 1 == T || gen_ring[(t + 1) % C::kGenRing] != g) mma_commit(&kv_empty[slot]);
-        return true;
-      };
-      bool ok = true;
-      for (int t = 0; ok && t < NWG && t < T; ++t) ok = issue_s(t);
-      for (int t = 0; ok && t < T; ++t) {
-        ok = issue_o(t);
-        if (ok && t + NWG < T) ok = issue_s(t + NWG);
-        if (*abort_flag) ok = false;
+              for (int p = 0; p < HD / 64; ++p) {
+                tma_load_2d_hint(k_s(slot) + p * (BS * 128), &tmap_k, &kv_full[kb], p * 64, y,
+                                 pol_kv);
+                tma_load_2d_hint(v_s(slot) + p * (BS * 128), &tmap_v, &kv_full[kb], p * 64, y,
+                                 pol_kv);
+              }
+            }
+          }
+          run_last[slot] = t;
+        }
+        __syncwarp();
+        if (*abort_flag) break;
       }
-      if (!ok) *abort_flag = 1;
-      // Make sure no MMA is in flight when TMEM is released.
-      mma_commit(drain);
-      mbar_wait(drain, 0, prm.err, kErrWaitDrain);
     }
-    __syncwarp();
-  } else if (warp < 4 * NWG) {
-    // ------------------------------------------------------------ softmax / epilogue
+  } else {
+    // ------------------------------------------------------------ softmax / MMA / epilogue
+    // Per item t (the group's n-th): S(t) -> registers, releasing the S
+    // columns for S(t + NWG); P(t) into the P columns once PV(t - NWG) is
+    // done; the epilogue of item t - NWG; then PV(t).  PV(t) runs while the
+    // group works on item t + NWG, so its latency is off the group's path.
     const int wg = warp >> 2;              // takes items t with t % NWG == wg
     const int quad = warp & 3;             // TMEM lane quadrant
+    const bool issuer = (quad == 0);       // this warp issues the group's PV MMAs
+    const bool s_issuer = (quad == 2);     // this warp issues the group's S MMAs
+    const bool storer = (quad == 1);       // this warp publishes the group's O progress
     const int r = quad * 32 + lane;        // row of the tile this thread owns
+    const uint32_t s_col = tbase + wg * C::kGroupCols;   // S (fp32), TMEM lane 0
+    const uint32_t p_col = s_col + BS;                   // P (bf16 pairs)
+    const uint32_t o_col = p_col + BS / 2;               // O (fp32)
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t s_addr = tbase + lane_off + wg * (BS + HD);
-    const uint32_t o_addr = s_addr + BS;
-    for (int t = wg; t < T; t += NWG) {
-      const int n = t / NWG, st = t % NQ;
+    const uint32_t s_addr = s_col + lane_off;
+    const uint32_t p_addr = p_col + lane_off;
+    const uint32_t o_addr = o_col + lane_off;
+    const uint64_t pol_o = policy_evict_first();   // partials are read once, much later
+    constexpr uint32_t idesc_s = idesc_bf16_f32(kTileRows, BS, false);
+    constexpr uint32_t idesc_o = idesc_bf16_f32(kTileRows, HD, true);
+    // Descriptors at stage / slot 0; the start-address field (bits 0-13,
+    // address >> 4) is advanced by adding byte offsets >> 4.
+    const uint64_t dq0 = smem_desc_sw128(smem_u32(q_s(0)), 16, 1024);
+    const uint64_t dk0 = smem_desc_sw128(smem_u32(k_s(0)), 16, 1024);
+    const uint64_t dv0 = smem_desc_sw128(smem_u32(v_s(0)), BS * 128, 1024);
+    unsigned char* out = smem + C::kOutOff + wg * C::kOutBytes;
+
+    // Lane 0 of the issuer warp: S(t) = Q K^T into the S columns.
+    auto mma_s = [&](int t, int kv) {
+      const int st = t % NQ;
+      const uint64_t dq = dq0 + ((st * C::kQBytes) >> 4);
+      const uint64_t dk = dk0 + (((kv & 0xff) * C::kKVBytes) >> 4);
+#pragma unroll
+      for (int kk = 0; kk < HD / 16; ++kk) {
+        const uint32_t off = (kk >> 2) * (kTileRows * 128) + (kk & 3) * 32;
+        const uint32_t offk = (kk >> 2) * (BS * 128) + (kk & 3) * 32;
+        mma_bf16(s_col, dq + (off >> 4), dk + (offk >> 4), idesc_s, kk > 0);
+      }
+      mma_commit(&s_full[wg]);
+    };
+    // Issuer warp: issue S(t) once its queries and K/V have landed (bounded wait).
+    auto issue_s = [&](int t) -> bool {
+      const int st = t % NQ;
       bool ok = mbar_wait(&q_full[st], (t / NQ) & 1, prm.err, kErrWaitQ);
+      int kv = 0;
+      if (ok) {
+        kv = meta(st)[kMetaKv];
+        ok = mbar_wait(&kv_full[(kv >> 8) & 0xff], (kv >> 16) & 1, prm.err, kErrWaitKV);
+      }
       ok = __all_sync(0xffffffffu, ok);
-      if (!ok || *abort_flag) { *abort_flag = 1; break; }
+      if (ok) {
+        tc_fence_after();
+        if (lane == 0) mma_s(t, kv);
+        __syncwarp();
+      }
+      return ok;
+    };
+    // Issuer warp: issue S(t) only if its queries and K/V have already landed.
+    auto try_issue_s = [&](int t) -> bool {
+      const int st = t % NQ;
+      bool ready = mbar_test(&q_full[st], (t / NQ) & 1);
+      int kv = 0;
+      if (ready) {
+        kv = meta(st)[kMetaKv];
+        ready = mbar_test(&kv_full[(kv >> 8) & 0xff], (kv >> 16) & 1);
+      }
+      ready = __all_sync(0xffffffffu, ready);
+      if (ready) {
+        tc_fence_after();
+        if (lane == 0) mma_s(t, kv);
+        __syncwarp();
+      }
+      return ready;
+    };
+    // Epilogue of item tp, the group's np-th, whose O is complete: O (not
+    // yet divided by l; the combine folds 1 / l into its weights) as bf16
+    // into this warp's 32 rows of the group's output tile (row r,
+    // 16-byte chunk c at the 128-byte swizzled place the TMA store expects),
+    // (m, l) per row, and the warp's own TMA store of its rows.  Each warp
+    // only waits for its own previous store to have read its rows.
+    auto epilogue = [&](int tp, int np, float mp, float lp) {
+      if (np >= 1 && lane == 0) bulk_wait_group_read0();
+      __syncwarp();
+#pragma unroll
+      for (int c0 = 0; c0 < HD; c0 += 64) {
+        float ov[64];
+        tmem_ld64(o_addr + c0, ov);
+#pragma unroll
+        for (int c = 0; c < 64; c += 8) {
+          const int ch = c >> 3;
+          *reinterpret_cast<uint4*>(out + (c0 >> 6) * (kTileRows * 128) + r * 128 +
+                                    ((ch ^ (r & 7)) << 4)) =
+              make_uint4(pack_bf16x2(ov[c], ov[c + 1]), pack_bf16x2(ov[c + 2], ov[c + 3]),
+                         pack_bf16x2(ov[c + 4], ov[c + 5]), pack_bf16x2(ov[c + 6], ov[c + 7]));
+        }
+      }
+      // Work item gi owns partial rows [128 gi, 128 gi + 128); rows past the
+      // item's count hold values that are never read.
+      const int gi = (int)t_begin + tp;
+      __stcs(prm.part_ml + (int64_t)gi * kTileRows + r, make_float2(mp, lp));
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+#pragma unroll
+        for (int p = 0; p < HD / 64; ++p)
+          tma_store_2d_hint(&tmap_o, out + p * (kTileRows * 128) + quad * 32 * 128, p * 64,
+                            gi * kTileRows + quad * 32, pol_o);
+        bulk_commit_group();
+      }
+    };
+    // O(t) complete means every MMA this group issued before it (S(t),
+    // PV(t) and all earlier items') is done reading its K/V slot.
+    auto publish_o_done = [&](int t) {
+      if (lane == 0) st_release_shared(&o_done[wg], t);
+    };
+
+    if (s_issuer && wg < T && !issue_s(wg)) *abort_flag = 1;
+    int n = 0, tp = -1;
+    float mp = 0.f, lp = 1.f;   // the previous item's row max (scaled) and sum
+    bool ok = true;
+    for (int t = wg; t < T; t += NWG, ++n) {
+      const int st = t % NQ;
+      ok = mbar_wait(&q_full[st], (t / NQ) & 1, prm.err, kErrWaitQ);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || *abort_flag) { ok = false; break; }
       const int32_t* m = meta(st);
-      const int4 it = reinterpret_cast<const int4*>(m + kTileRows)[0];
-      const int u = it.x, j = it.y, cnt = it.w;
-      const bool valid = r < cnt;
-      const int32_t e = m[r];
-      const int qrow = e >> 6, slot = e & 63;
+      const int j = reinterpret_cast<const int4*>(m + kTileRows)[0].y;
+      const int kv = m[kMetaKv];
+      const int qrow = m[r];   // rows past the item's count repeat its first query
 
       ok = mbar_wait(&s_full[wg], n & 1, prm.err, kErrWaitS);
       ok = __all_sync(0xffffffffu, ok);
-      if (!ok || *abort_flag) { *abort_flag = 1; break; }
+      if (!ok || *abort_flag) { ok = false; break; }
       tc_fence_after();
+      // S(t) is done, so its query rows are dead; every lane has read the
+      // stage's entries and K/V word above: hand the stage back.
+      if (lane == 0) mbar_arrive(&q_empty[st]);
       const int key0 = j * BS;
       const bool diag = s.causal && key0 + BS - 1 > qrow;
       float sv[64];
@@ -557,8 +716,20 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant
         }
         mx = fmaxf(mx, fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)));
       }
+      if (BS == 64) {   // S(t) is all in registers: its columns are free
+        tc_fence_before();
+        mbar_arrive(&s_free[wg]);
+      }
       // Padding rows of a short item can be fully masked; keep them finite.
       const float msc = (mx == -INFINITY) ? 0.f : mx * sc;
+      if (n >= 1) {
+        // PV(t - NWG) done: the P columns are free and O(t - NWG) is final.
+        ok = mbar_wait(&o_full[wg], (n - 1) & 1, prm.err, kErrWaitO);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok || *abort_flag) { ok = false; break; }
+        tc_fence_after();
+        if (storer) publish_o_done(tp);
+      }
       float l0 = 0.f, l1 = 0.f;
 #pragma unroll
       for (int c0 = 0; c0 < BS; c0 += 64) {
@@ -572,62 +743,75 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant
           l1 += p1;
           pk[c >> 1] = pack_bf16x2(p0, p1);
         }
-        // P (bf16 pairs) overwrites the S columns this chunk has consumed.
-        tmem_st32(s_addr + (c0 >> 1), pk);
+        tmem_st32(p_addr + (c0 >> 1), pk);
+      }
+      if (BS > 64) {
+        tc_fence_before();
+        mbar_arrive(&s_free[wg]);
       }
       const float l = l0 + l1;
-      tc_fence_before();
+      bool issued_next = false;
+      if (s_issuer && t + NWG < T) {
+        // Every row of S(t) has been read: S(t + NWG) may go into its columns
+        // now, if its queries and K/V are already there.  (S and PV use
+        // disjoint TMEM columns and operands, so they may come from two
+        // threads.)
+        ok = mbar_wait(&s_free[wg], n & 1, prm.err, kErrWaitS);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) { *abort_flag = 1; break; }
+        issued_next = try_issue_s(t + NWG);
+      }
+      if (n >= 1) epilogue(tp, n - 1, mp, lp);
+      tc_fence_before();   // P(t) stored, O(t - NWG) read out
       mbar_arrive(&p_full[wg]);
-
-      ok = mbar_wait(&o_full[wg], n & 1, prm.err, kErrWaitO);
+      if (issuer) {
+        ok = mbar_wait(&p_full[wg], n & 1, prm.err, kErrWaitP);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) { *abort_flag = 1; break; }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint64_t dv = dv0 + (((kv & 0xff) * C::kKVBytes) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < BS / 16; ++kk)
+            mma_bf16_ts(o_col, p_col + kk * 8, dv + ((kk * 16 * 128) >> 4), idesc_o, kk > 0);
+          mma_commit(&o_full[wg]);
+        }
+        __syncwarp();
+      }
+      if (s_issuer) {
+        if (t + NWG < T && !issued_next) {
+          // The next item's S has to wait for its queries or K/V.  The K/V
+          // load may itself wait for this group's progress, so publish O(t)
+          // first: it depends on nothing but PV(t).
+          ok = mbar_wait(&o_full[wg], n & 1, prm.err, kErrWaitO);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) { *abort_flag = 1; break; }
+          publish_o_done(t);
+          if (!issue_s(t + NWG)) { ok = false; *abort_flag = 1; break; }
+        }
+      }
+      tp = t;
+      mp = msc;
+      lp = l;
+    }
+    if (!ok) *abort_flag = 1;
+    if (ok && tp >= 0) {
+      // The group's last item.
+      ok = mbar_wait(&o_full[wg], (n - 1) & 1, prm.err, kErrWaitO);
       ok = __all_sync(0xffffffffu, ok);
-      if (!ok || *abort_flag) { *abort_flag = 1; break; }
-      tc_fence_after();
-      const float inv = 1.f / l;
-      // The item's query rows are consumed (S(t) is done), so its stage holds
-      // the output rows for a coalesced store: row r, chunk c at the same
-      // swizzled place a gathered query chunk occupied.
-      unsigned char* stage = q_s(st);
-#pragma unroll
-      for (int c0 = 0; c0 < HD; c0 += 64) {
-        float ov[64];
-        tmem_ld64(o_addr + c0, ov);
-        if (c0 + 64 >= HD) {
-          tc_fence_before();
-          mbar_arrive(&o_free[wg]);
-        }
-#pragma unroll
-        for (int c = 0; c < 64; c += 8) {
-          const int ch = c >> 3;
-          *reinterpret_cast<uint4*>(stage + (c0 >> 6) * (kTileRows * 128) + r * 128 +
-                                    ((ch ^ (r & 7)) << 4)) =
-              make_uint4(pack_bf16x2(ov[c] * inv, ov[c + 1] * inv),
-                         pack_bf16x2(ov[c + 2] * inv, ov[c + 3] * inv),
-                         pack_bf16x2(ov[c + 4] * inv, ov[c + 5] * inv),
-                         pack_bf16x2(ov[c + 6] * inv, ov[c + 7] * inv));
-        }
+      if (ok) {
+        tc_fence_after();
+        if (storer) publish_o_done(tp);
+        epilogue(tp, n - 1, mp, lp);
       }
-      const int64_t pe = ((int64_t)u * s.N + qrow) * s.k + slot;
-      if (valid) prm.part_ml[pe] = make_float2(msc, l);
+      if (!ok) *abort_flag = 1;
+    }
+    if (lane == 0) bulk_wait_group0();   // this warp's tile stores complete
+    if (issuer || s_issuer) {
+      // No MMA of this group in flight when TMEM is released.
+      if (lane == 0) mma_commit(&drain[wg]);
       __syncwarp();
-      {
-        // This warp's 32 rows, 32 / CPR whole rows per instruction.
-        constexpr int CPR = HD / 8, RPI = 32 / CPR;
-        const int chunk = lane % CPR, panel = chunk >> 3, cc = chunk & 7;
-#pragma unroll 4
-        for (int i = 0; i < 32 / RPI; ++i) {
-          const int rr = quad * 32 + i * RPI + lane / CPR;
-          if (rr < cnt) {
-            const int32_t er = m[rr];
-            const int64_t pr = ((int64_t)u * s.N + (er >> 6)) * s.k + (er & 63);
-            const uint4 v = *reinterpret_cast<const uint4*>(
-                stage + panel * (kTileRows * 128) + rr * 128 + ((cc ^ (rr & 7)) << 4));
-            reinterpret_cast<uint4*>(prm.part_o + pr * HD)[chunk] = v;
-          }
-        }
-      }
-      __syncwarp();
-      mbar_arrive(&q_empty[st]);   // this thread is done with the stage
+      mbar_wait(&drain[wg], 0, prm.err, kErrWaitDrain);
     }
   }
   tc_fence_before();
@@ -636,37 +820,42 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant
   if (warp == 0) tmem_dealloc(tbase, C::kTmemCols);
 }
 
-// 5. Per query: merge its partials (m in the base-2 domain, l, O / l).
+// 5. Per query: merge its partials (m in the base-2 domain, l, and O = sum of
+//    2^(s - m) v, not divided by l), found through the (query, slot) ->
+//    partial row map.
 template <int HD>
 __global__ void __launch_bounds__(256)
-combine_kernel(const int32_t* __restrict__ idx, const __nv_bfloat16* __restrict__ part_o,
-               const float2* __restrict__ part_ml, __nv_bfloat16* __restrict__ O, Shape s) {
+combine_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ inv,
+               const __nv_bfloat16* __restrict__ part_o, const float2* __restrict__ part_ml,
+               __nv_bfloat16* __restrict__ O, Shape s) {
   constexpr int CH = HD / 8;  // 16-byte chunks per row
   const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t R = gid / CH;  // global query row (unit * N + row)
   const int c = (int)(gid % CH);
   if (R >= (int64_t)s.units * s.N) return;
   const int32_t* sel = idx + R * s.k;
+  const int32_t* prow = inv + R * s.k;
   float M = -INFINITY;
   for (int q = 0; q < s.k; ++q)
-    if (__ldg(sel + q) >= 0) M = fmaxf(M, __ldg(&part_ml[R * s.k + q].x));
+    if (__ldg(sel + q) >= 0) M = fmaxf(M, __ldcs(&part_ml[__ldg(prow + q)].x));
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float L = 0.f;
   for (int q = 0; q < s.k; ++q) {
     if (__ldg(sel + q) < 0) continue;
-    const float2 ml = __ldg(&part_ml[R * s.k + q]);
-    const float w = ml.y * fast_exp2(ml.x - M);
-    L += w;
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(part_o + (R * s.k + q) * HD) + c);
+    const int64_t pr = __ldg(prow + q);
+    const float2 ml = __ldcs(&part_ml[pr]);
+    const float w = fast_exp2(ml.x - M);
+    L = fmaf(ml.y, w, L);
+    const uint4 v = __ldcs(reinterpret_cast<const uint4*>(part_o + pr * HD) + c);
     acc[0] = fmaf(w, bf16_lo(v.x), acc[0]); acc[1] = fmaf(w, bf16_hi(v.x), acc[1]);
     acc[2] = fmaf(w, bf16_lo(v.y), acc[2]); acc[3] = fmaf(w, bf16_hi(v.y), acc[3]);
     acc[4] = fmaf(w, bf16_lo(v.z), acc[4]); acc[5] = fmaf(w, bf16_hi(v.z), acc[5]);
     acc[6] = fmaf(w, bf16_lo(v.w), acc[6]); acc[7] = fmaf(w, bf16_hi(v.w), acc[7]);
   }
-  const float inv = 1.f / L;
+  const float rl = 1.f / L;
   reinterpret_cast<uint4*>(O + R * HD)[c] =
-      make_uint4(pack_bf16x2(acc[0] * inv, acc[1] * inv), pack_bf16x2(acc[2] * inv, acc[3] * inv),
-                 pack_bf16x2(acc[4] * inv, acc[5] * inv), pack_bf16x2(acc[6] * inv, acc[7] * inv));
+      make_uint4(pack_bf16x2(acc[0] * rl, acc[1] * rl), pack_bf16x2(acc[2] * rl, acc[3] * rl),
+                 pack_bf16x2(acc[4] * rl, acc[5] * rl), pack_bf16x2(acc[6] * rl, acc[7] * rl));
 }
 
 // ---------------------------------------------------------------------------
@@ -718,21 +907,22 @@ static cudaError_t launch_kv_kernel(const __nv_bfloat16* Q, const __nv_bfloat16*
   using C = KvCfg<BS, HD>;
   CUtensorMap mk, mv;
   const uint64_t rows = (uint64_t)s.units * s.N;
-  if (!make_map(&mk, K, rows, HD, BS) || !make_map(&mv, V, rows, HD, BS))
+  CUtensorMap mq, mo;
+  if (!make_map(&mq, Q, rows, HD, 1) || !make_map(&mk, K, rows, HD, BS) ||
+      !make_map(&mv, V, rows, HD, BS) ||
+      !make_map(&mo, w.part_o, (uint64_t)w.part_rows, HD, 32))
     return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(fine_kv_kernel<BS, HD>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   if (e != cudaSuccess) return e;
   FineKvParams prm;
-  prm.q = Q;
   prm.items = w.items;
   prm.lists = w.lists;
   prm.total_items = w.err + 1;
-  prm.part_o = w.part_o;
   prm.part_ml = w.part_ml;
   prm.err = w.err;
   prm.s = s;
-  fine_kv_kernel<BS, HD><<<num_sms(), C::kThreads, C::kSmem, st>>>(mk, mv, prm);
+  fine_kv_kernel<BS, HD><<<num_sms(), C::kThreads, C::kSmem, st>>>(mq, mk, mv, mo, prm);
   return cudaGetLastError();
 }
 
@@ -756,9 +946,10 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                          (int)hist_smem);
   }
   bucket_count_kernel<<<bgrid, 256, hist_smem, st>>>(idx, w.counts, s);
-  bucket_scan_kernel<<<s.units, 1024, 0, st>>>(w.counts, w.offsets, w.items, w.err, s,
-                                               max_items_per_unit(s));
-  bucket_scatter_kernel<<<bgrid, 256, hist_smem, st>>>(idx, w.offsets, w.cursors, w.lists, s);
+  bucket_scan_kernel<<<s.units, 1024, 0, st>>>(w.counts, w.offsets, w.item_off, w.items, w.err,
+                                               s);
+  bucket_scatter_kernel<<<bgrid, 256, hist_smem, st>>>(idx, w.offsets, w.item_off, w.cursors,
+                                                       w.lists, w.inv, s);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   mark(2);
   if (s.bs == 64 && s.D == 64) e = launch_kv_kernel<64, 64>(Q, K, V, w, s, st);
@@ -769,8 +960,10 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
   mark(3);
   const int64_t threads = (int64_t)s.units * s.N * (s.D / 8);
   const unsigned blocks = (unsigned)((threads + 255) / 256);
-  if (s.D == 64) combine_kernel<64><<<blocks, 256, 0, st>>>(idx, w.part_o, w.part_ml, O, s);
-  else combine_kernel<128><<<blocks, 256, 0, st>>>(idx, w.part_o, w.part_ml, O, s);
+  if (s.D == 64)
+    combine_kernel<64><<<blocks, 256, 0, st>>>(idx, w.inv, w.part_o, w.part_ml, O, s);
+  else
+    combine_kernel<128><<<blocks, 256, 0, st>>>(idx, w.inv, w.part_o, w.part_ml, O, s);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   mark(4);
   *n_launches = 5;
