@@ -258,14 +258,16 @@ select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
 #pragma unroll
             for (int i = 0; i < 32; ++i) gm[i] = fmaxf(gm[i], x[i]);
           } else {
-            bool anyp = false;
+            // The chunk's candidates as a bit mask; the buffer compacts only
+            // if this row's own candidates would overflow it.
+            uint32_t pm = 0;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) anyp |= sel.passes(x[i]);
-            if (__any_sync(0xffffffffu, anyp)) {
-              sel.reserve(32);
+            for (int i = 0; i < 32; ++i) pm |= sel.passes(x[i]) ? (1u << i) : 0u;
+            if (pm) {
+              sel.reserve(__popc(pm));
 #pragma unroll
               for (int i = 0; i < 32; ++i)
-                if (sel.passes(x[i])) sel.append(x[i], j0 + i);
+                if ((pm >> i) & 1u) sel.append(x[i], j0 + i);
             }
           }
         }
