@@ -330,8 +330,9 @@ def run_ours(args, cfg):
                 "achieved": round(achieved, 2) if achieved else None, "peak": peak,
                 "unit": "TFLOP/s", "frac": round(achieved / peak, 4) if achieved else None,
                 "peak_source": f"{peak_kind} bf16_tflops (burst)",
-                "traffic": traffic, "flops_per_launch": fine_flops,
-                "launch_ms": round(fine_ms, 4)}
+                "traffic": traffic, "traffic_unit": "bytes per launch (ncu, profiles/)",
+                "traffic_gbs": round(traffic / (fine_ms * 1e-3) / 1e9, 1) if traffic and fine_ms > 0 else None,
+                "flops_per_launch": fine_flops, "launch_ms": round(fine_ms, 4)}
 
     if world > 1:
         dist.barrier()
