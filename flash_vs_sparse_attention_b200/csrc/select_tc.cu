@@ -258,11 +258,13 @@ select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
 #pragma unroll
             for (int i = 0; i < 32; ++i) gm[i] = fmaxf(gm[i], x[i]);
           } else {
-            // The chunk's candidates as a bit mask; the buffer compacts only
-            // if this row's own candidates would overflow it.
-            uint32_t pm = 0;
+            // The chunk's candidates as a bit mask (four independent 8-bit
+            // parts); the buffer compacts only if this row's own candidates
+            // would overflow it.
+            uint32_t pq[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-            for (int i = 0; i < 32; ++i) pm |= sel.passes(x[i]) ? (1u << i) : 0u;
+            for (int i = 0; i < 32; ++i) pq[i >> 3] |= sel.passes(x[i]) ? (1u << i) : 0u;
+            const uint32_t pm = (pq[0] | pq[1]) | (pq[2] | pq[3]);
             if (pm) {
               sel.reserve(__popc(pm));
 #pragma unroll

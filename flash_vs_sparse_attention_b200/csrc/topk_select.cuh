@@ -31,6 +31,7 @@ struct RowTopK {
   int k;
   float theta_excl;
   float theta_incl;
+  float thr;          // passes(x) <=> x >= thr: max(theta_incl, the float after theta_excl)
 
   __device__ __forceinline__ void init(uint2* b, int stride_, int cap_, int k_) {
     buf = b;
@@ -40,11 +41,16 @@ struct RowTopK {
     k = k_;
     theta_excl = -INFINITY;
     theta_incl = -INFINITY;
+    update_thr();
   }
 
-  __device__ __forceinline__ bool passes(float x) const {
-    return x > theta_excl && x >= theta_incl;
+  // x > theta_excl is x >= (the next float above theta_excl) for every
+  // non-NaN x (for theta_excl = -inf that is -FLT_MAX, so -inf never passes).
+  __device__ __forceinline__ void update_thr() {
+    thr = fmaxf(theta_incl, nextafterf(theta_excl, INFINITY));
   }
+
+  __device__ __forceinline__ bool passes(float x) const { return x >= thr; }
 
   // Append unconditionally (the caller checked passes()).
   __device__ __forceinline__ void append(float x, int32_t j) {
@@ -63,6 +69,7 @@ struct RowTopK {
 
   __device__ __forceinline__ void raise_floor(float lower_bound) {
     theta_incl = fmaxf(theta_incl, lower_bound);
+    update_thr();
   }
 
   // Exact k-th largest value of the buffer: a descending min/max insertion
@@ -112,6 +119,7 @@ struct RowTopK {
     }
     cnt = w;
     theta_excl = fmaxf(theta_excl, T);
+    update_thr();
   }
 
   // Final top-k, written as k int32 in ascending block order, -1 padded.
