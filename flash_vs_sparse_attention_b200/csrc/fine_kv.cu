@@ -195,7 +195,8 @@ bucket_scan_kernel(const int32_t* __restrict__ counts, int32_t* __restrict__ off
 __global__ void __launch_bounds__(256)
 bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ offsets,
                       const int32_t* __restrict__ item_off, int32_t* __restrict__ cursors,
-                      int32_t* __restrict__ lists, int32_t* __restrict__ inv, Shape s) {
+                      int32_t* __restrict__ lists, int32_t* __restrict__ inv, Shape s,
+                      float inv_k) {
   extern __shared__ int32_t hist[];
   const int u = blockIdx.y;
   for (int j = threadIdx.x; j < s.nb; j += blockDim.x) hist[j] = 0;
@@ -220,8 +221,11 @@ bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict
     if (j >= 0) {
       const int64_t g = (int64_t)u * s.nb + j;
       const int pos = atomicAdd(&hist[j], 1);   // position within block j's list
-      const int64_t le = row0 * s.k + e;        // entry index within the unit
-      ul[offsets[g] + pos] = (int)(le / s.k);
+      // e / k without an integer division: e < 1024 * 64, so the float
+      // product is within 2^-10 of e / k, while (e + 1/2) / k sits at least
+      // 1 / 128 away from an integer.
+      const int r = __float2int_rz(((float)e + 0.5f) * inv_k);
+      ul[offsets[g] + pos] = (int)row0 + r;
       inv[e0 + e] = item_off[g] * kTileRows + pos;
     }
   }
@@ -960,7 +964,7 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
   bucket_scan_kernel<<<s.units, 1024, 0, st>>>(w.counts, w.offsets, w.item_off, w.items, w.err,
                                                s);
   bucket_scatter_kernel<<<bgrid, 256, hist_smem, st>>>(idx, w.offsets, w.item_off, w.cursors,
-                                                       w.lists, w.inv, s);
+                                                       w.lists, w.inv, s, 1.0f / (float)s.k);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   mark(2);
   if (s.bs == 64 && s.D == 64) e = launch_kv_kernel<64, 64>(Q, K, V, w, s, st);
