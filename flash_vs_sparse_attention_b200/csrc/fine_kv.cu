@@ -837,40 +837,93 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
 
 // 5. Per query: merge its partials (m in the base-2 domain, l, and O = sum of
 //    2^(s - m) v, not divided by l), found through the (query, slot) ->
-//    partial row map.
-template <int HD>
+//    partial row map.  CH = HD / 8 threads per query row, one 16-byte chunk
+//    of the output each.  The row's slot metadata (selection, partial row,
+//    m, l) is loaded once, spread over the CH threads (slot q by thread
+//    q % CH) and shared by shuffles; every partial chunk load of the row is
+//    issued before the first is used, so a thread keeps up to KMAX loads in
+//    flight instead of a chain of dependent ones.
+template <int HD, int KMAX>
 __global__ void __launch_bounds__(256)
 combine_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ inv,
                const __nv_bfloat16* __restrict__ part_o, const float2* __restrict__ part_ml,
                __nv_bfloat16* __restrict__ O, Shape s) {
-  constexpr int CH = HD / 8;  // 16-byte chunks per row
+  constexpr int CH = HD / 8;           // threads per row (8 or 16), a power of two <= 32
+  constexpr int PER = (KMAX + CH - 1) / CH;   // slots whose metadata one thread loads
+  const int64_t rows = (int64_t)s.units * s.N;
   const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t R = gid / CH;  // global query row (unit * N + row)
   const int c = (int)(gid % CH);
-  if (R >= (int64_t)s.units * s.N) return;
+  const bool live = gid / CH < rows;
+  const int64_t R = live ? gid / CH : rows - 1;   // dead lanes mirror a real row
+  const int lane = threadIdx.x & 31, base = lane & ~(CH - 1);
   const int32_t* sel = idx + R * s.k;
   const int32_t* prow = inv + R * s.k;
-  float M = -INFINITY;
-  for (int q = 0; q < s.k; ++q)
-    if (__ldg(sel + q) >= 0) M = fmaxf(M, __ldcs(&part_ml[__ldg(prow + q)].x));
-  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  float L = 0.f;
-  for (int q = 0; q < s.k; ++q) {
-    if (__ldg(sel + q) < 0) continue;
-    const int64_t pr = __ldg(prow + q);
-    const float2 ml = __ldcs(&part_ml[pr]);
-    const float w = fast_exp2(ml.x - M);
-    L = fmaf(ml.y, w, L);
-    const uint4 v = __ldcs(reinterpret_cast<const uint4*>(part_o + pr * HD) + c);
-    acc[0] = fmaf(w, bf16_lo(v.x), acc[0]); acc[1] = fmaf(w, bf16_hi(v.x), acc[1]);
-    acc[2] = fmaf(w, bf16_lo(v.y), acc[2]); acc[3] = fmaf(w, bf16_hi(v.y), acc[3]);
-    acc[4] = fmaf(w, bf16_lo(v.z), acc[4]); acc[5] = fmaf(w, bf16_hi(v.z), acc[5]);
-    acc[6] = fmaf(w, bf16_lo(v.w), acc[6]); acc[7] = fmaf(w, bf16_hi(v.w), acc[7]);
+  int32_t pr[PER];
+  float m[PER], l[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int q = c + i * CH;
+    pr[i] = (q < s.k && __ldg(sel + q) >= 0) ? __ldg(prow + q) : -1;
   }
+  float M = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    float2 ml = make_float2(-INFINITY, 0.f);
+    if (pr[i] >= 0) ml = __ldcs(&part_ml[pr[i]]);
+    m[i] = ml.x;
+    l[i] = ml.y;
+    M = fmaxf(M, ml.x);
+  }
+#pragma unroll
+  for (int o = CH / 2; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float L = 0.f;
+  float w[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    w[i] = pr[i] >= 0 ? fast_exp2(m[i] - M) : 0.f;
+    L = fmaf(l[i], w[i], L);
+  }
+#pragma unroll
+  for (int o = CH / 2; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  // Every slot's partial row and weight, then its chunk of the partial row.
+  uint4 v[KMAX];
+  float wq[KMAX];
+#pragma unroll
+  for (int q = 0; q < KMAX; ++q) {
+    const int owner = base + (q % CH);
+    const int32_t p = __shfl_sync(0xffffffffu, pr[q / CH], owner);
+    wq[q] = __shfl_sync(0xffffffffu, w[q / CH], owner);
+    v[q] = (q < s.k && p >= 0)
+               ? __ldcs(reinterpret_cast<const uint4*>(part_o + (int64_t)p * HD) + c)
+               : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int q = 0; q < KMAX; ++q) {
+    const float wt = wq[q];
+    acc[0] = fmaf(wt, bf16_lo(v[q].x), acc[0]); acc[1] = fmaf(wt, bf16_hi(v[q].x), acc[1]);
+    acc[2] = fmaf(wt, bf16_lo(v[q].y), acc[2]); acc[3] = fmaf(wt, bf16_hi(v[q].y), acc[3]);
+    acc[4] = fmaf(wt, bf16_lo(v[q].z), acc[4]); acc[5] = fmaf(wt, bf16_hi(v[q].z), acc[5]);
+    acc[6] = fmaf(wt, bf16_lo(v[q].w), acc[6]); acc[7] = fmaf(wt, bf16_hi(v[q].w), acc[7]);
+  }
+  if (!live) return;
   const float rl = 1.f / L;
   reinterpret_cast<uint4*>(O + R * HD)[c] =
       make_uint4(pack_bf16x2(acc[0] * rl, acc[1] * rl), pack_bf16x2(acc[2] * rl, acc[3] * rl),
                  pack_bf16x2(acc[4] * rl, acc[5] * rl), pack_bf16x2(acc[6] * rl, acc[7] * rl));
+}
+
+template <int HD>
+static void launch_combine(const int32_t* idx, const FineWs& w, __nv_bfloat16* O, const Shape& s,
+                           cudaStream_t st) {
+  const int64_t threads = (int64_t)s.units * s.N * (HD / 8);
+  const unsigned blocks = (unsigned)((threads + 255) / 256);
+  if (s.k <= 16)
+    combine_kernel<HD, 16><<<blocks, 256, 0, st>>>(idx, w.inv, w.part_o, w.part_ml, O, s);
+  else if (s.k <= 32)
+    combine_kernel<HD, 32><<<blocks, 256, 0, st>>>(idx, w.inv, w.part_o, w.part_ml, O, s);
+  else
+    combine_kernel<HD, 64><<<blocks, 256, 0, st>>>(idx, w.inv, w.part_o, w.part_ml, O, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -973,12 +1026,8 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
   else e = cudaErrorNotSupported;
   if (e != cudaSuccess) return e;
   mark(3);
-  const int64_t threads = (int64_t)s.units * s.N * (s.D / 8);
-  const unsigned blocks = (unsigned)((threads + 255) / 256);
-  if (s.D == 64)
-    combine_kernel<64><<<blocks, 256, 0, st>>>(idx, w.inv, w.part_o, w.part_ml, O, s);
-  else
-    combine_kernel<128><<<blocks, 256, 0, st>>>(idx, w.inv, w.part_o, w.part_ml, O, s);
+  if (s.D == 64) launch_combine<64>(idx, w, O, s, st);
+  else launch_combine<128>(idx, w, O, s, st);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   mark(4);
   *n_launches = 5;
