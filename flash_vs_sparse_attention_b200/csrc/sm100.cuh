@@ -1,5 +1,5 @@
 // Thin wrappers over the sm_100a instructions the tensor-core kernels use:
-// mbarriers, TMA (tiled loads and 4-row gathers, no multicast), tcgen05 MMA
+// mbarriers, TMA (tiled loads, 4-row gathers, tiled stores; no cluster-wide copies), tcgen05 MMA
 // with fp32 accumulators in tensor memory, and tensor-memory loads.
 //
 // Every wait on an mbarrier is bounded: after ~kWaitLimitNs of spinning it
