@@ -736,10 +736,8 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
         tc_fence_after();
         if (storer) publish_o_done(tp);
       }
-      // p = 2^(s sc - m sc): pairs of columns share one f32x2 fma and one
-      // f32x2 add into the (even, odd) row sums.
-      const uint64_t sc2 = f2_pack(sc, sc), nm2 = f2_pack(-msc, -msc);
-      uint64_t l2 = f2_pack(0.f, 0.f);
+      // p = 2^(s sc - m sc), summed per row in (even, odd) column halves.
+      float l0 = 0.f, l1 = 0.f;
 #pragma unroll
       for (int c0 = 0; c0 < BS; c0 += 64) {
         if (BS > 64) load_s(c0);   // with one chunk the values are still in sv
@@ -748,18 +746,15 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
           uint32_t pk[16];
 #pragma unroll
           for (int c = 0; c < 32; c += 2) {
-            float x0, x1;
-            f2_unpack(f2_fma(f2_pack(sv[h + c], sv[h + c + 1]), sc2, nm2), x0, x1);
-            const float p0 = fast_exp2(x0);
-            const float p1 = fast_exp2(x1);
-            l2 = f2_add(l2, f2_pack(p0, p1));
+            const float p0 = fast_exp2(fmaf(sv[h + c], sc, -msc));
+            const float p1 = fast_exp2(fmaf(sv[h + c + 1], sc, -msc));
+            l0 += p0;
+            l1 += p1;
             pk[c >> 1] = pack_bf16x2(p0, p1);
           }
           tmem_st16(p_addr + ((c0 + h) >> 1), pk);
         }
       }
-      float l0, l1;
-      f2_unpack(l2, l0, l1);
       if (BS > 64) {
         tc_fence_before();
         mbar_arrive(&s_free[wg]);

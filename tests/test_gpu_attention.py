@@ -133,3 +133,52 @@ def test_flags_agree_on_config3_unit(cuda):
     b = bi.attention(Qg, Kg, Vg, causal=True, flags=simt).float()
     d = (a - b).abs()[same]
     assert d.max().item() <= 2e-2 and d.mean().item() <= 1e-3
+
+
+@pytest.mark.parametrize("shape", [
+    (1, 4, 4096, 64, 64, 16, True, 1),    # one unit per chunk
+    (2, 3, 2048, 64, 64, 16, False, 4),   # 6 units in chunks of 4 (the last one short)
+    (1, 3, 4096, 128, 64, 32, True, 2),
+    (1, 2, 8192, 64, 128, 16, True, None),
+])
+def test_attention_from_host_matches_device(cuda, shape):
+    """The pipelined host-buffer entry point returns exactly what the device
+    entry point computes, for any chunking of the units."""
+    Bh, Hh, Nh, Dh, bs, k, causal, g = shape
+    gen = torch.Generator().manual_seed(7)
+    Qh, Kh, Vh = (torch.randn(Bh, Hh, Nh, Dh, generator=gen).to(torch.bfloat16).pin_memory()
+                  for _ in range(3))
+    want = bi.attention(Qh.cuda(), Kh.cuda(), Vh.cuda(), causal=causal, block_size=bs,
+                        top_k=k).cpu()
+    got = bi.attention_from_host(Qh, Kh, Vh, causal=causal, block_size=bs, top_k=k,
+                                 units_per_chunk=g)
+    assert got.device.type == "cpu" and got.shape == want.shape
+    assert torch.equal(got, want)
+
+
+def test_attention_from_host_rejects_device_tensors(cuda):
+    Q, K, V = make_ref_inputs()
+    with pytest.raises(RuntimeError, match="block_indexer_b200"):
+        bi.attention_from_host(Q, K, V, block_size=8, top_k=4)
+
+
+@pytest.mark.parametrize("shape", [
+    (1, 2, 4096, 64, 64, 16),    # fine_kv<64, 64>
+    (1, 2, 8192, 64, 128, 16),   # fine_kv<128, 64>
+    (1, 2, 4096, 128, 64, 32),   # fine_kv<64, 128>
+])
+def test_tensor_core_path_is_deterministic(cuda, shape):
+    """Repeated calls on the same inputs give bit-identical outputs, and each
+    unit's result does not depend on the other units of the call (work items
+    land on different CTAs and list positions from run to run)."""
+    Bd, Hd, Nd, Dd, bs, k = shape
+    gen = torch.Generator().manual_seed(11)
+    Q, K, V = (torch.randn(Bd, Hd, Nd, Dd, generator=gen).to(torch.bfloat16).cuda()
+               for _ in range(3))
+    outs = [bi.attention(Q, K, V, causal=True, block_size=bs, top_k=k) for _ in range(3)]
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    per_unit = torch.cat([bi.attention(Q[:, u:u + 1].contiguous(), K[:, u:u + 1].contiguous(),
+                                       V[:, u:u + 1].contiguous(), causal=True, block_size=bs,
+                                       top_k=k) for u in range(Hd)], dim=1)
+    assert torch.equal(per_unit, outs[0])
