@@ -168,8 +168,8 @@ int bsa_forward_ex(const bsa_problem* p, const void* Q, const void* K, const voi
       if (first && events != nullptr && stage < n_events && events[stage] != nullptr)
         cudaEventRecord((cudaEvent_t)events[stage], s_);
     };
-    // The pool kernel also clears the fine stage's counters and error word,
-    // and the scorer reports into that error word.
+    // The pool kernel also clears the fine stage's error word and work-item
+    // counter, and the scorer reports into that error word.
     const bool kv = fine_uses_tensor_cores(s, p->flags);
     void* zero = kv ? (void*)(ws + L.fine) : nullptr;
     const size_t zero_bytes = kv ? fine_kv_zero_bytes(s) : 0;

@@ -8,9 +8,10 @@
 // block is picked by ~N*top_k/num_blocks queries, which fills 128-row MMA
 // tiles.  The stage therefore runs as:
 //
-//  1. bucket_count   per-unit histogram of the selected block ids
-//  2. bucket_scan    per block: list offset, first work item, and work items
-//                    of at most 128 queries
+//  1. bucket_count   per chunk of rows, the histogram of its selected blocks
+//  2. bucket_scan    per block: list offset, work items of at most 128
+//                    queries, and where each chunk's entries of the block
+//                    start in the block's list
 //  3. bucket_scatter per block, the query rows that picked it (its list), and
 //                    for every (query, slot) the partial row its result goes
 //                    to: work item i owns partial rows [128 i, 128 i + 128)
@@ -41,8 +42,15 @@ namespace bsa {
 using namespace sm100;
 
 constexpr int kTileRows = 128;      // queries per work item (MMA M)
-constexpr int kRowsPerBucketCta = 1024;
-constexpr int kMaxNbKv = 32768;
+constexpr int kMaxNbKv = 16384;
+// Bucket kernels: a CTA of kBucketThreads handles one chunk of a unit's rows,
+// in batches of kBucketBatch (query, slot) entries held in registers
+// (kBucketPer per thread).  A unit has at most kMaxChunksPerUnit chunks.
+constexpr int kBucketThreads = 512;
+constexpr int kBucketBatch = 16384;
+constexpr int kBucketPer = kBucketBatch / kBucketThreads;
+constexpr int kMaxChunksPerUnit = 64;
+constexpr int kRowBits = 14;   // staged entry: block << kRowBits | row in batch
 
 // Error codes ORed into the workspace error word.
 enum : uint32_t {
@@ -51,22 +59,37 @@ enum : uint32_t {
 };
 
 struct FineWs {
-  int32_t* counts;     // units * nb
-  int32_t* cursors;    // units * nb
-  uint32_t* err;       // [0] error bits, [1] total work items
-  int32_t* offsets;    // units * nb: a block's first position in its unit's list
-  int32_t* item_off;   // units * nb: a block's first work item (global item index)
+  uint32_t* err;       // [0] error bits, [1] total work items (zeroed before the stage)
+  int32_t* chunk_hist; // units * chunks * nb: entries of (chunk, block), then their start
+  int32_t* inv_base;   // units * nb: 128 * (block's first work item) - (its list offset)
   int4* items;         // units * max_items_per_unit
   int32_t* lists;      // units * N * k: query rows grouped by block
   int32_t* inv;        // units * N * k: (query, slot) -> partial row
   __nv_bfloat16* part_o;  // 128 rows per work item, D columns
   float2* part_ml;     // 128 rows per work item
-  size_t zero_bytes;   // counts + cursors + err, contiguous from counts
+  size_t zero_bytes;   // the error word, at the start of the region
   int64_t part_rows;   // rows of part_o / part_ml
   size_t total;
 };
 
 static size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// How the bucket kernels cut a unit's rows: batches of rows_batch rows
+// (rows_batch * k <= kBucketBatch entries), chunks of whole batches.
+struct BucketGeom {
+  int rows_batch;
+  int chunk_rows;
+  int chunks;
+};
+
+static BucketGeom bucket_geom(const Shape& s) {
+  BucketGeom g;
+  g.rows_batch = kBucketBatch / s.k;
+  const int batches = (s.N + g.rows_batch - 1) / g.rows_batch;
+  g.chunk_rows = g.rows_batch * ((batches + kMaxChunksPerUnit - 1) / kMaxChunksPerUnit);
+  g.chunks = (s.N + g.chunk_rows - 1) / g.chunk_rows;
+  return g;
+}
 
 static int64_t max_items_per_unit(const Shape& s) {
   return ((int64_t)s.N * s.k + kTileRows - 1) / kTileRows + s.nb;
@@ -82,12 +105,10 @@ static FineWs fine_ws_layout(const Shape& s, unsigned char* base) {
     return base ? base + o : nullptr;
   };
   w.part_rows = (int64_t)U * max_items_per_unit(s) * kTileRows;
-  w.counts = (int32_t*)take(4 * U * nb);
-  w.cursors = (int32_t*)take(4 * U * nb);
   w.err = (uint32_t*)take(16);
   w.zero_bytes = off;
-  w.offsets = (int32_t*)take(4 * U * nb);
-  w.item_off = (int32_t*)take(4 * U * nb);
+  w.chunk_hist = (int32_t*)take(4 * U * (size_t)bucket_geom(s).chunks * nb);
+  w.inv_base = (int32_t*)take(4 * U * nb);
   w.items = (int4*)take(16 * U * (size_t)max_items_per_unit(s));
   w.lists = (int32_t*)take(4 * (U * Nk + 256));   // slack for aligned list-slice copies
   w.inv = (int32_t*)take(4 * U * Nk);
@@ -109,50 +130,113 @@ size_t fine_kv_workspace_bytes(const Shape& s) { return fine_ws_layout(s, nullpt
 
 size_t fine_kv_zero_bytes(const Shape& s) { return fine_ws_layout(s, nullptr).zero_bytes; }
 
-size_t fine_kv_error_offset(const Shape& s) {
-  // counts and cursors precede the error word, each 256-byte aligned.
-  return 2 * a256(4 * (size_t)s.units * s.nb);
-}
+size_t fine_kv_error_offset(const Shape&) { return 0; }   // the error word leads the region
 
 // ---------------------------------------------------------------------------
-// 1. Histogram of selected block ids per unit.
-__global__ void __launch_bounds__(256)
-bucket_count_kernel(const int32_t* __restrict__ idx, int32_t* __restrict__ counts, Shape s) {
-  extern __shared__ int32_t hist[];
-  const int u = blockIdx.y;
-  for (int j = threadIdx.x; j < s.nb; j += blockDim.x) hist[j] = 0;
-  __syncthreads();
-  const int64_t row0 = (int64_t)blockIdx.x * kRowsPerBucketCta;
-  const int64_t e0 = ((int64_t)u * s.N + row0) * s.k;
-  const int64_t ne = (int64_t)min((int64_t)kRowsPerBucketCta, s.N - row0) * s.k;
-  for (int64_t e = threadIdx.x; e < ne; e += blockDim.x) {
-    int j = idx[e0 + e];
-    if (j >= 0) atomicAdd(&hist[j], 1);
-  }
-  __syncthreads();
-  for (int j = threadIdx.x; j < s.nb; j += blockDim.x)
-    if (hist[j]) atomicAdd(&counts[(int64_t)u * s.nb + j], hist[j]);
+// Bucket helpers.
+//
+// A batch of n (query, slot) entries starting at src, kBucketPer per thread,
+// -1 past the end.  VEC (top_k a multiple of 4, so every batch starts on a
+// 16-byte boundary): thread t holds entries 4 (t + kBucketThreads i) + c;
+// otherwise entries t + kBucketThreads i.
+template <bool VEC>
+__device__ __forceinline__ int batch_entry(int i) {
+  return VEC ? 4 * ((int)threadIdx.x + kBucketThreads * (i >> 2)) + (i & 3)
+             : (int)threadIdx.x + kBucketThreads * i;
 }
 
-// 2. Per unit: exclusive scan of counts -> list offsets, and work items of at
-//    most 128 queries per block.  One CTA of 1024 threads per unit.
+template <bool VEC>
+__device__ __forceinline__ void load_batch(const int32_t* __restrict__ src, int n,
+                                           int (&v)[kBucketPer]) {
+  if constexpr (VEC) {
+    const int4* s4 = reinterpret_cast<const int4*>(src);
+#pragma unroll
+    for (int i = 0; i < kBucketPer / 4; ++i) {
+      const int q = (int)threadIdx.x + kBucketThreads * i;
+      const int4 x = 4 * q < n ? __ldcg(s4 + q) : make_int4(-1, -1, -1, -1);
+      v[4 * i] = x.x; v[4 * i + 1] = x.y; v[4 * i + 2] = x.z; v[4 * i + 3] = x.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kBucketPer; ++i) {
+      const int e = batch_entry<false>(i);
+      v[i] = e < n ? __ldcg(src + e) : -1;
+    }
+  }
+}
+
+// Block-wide exclusive scan of one value per thread; *total gets the sum.
+// `warp_sums` holds kBucketThreads / 32 ints.  Ends with a barrier.
+__device__ __forceinline__ int block_exclusive_scan(int x, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int inc = x;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) warp_sums[warp] = inc;
+  __syncthreads();
+  constexpr int W = kBucketThreads / 32;
+  int before = 0, all = 0;
+#pragma unroll
+  for (int i = 0; i < W; ++i) {
+    const int ws = warp_sums[i];
+    before += i < warp ? ws : 0;
+    all += ws;
+  }
+  *total = all;
+  __syncthreads();   // warp_sums may be reused right after
+  return before + inc - x;
+}
+
+// 1. Per chunk of a unit's rows: how many of its selections pick each block.
+template <bool VEC>
+__global__ void __launch_bounds__(kBucketThreads, 2)
+bucket_count_kernel(const int32_t* __restrict__ idx, int32_t* __restrict__ chunk_hist, Shape s,
+                    BucketGeom g) {
+  extern __shared__ int32_t hist[];
+  const int u = blockIdx.y, chunk = blockIdx.x;
+  for (int j = threadIdx.x; j < s.nb; j += kBucketThreads) hist[j] = 0;
+  __syncthreads();
+  const int row_end = min(s.N, (chunk + 1) * g.chunk_rows);
+  for (int row0 = chunk * g.chunk_rows; row0 < row_end; row0 += g.rows_batch) {
+    const int n = min(g.rows_batch, row_end - row0) * s.k;
+    int v[kBucketPer];
+    load_batch<VEC>(idx + ((int64_t)u * s.N + row0) * s.k, n, v);
+#pragma unroll
+    for (int i = 0; i < kBucketPer; ++i)
+      if (v[i] >= 0) atomicAdd(&hist[v[i]], 1);
+  }
+  __syncthreads();
+  int32_t* out = chunk_hist + ((int64_t)u * g.chunks + chunk) * s.nb;
+  for (int j = threadIdx.x; j < s.nb; j += kBucketThreads) out[j] = hist[j];
+}
+
+// 2. Per unit: block counts (sums over chunks), list offsets (an exclusive
+//    scan over blocks), work items of at most 128 queries per block, each
+//    block's inv_base, and, in place of each chunk's count, the position in
+//    the unit's list where that chunk's entries of the block start.  One CTA
+//    of 1024 threads per unit.  Thread t handles blocks t, t + 1024, ...; the
+//    scan runs over blocks in that thread-major order -- list ranges only
+//    need to be disjoint, and items of one block adjacent (the fine kernel
+//    reuses a K/V tile across consecutive items of a block).
 __global__ void __launch_bounds__(1024)
-bucket_scan_kernel(const int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
-                   int32_t* __restrict__ item_off, int4* __restrict__ items,
-                   uint32_t* __restrict__ err, Shape s) {
+bucket_scan_kernel(int32_t* __restrict__ chunk_hist, int32_t* __restrict__ inv_base,
+                   int4* __restrict__ items, uint32_t* __restrict__ err, Shape s, int chunks) {
   __shared__ int32_t wsum_c[32], wsum_t[32];
   __shared__ int32_t item_base;
   const int u = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int per = (s.nb + blockDim.x - 1) / blockDim.x;
-  const int j0 = tid * per, j1 = min(s.nb, j0 + per);
-  const int32_t* c = counts + (int64_t)u * s.nb;
+  int32_t* h = chunk_hist + (int64_t)u * chunks * s.nb;   // [chunk][block]
   int sc = 0, st = 0;
-  for (int j = j0; j < j1; ++j) {
-    sc += c[j];
-    st += (c[j] + kTileRows - 1) / kTileRows;
+  for (int j = tid; j < s.nb; j += blockDim.x) {
+    int cj = 0;
+#pragma unroll 8
+    for (int ch = 0; ch < chunks; ++ch) cj += h[(int64_t)ch * s.nb + j];
+    sc += cj;
+    st += (cj + kTileRows - 1) / kTileRows;
   }
-  // Block-wide exclusive scans of (sc, st).
   int ic = sc, it = st;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -174,60 +258,121 @@ bucket_scan_kernel(const int32_t* __restrict__ counts, int32_t* __restrict__ off
     if (lane == 31) item_base = (int)atomicAdd(&err[1], (uint32_t)ib);
   }
   __syncthreads();
-  int oc = wsum_c[warp] + ic - sc;   // exclusive prefix of this thread's chunk
+  int oc = wsum_c[warp] + ic - sc;   // exclusive prefix of this thread's blocks
   int ot = wsum_t[warp] + it - st;
   const int64_t list_base = (int64_t)u * s.N * s.k;
   int4* out = items + item_base;
-  for (int j = j0; j < j1; ++j) {
-    const int cj = c[j];
-    offsets[(int64_t)u * s.nb + j] = oc;
-    item_off[(int64_t)u * s.nb + j] = item_base + ot;
-    for (int t = 0; t * kTileRows < cj; ++t) {
-      out[ot++] = make_int4(u, j, (int)(list_base + oc + t * kTileRows), min(kTileRows, cj - t * kTileRows));
+  for (int j = tid; j < s.nb; j += blockDim.x) {
+    inv_base[(int64_t)u * s.nb + j] = (item_base + ot) * kTileRows - oc;
+    int pos = oc;
+#pragma unroll 8
+    for (int ch = 0; ch < chunks; ++ch) {
+      int32_t* hc = h + (int64_t)ch * s.nb + j;
+      const int n = *hc;
+      *hc = pos;
+      pos += n;
     }
-    oc += cj;
+    const int cj = pos - oc;
+    for (int t = 0; t * kTileRows < cj; ++t)
+      out[ot++] = make_int4(u, j, (int)(list_base + oc + t * kTileRows),
+                            min(kTileRows, cj - t * kTileRows));
+    oc = pos;
   }
 }
 
 // 3. Per block, the query rows that picked it (its list), and for every
-//    (query, slot) the partial row its result lands in: work item i owns
-//    partial rows [128 i, 128 i + 128), one per list entry of the item.
-__global__ void __launch_bounds__(256)
-bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ offsets,
-                      const int32_t* __restrict__ item_off, int32_t* __restrict__ cursors,
-                      int32_t* __restrict__ lists, int32_t* __restrict__ inv, Shape s,
-                      float inv_k) {
-  extern __shared__ int32_t hist[];
-  const int u = blockIdx.y;
-  for (int j = threadIdx.x; j < s.nb; j += blockDim.x) hist[j] = 0;
-  __syncthreads();
-  const int64_t row0 = (int64_t)blockIdx.x * kRowsPerBucketCta;
-  const int64_t e0 = ((int64_t)u * s.N + row0) * s.k;
-  const int64_t ne = (int64_t)min((int64_t)kRowsPerBucketCta, s.N - row0) * s.k;
-  for (int64_t e = threadIdx.x; e < ne; e += blockDim.x) {
-    int j = idx[e0 + e];
-    if (j >= 0) atomicAdd(&hist[j], 1);
-  }
-  __syncthreads();
-  // Reserve this CTA's range within every block's list.
-  for (int j = threadIdx.x; j < s.nb; j += blockDim.x) {
-    int n = hist[j];
-    if (n) hist[j] = atomicAdd(&cursors[(int64_t)u * s.nb + j], n);
-  }
+//    (query, slot) the partial row its result goes to -- work item i owns
+//    partial rows [128 i, 128 i + 128), one per list entry of the item --
+//    or -1 for an empty slot.
+//
+//    Per batch of entries: a histogram in shared memory, its exclusive scan
+//    (a local layout with each block's entries contiguous), a second pass
+//    that places every entry in that layout, then one coalesced copy of the
+//    layout to the list, block by block.  cur[j] - pre[j] is kept in `gap`,
+//    so local position p of block j goes to list position gap[j] + p.
+template <bool VEC>
+__global__ void __launch_bounds__(kBucketThreads, 2)
+bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ chunk_hist,
+                      const int32_t* __restrict__ inv_base, int32_t* __restrict__ lists,
+                      int32_t* __restrict__ inv, Shape s, BucketGeom g, float inv_k) {
+  extern __shared__ int32_t smem_i[];
+  int32_t* cnt = smem_i;                 // nb: batch counts -> local prefix -> local cursor
+  int32_t* gap = smem_i + s.nb;          // nb: list cursor of the block minus its local prefix
+  int32_t* stage = smem_i + 2 * s.nb;    // kBucketBatch staged entries
+  __shared__ int32_t warp_sums[kBucketThreads / 32];
+  const int u = blockIdx.y, chunk = blockIdx.x;
+  const int t = threadIdx.x;
+  const int per = (s.nb + kBucketThreads - 1) / kBucketThreads;
+  // Thread t owns blocks t + kBucketThreads m (the layout is in that order).
+  const int32_t* start = chunk_hist + ((int64_t)u * g.chunks + chunk) * s.nb;
+  for (int j = t; j < s.nb; j += kBucketThreads) { gap[j] = start[j]; cnt[j] = 0; }
   __syncthreads();
   int32_t* ul = lists + (int64_t)u * s.N * s.k;
-  for (int64_t e = threadIdx.x; e < ne; e += blockDim.x) {
-    int j = idx[e0 + e];
-    if (j >= 0) {
-      const int64_t g = (int64_t)u * s.nb + j;
-      const int pos = atomicAdd(&hist[j], 1);   // position within block j's list
-      // e / k without an integer division: e < 1024 * 64, so the float
-      // product is within 2^-10 of e / k, while (e + 1/2) / k sits at least
-      // 1 / 128 away from an integer.
-      const int r = __float2int_rz(((float)e + 0.5f) * inv_k);
-      ul[offsets[g] + pos] = (int)row0 + r;
-      inv[e0 + e] = item_off[g] * kTileRows + pos;
+  const int32_t* ib = inv_base + (int64_t)u * s.nb;
+  const int row_end = min(s.N, (chunk + 1) * g.chunk_rows);
+  for (int row0 = chunk * g.chunk_rows; row0 < row_end; row0 += g.rows_batch) {
+    const int n = min(g.rows_batch, row_end - row0) * s.k;
+    const int64_t e0 = ((int64_t)u * s.N + row0) * s.k;
+    int v[kBucketPer];
+    load_batch<VEC>(idx + e0, n, v);
+#pragma unroll
+    for (int i = 0; i < kBucketPer; ++i)
+      if (v[i] >= 0) atomicAdd(&cnt[v[i]], 1);
+    __syncthreads();
+    int mine = 0;
+    for (int m = 0; m < per; ++m) {
+      const int j = t + kBucketThreads * m;
+      if (j < s.nb) mine += cnt[j];
     }
+    int total;
+    int pre = block_exclusive_scan(mine, warp_sums, &total);
+    for (int m = 0; m < per; ++m) {
+      const int j = t + kBucketThreads * m;
+      if (j < s.nb) {
+        const int c = cnt[j];
+        cnt[j] = pre;
+        gap[j] -= pre;
+        pre += c;
+      }
+    }
+    __syncthreads();
+    // v[i] becomes the entry's partial row.
+#pragma unroll
+    for (int i = 0; i < kBucketPer; ++i) {
+      const int j = v[i];
+      v[i] = -1;
+      if (j >= 0) {
+        const int lp = atomicAdd(&cnt[j], 1);
+        // Row of entry e within the batch, e / k without an integer
+        // division: e < 2^14, so the float product is within 2^-9 of e / k,
+        // while (e + 1/2) / k sits at least 1 / 128 away from an integer.
+        const int r = __float2int_rz(((float)batch_entry<VEC>(i) + 0.5f) * inv_k);
+        stage[lp] = (j << kRowBits) | r;
+        v[i] = ib[j] + gap[j] + lp;
+      }
+    }
+    if constexpr (VEC) {
+      int4* d4 = reinterpret_cast<int4*>(inv + e0);
+#pragma unroll
+      for (int i = 0; i < kBucketPer / 4; ++i) {
+        const int q = t + kBucketThreads * i;
+        if (4 * q < n) __stcg(d4 + q, make_int4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < kBucketPer; ++i) {
+        const int e = batch_entry<false>(i);
+        if (e < n) __stcg(inv + e0 + e, v[i]);
+      }
+    }
+    __syncthreads();
+    for (int p = t; p < total; p += kBucketThreads) {
+      const int w = stage[p];
+      ul[gap[w >> kRowBits] + p] = row0 + (w & ((1 << kRowBits) - 1));
+    }
+    __syncthreads();
+    for (int j = t; j < s.nb; j += kBucketThreads) { gap[j] += cnt[j]; cnt[j] = 0; }
+    __syncthreads();
   }
 }
 
@@ -832,15 +977,15 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
 
 // 5. Per query: merge its partials (m in the base-2 domain, l, and O = sum of
 //    2^(s - m) v, not divided by l), found through the (query, slot) ->
-//    partial row map.  CH = HD / 8 threads per query row, one 16-byte chunk
-//    of the output each.  The row's slot metadata (selection, partial row,
-//    m, l) is loaded once, spread over the CH threads (slot q by thread
+//    partial row map (-1 for an empty slot).  CH = HD / 8 threads per query
+//    row, one 16-byte chunk of the output each.  The row's slot metadata
+//    (partial row, m, l) is loaded once, spread over the CH threads (slot q by thread
 //    q % CH) and shared by shuffles; every partial chunk load of the row is
 //    issued before the first is used, so a thread keeps up to KMAX loads in
 //    flight instead of a chain of dependent ones.
 template <int HD, int KMAX>
 __global__ void __launch_bounds__(256)
-combine_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ inv,
+combine_kernel(const int32_t* __restrict__ inv,
                const __nv_bfloat16* __restrict__ part_o, const float2* __restrict__ part_ml,
                __nv_bfloat16* __restrict__ O, Shape s) {
   constexpr int CH = HD / 8;           // threads per row (8 or 16), a power of two <= 32
@@ -851,14 +996,13 @@ combine_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ inv,
   const bool live = gid / CH < rows;
   const int64_t R = live ? gid / CH : rows - 1;   // dead lanes mirror a real row
   const int lane = threadIdx.x & 31, base = lane & ~(CH - 1);
-  const int32_t* sel = idx + R * s.k;
-  const int32_t* prow = inv + R * s.k;
+  const int32_t* prow = inv + R * s.k;   // -1: empty slot
   int32_t pr[PER];
   float m[PER], l[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int q = c + i * CH;
-    pr[i] = (q < s.k && __ldg(sel + q) >= 0) ? __ldg(prow + q) : -1;
+    pr[i] = q < s.k ? __ldg(prow + q) : -1;
   }
   float M = -INFINITY;
 #pragma unroll
@@ -909,16 +1053,15 @@ combine_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ inv,
 }
 
 template <int HD>
-static void launch_combine(const int32_t* idx, const FineWs& w, __nv_bfloat16* O, const Shape& s,
-                           cudaStream_t st) {
+static void launch_combine(const FineWs& w, __nv_bfloat16* O, const Shape& s, cudaStream_t st) {
   const int64_t threads = (int64_t)s.units * s.N * (HD / 8);
   const unsigned blocks = (unsigned)((threads + 255) / 256);
   if (s.k <= 16)
-    combine_kernel<HD, 16><<<blocks, 256, 0, st>>>(idx, w.inv, w.part_o, w.part_ml, O, s);
+    combine_kernel<HD, 16><<<blocks, 256, 0, st>>>(w.inv, w.part_o, w.part_ml, O, s);
   else if (s.k <= 32)
-    combine_kernel<HD, 32><<<blocks, 256, 0, st>>>(idx, w.inv, w.part_o, w.part_ml, O, s);
+    combine_kernel<HD, 32><<<blocks, 256, 0, st>>>(w.inv, w.part_o, w.part_ml, O, s);
   else
-    combine_kernel<HD, 64><<<blocks, 256, 0, st>>>(idx, w.inv, w.part_o, w.part_ml, O, s);
+    combine_kernel<HD, 64><<<blocks, 256, 0, st>>>(w.inv, w.part_o, w.part_ml, O, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -999,20 +1142,27 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
       cudaEventRecord((cudaEvent_t)events[i], st);
   };
   cudaError_t e = cudaSuccess;
-  if (!pre_zeroed && (e = cudaMemsetAsync(w.counts, 0, w.zero_bytes, st)) != cudaSuccess) return e;
-  const size_t hist_smem = sizeof(int32_t) * s.nb;
-  dim3 bgrid((s.N + kRowsPerBucketCta - 1) / kRowsPerBucketCta, s.units);
-  if (hist_smem > 48 * 1024) {
-    cudaFuncSetAttribute(bucket_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)hist_smem);
-    cudaFuncSetAttribute(bucket_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)hist_smem);
-  }
-  bucket_count_kernel<<<bgrid, 256, hist_smem, st>>>(idx, w.counts, s);
-  bucket_scan_kernel<<<s.units, 1024, 0, st>>>(w.counts, w.offsets, w.item_off, w.items, w.err,
-                                               s);
-  bucket_scatter_kernel<<<bgrid, 256, hist_smem, st>>>(idx, w.offsets, w.item_off, w.cursors,
-                                                       w.lists, w.inv, s, 1.0f / (float)s.k);
+  if (!pre_zeroed && (e = cudaMemsetAsync(w.err, 0, w.zero_bytes, st)) != cudaSuccess) return e;
+  const BucketGeom g = bucket_geom(s);
+  const dim3 bgrid(g.chunks, s.units);
+  const size_t count_smem = sizeof(int32_t) * s.nb;
+  const size_t scatter_smem = sizeof(int32_t) * (2 * (size_t)s.nb + kBucketBatch);
+  // 16-byte entry loads when every batch starts on a 16-byte boundary.
+  const bool vec = (s.k % 4 == 0) && ((uintptr_t)idx % 16 == 0);
+  auto count_k = vec ? bucket_count_kernel<true> : bucket_count_kernel<false>;
+  auto scatter_k = vec ? bucket_scatter_kernel<true> : bucket_scatter_kernel<false>;
+  if (count_smem > 48 * 1024 &&
+      (e = cudaFuncSetAttribute(count_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)count_smem)) != cudaSuccess)
+    return e;
+  if ((e = cudaFuncSetAttribute(scatter_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)scatter_smem)) != cudaSuccess)
+    return e;
+  count_k<<<bgrid, kBucketThreads, count_smem, st>>>(idx, w.chunk_hist, s, g);
+  bucket_scan_kernel<<<s.units, 1024, 0, st>>>(w.chunk_hist, w.inv_base, w.items, w.err, s,
+                                               g.chunks);
+  scatter_k<<<bgrid, kBucketThreads, scatter_smem, st>>>(idx, w.chunk_hist, w.inv_base, w.lists,
+                                                         w.inv, s, g, 1.0f / (float)s.k);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   mark(2);
   if (s.bs == 64 && s.D == 64) e = launch_kv_kernel<64, 64>(Q, K, V, w, s, st);
@@ -1021,8 +1171,8 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
   else e = cudaErrorNotSupported;
   if (e != cudaSuccess) return e;
   mark(3);
-  if (s.D == 64) launch_combine<64>(idx, w, O, s, st);
-  else launch_combine<128>(idx, w, O, s, st);
+  if (s.D == 64) launch_combine<64>(w, O, s, st);
+  else launch_combine<128>(w, O, s, st);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   mark(4);
   *n_launches = 5;

@@ -7,7 +7,8 @@ namespace bsa {
 
 // Stage 1 (pool.cu).
 // `zero`/`zero_bytes` (optional): a 16-byte-aligned region the kernel clears
-// on the way (the fine stage's counters), saving a memset launch.
+// on the way (the fine stage's error word and work-item counter), saving a
+// memset launch.
 cudaError_t launch_pool_k(const __nv_bfloat16* K, float* K_repr, __nv_bfloat16* K_hi,
                           __nv_bfloat16* K_lo, const Shape& s, cudaStream_t st,
                           void* zero = nullptr, size_t zero_bytes = 0);

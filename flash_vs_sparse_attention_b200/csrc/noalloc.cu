@@ -13,7 +13,7 @@
 //    unit needs more is rejected with BSA_ERR_WORKSPACE.
 //  * Every call on a device uses the same array, and the array keeps the last
 //    call's contents.  The forward clears what must start at zero (its
-//    per-block counters and error word) at the start of every pass, so
+//    error word and work-item counter) at the start of every pass, so
 //    back-to-back calls are independent -- but two calls whose GPU work
 //    overlaps (different streams, no ordering between them) race on the
 //    array and produce garbage.
