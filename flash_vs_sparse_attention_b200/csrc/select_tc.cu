@@ -221,6 +221,9 @@ select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
       const bool valid = row < s.N;
       const int nbv = visible_blocks(tile);
       const int nw = (nbv + W - 1) / W;
+      // This row may select blocks [0, lim): the causal mask of
+      // block_indexer.py:46-50 keeps block j while j * bs <= row.
+      const int lim = !valid ? 0 : (s.causal ? min(s.nb, row / s.bs + 1) : s.nb);
       RowTopK<KCAP> sel;
       sel.init(cbuf + r, kSelRows, C::kCap, s.k);
       float gm[32];
@@ -247,16 +250,21 @@ select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
             mbar_arrive(&s_free[b]);
           }
           const int j0 = jb + c * 32;
+          // The chunk's selectable columns as a bit mask: the first lim - j0.
+          uint32_t vm = 0xffffffffu;
           if (need_mask || !valid) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int j = j0 + i;
-              if (!valid || j >= s.nb || (s.causal && (int64_t)j * s.bs > row)) x[i] = -INFINITY;
-            }
+            const int nv = lim - j0;
+            vm = nv >= 32 ? 0xffffffffu : (nv <= 0 ? 0u : (1u << nv) - 1u);
           }
           if (pass == 0) {
+            if (need_mask || !valid) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) gm[i] = fmaxf(gm[i], x[i]);
+              for (int i = 0; i < 32; ++i)
+                gm[i] = fmaxf(gm[i], ((vm >> i) & 1u) ? x[i] : -INFINITY);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) gm[i] = fmaxf(gm[i], x[i]);
+            }
           } else {
             // The chunk's candidates as a bit mask (four independent 8-bit
             // parts); the buffer compacts only if this row's own candidates
@@ -264,12 +272,10 @@ select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
             uint32_t pq[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
             for (int i = 0; i < 32; ++i) pq[i >> 3] |= sel.passes(x[i]) ? (1u << i) : 0u;
-            const uint32_t pm = (pq[0] | pq[1]) | (pq[2] | pq[3]);
+            const uint32_t pm = ((pq[0] | pq[1]) | (pq[2] | pq[3])) & vm;
             if (pm) {
               sel.reserve(__popc(pm));
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if ((pm >> i) & 1u) sel.append(x[i], j0 + i);
+              sel.append_mask(x, pm, j0);
             }
           }
         }

@@ -58,6 +58,34 @@ struct RowTopK {
     ++cnt;
   }
 
+  // Append x[i] (block j0 + i) for every set bit i of pm, in ascending i (the
+  // caller reserved room).  The four 8-bit parts of pm are four independent
+  // store chains, each starting where the parts below it end, instead of
+  // one chain of 32 dependent steps.  The buffer is in shared memory.
+  __device__ __forceinline__ void append_mask(const float (&x)[32], uint32_t pm, int32_t j0) {
+    const uint32_t step = (uint32_t)stride * (uint32_t)sizeof(uint2);
+    uint32_t a[4];
+    a[0] = (uint32_t)__cvta_generic_to_shared(buf) + (uint32_t)cnt * step;
+    a[1] = a[0] + (uint32_t)__popc(pm & 0x000000ffu) * step;
+    a[2] = a[1] + (uint32_t)__popc(pm & 0x0000ff00u) * step;
+    a[3] = a[2] + (uint32_t)__popc(pm & 0x00ff0000u) * step;
+    // Program order interleaves the chains (the stores are volatile).
+#pragma unroll
+    for (int ii = 0; ii < 8; ++ii) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int i = 8 * g + ii;
+        if ((pm >> i) & 1u) {
+          asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(a[g]),
+                       "r"(__float_as_uint(x[i])), "r"((uint32_t)(j0 + i))
+                       : "memory");
+          a[g] += step;
+        }
+      }
+    }
+    cnt += __popc(pm);
+  }
+
   __device__ __forceinline__ void push(float x, int32_t j) {
     if (passes(x)) append(x, j);
   }
@@ -122,10 +150,17 @@ struct RowTopK {
     update_thr();
   }
 
-  // Final top-k, written as k int32 in ascending block order, -1 padded.
+  // Final top-k, written as k int32 in ascending block order, -1 padded
+  // (16-byte stores when k is a multiple of 4 and out is 16-byte aligned).
   __device__ __forceinline__ void emit(int32_t* out) {
     compact();
-    for (int e = 0; e < k; ++e) out[e] = e < cnt ? (int32_t)buf[e * stride].y : -1;
+    auto at = [&](int e) { return e < cnt ? (int32_t)buf[e * stride].y : -1; };
+    if ((k & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+      for (int e = 0; e < k; e += 4)
+        *reinterpret_cast<int4*>(out + e) = make_int4(at(e), at(e + 1), at(e + 2), at(e + 3));
+    } else {
+      for (int e = 0; e < k; ++e) out[e] = at(e);
+    }
   }
 };
 
