@@ -100,22 +100,20 @@ struct RowTopK {
     update_thr();
   }
 
-  // Exact k-th largest value of the buffer: a descending min/max insertion
-  // network over KCAP registers (2 ops per cell and entry).  The entry loop
-  // is unrolled so the dependent chains of consecutive entries interleave.
+  // Exact k-th largest value of the buffer: the KCAP largest values kept
+  // in descending registers.  Inserting x sets a[p] = max(a[p], min(a[p-1],
+  // x)) from the old a[p-1] (a[0] = max(a[0], x)): 2 ops per cell, and no
+  // cell waits for another, so an entry's update is two ops deep.
   __device__ __forceinline__ float kth_value(int* n_gt_out) const {
     float a[KCAP];
 #pragma unroll
     for (int p = 0; p < KCAP; ++p) a[p] = -INFINITY;
 #pragma unroll 4
     for (int e = 0; e < cnt; ++e) {
-      float x = __uint_as_float(buf[e * stride].x);
+      const float x = __uint_as_float(buf[e * stride].x);
 #pragma unroll
-      for (int p = 0; p < KCAP; ++p) {
-        const float hi = fmaxf(a[p], x);
-        x = fminf(a[p], x);
-        a[p] = hi;
-      }
+      for (int p = KCAP - 1; p >= 1; --p) a[p] = fmaxf(a[p], fminf(a[p - 1], x));
+      a[0] = fmaxf(a[0], x);
     }
     float T = INFINITY;
     int n_gt = 0;
@@ -133,16 +131,25 @@ struct RowTopK {
     const float T = kth_value(&n_gt);
     int keep_eq = k - n_gt;
     int w = 0;
+    // Four entries are read before any is written back: every write goes at
+    // or below the entry being read, so no unread entry is overwritten.
 #pragma unroll 1
-    for (int e = 0; e < cnt; ++e) {
-      const uint2 en = buf[e * stride];
-      const float v = __uint_as_float(en.x);
-      const bool eq = !(v > T) && (v == T) && keep_eq > 0;
-      const bool take = v > T || eq;
-      keep_eq -= eq ? 1 : 0;
-      if (take) {
-        buf[w * stride] = en;
-        ++w;
+    for (int e0 = 0; e0 < cnt; e0 += 4) {
+      uint2 en[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        en[q] = e0 + q < cnt ? buf[(e0 + q) * stride] : make_uint2(0xff800000u, 0u);  // -inf
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float v = __uint_as_float(en[q].x);
+        const bool live = e0 + q < cnt;
+        const bool eq = live && !(v > T) && (v == T) && keep_eq > 0;
+        const bool take = live && (v > T || eq);
+        keep_eq -= eq ? 1 : 0;
+        if (take) {
+          buf[w * stride] = en[q];
+          ++w;
+        }
       }
     }
     cnt = w;
