@@ -18,8 +18,9 @@
 // largest is a valid floor for the row's final threshold (k distinct row
 // elements) and lets only ~4% of a 512-block row through.  Pass 2: the row's
 // scores at or above the floor go to the streaming top-k buffer
-// (topk_select.cuh), whose final emission sorts the ~20 survivors with a
-// bitonic network.  Causal tiles stop at the last block their rows can see.
+// (topk_select.cuh), whose final emission keeps the top k of the ~20
+// survivors with a min/max insertion network.  Causal tiles stop at the last
+// block their rows can see.
 // The scores arrive pre-scaled: the pool kernel splits mean * scale.
 //
 // Warps: 0-3 select (thread = row), 4 issues TMA, one thread of 5 issues MMAs.
