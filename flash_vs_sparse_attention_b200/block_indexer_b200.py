@@ -124,13 +124,13 @@ def attention_from_host(Q, K, V, causal=False, block_size=64, top_k=16, *, devic
 
     Q, K, V: (batch, heads, seq_len, head_dim) bf16 CPU tensors (pinned memory
     lets the copies run asynchronously); ``out``: optional host tensor of the
-    same shape (pinned when allocated here).  The (batch, head) units travel
-    in chunks of ``units_per_chunk`` (default: about an eighth of them): the
+    same shape (pinned when allocated here).  One call of the C entry point
+    ``bsa_forward_host``: the (batch, head) units travel in chunks of
+    ``units_per_chunk`` (default: about a quarter of them), and the
     host->device copy of chunk i + 1, the forward of chunk i and the
-    device->host copy of chunk i - 1 run on three streams at once, on two
-    device buffers per tensor, so the PCIe transfers hide the compute.  Each
-    unit's result is the one ``attention`` computes.  Returns when the output
-    is in host memory.
+    device->host copy of chunk i - 1 run on three streams at once, so the
+    PCIe transfers hide the compute.  Each unit's result is the one
+    ``attention`` computes.  Returns when the output is in host memory.
     """
     L = _require_backend()
     B, H, N, D = Q.shape
@@ -145,54 +145,24 @@ def attention_from_host(Q, K, V, causal=False, block_size=64, top_k=16, *, devic
         if t.dtype != torch.bfloat16:
             raise TypeError(f"{VARIANT}: {name} must be torch.bfloat16 (got {t.dtype})")
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-    U = B * H
-    g = units_per_chunk or max(1, -(-U // 8))
-    g = max(1, min(g, U))
-    Qf, Kf, Vf = (t.contiguous().view(U, N, D) for t in (Q, K, V))
+    Qc, Kc, Vc = (t.contiguous() for t in (Q, K, V))
     if out is None:
         out = torch.empty((B, H, N, D), dtype=torch.bfloat16, pin_memory=True)
-    Of = out.view(U, N, D)
+    if out.shape != Q.shape or out.dtype != torch.bfloat16 or out.device.type != "cpu" \
+            or not out.is_contiguous():
+        raise ValueError(f"{VARIANT}: out must be a contiguous bf16 host tensor of Q's shape")
+    p = problem(B, H, N, D, causal, block_size, top_k, flags)
+    g = int(units_per_chunk or 0)
     with torch.cuda.device(dev):
-        main = torch.cuda.current_stream(dev)
-        s_in, s_comp, s_out = (torch.cuda.Stream(dev) for _ in range(3))
-        for s_ in (s_in, s_comp, s_out):
-            s_.wait_stream(main)
-        dq, dk, dv, do = ([torch.empty((g, N, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
-                          for _ in range(4))
-        p_full = problem(1, g, N, D, causal, block_size, top_k, flags)
-        nbytes = workspace_bytes(p_full)
-        ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
-        ev_in = [torch.cuda.Event() for _ in range(2)]
-        ev_comp = [torch.cuda.Event() for _ in range(2)]
-        ev_out = [torch.cuda.Event() for _ in range(2)]
-        for i, u0 in enumerate(range(0, U, g)):
-            gu = min(g, U - u0)
-            b = i % 2
-            with torch.cuda.stream(s_in):
-                if i >= 2:
-                    s_in.wait_event(ev_comp[b])      # the forward of chunk i - 2 read buffer b
-                dq[b][:gu].copy_(Qf[u0:u0 + gu], non_blocking=True)
-                dk[b][:gu].copy_(Kf[u0:u0 + gu], non_blocking=True)
-                dv[b][:gu].copy_(Vf[u0:u0 + gu], non_blocking=True)
-                ev_in[b].record(s_in)
-            s_comp.wait_event(ev_in[b])
-            if i >= 2:
-                s_comp.wait_event(ev_out[b])         # chunk i - 2's output left buffer b
-            p = problem(1, gu, N, D, causal, block_size, top_k, flags)
-            st = L.bsa_forward(ctypes.byref(p), _ptr(dq[b]), _ptr(dk[b]), _ptr(dv[b]),
-                               _ptr(do[b]), _ptr(ws), ctypes.c_size_t(ws.numel()),
-                               ctypes.c_void_p(s_comp.cuda_stream))
-            _lib.check(st, VARIANT)
-            ev_comp[b].record(s_comp)
-            with torch.cuda.stream(s_out):
-                s_out.wait_event(ev_comp[b])
-                Of[u0:u0 + gu].copy_(do[b][:gu], non_blocking=True)
-                ev_out[b].record(s_out)
-        # The caller's stream (where the buffers were allocated) waits for all
-        # three before they can be reused; the host waits for the output.
-        for s_ in (s_in, s_comp, s_out):
-            main.wait_stream(s_)
-        s_out.synchronize()
+        nbytes = L.bsa_host_workspace_bytes(ctypes.byref(p), g)
+        if nbytes == 0:
+            _lib.check(L.bsa_check_problem(ctypes.byref(p)), VARIANT)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        stream = torch.cuda.current_stream(dev)
+        _lib.check(L.bsa_forward_host(ctypes.byref(p), _ptr(Qc), _ptr(Kc), _ptr(Vc), _ptr(out), g,
+                                      _ptr(ws), ctypes.c_size_t(nbytes),
+                                      ctypes.c_void_p(stream.cuda_stream)), VARIANT)
+        stream.synchronize()
     return out
 
 

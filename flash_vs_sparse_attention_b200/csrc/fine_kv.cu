@@ -9,10 +9,11 @@
 // tiles.  The stage therefore runs as:
 //
 //  1. bucket_count   per chunk of rows, the histogram of its selected blocks
-//  2. bucket_scan    per block: list offset, work items of at most 128
-//                    queries, and where each chunk's entries of the block
-//                    start in the block's list
-//  3. bucket_scatter per block, the query rows that picked it (its list), and
+//                    and where the chunk's entries of each block start in
+//                    that block's list; the unit's last chunk to finish then
+//                    lays out the unit: per block its list offset and work
+//                    items of at most 128 queries
+//  2. bucket_scatter per block, the query rows that picked it (its list), and
 //                    for every (query, slot) the partial row its result goes
 //                    to: work item i owns partial rows [128 i, 128 i + 128)
 //  4. fine_kv        persistent kernel over work items.  For each item (one
@@ -59,15 +60,18 @@ enum : uint32_t {
 };
 
 struct FineWs {
-  uint32_t* err;       // [0] error bits, [1] total work items (zeroed before the stage)
-  int32_t* chunk_hist; // units * chunks * nb: entries of (chunk, block), then their start
-  int32_t* inv_base;   // units * nb: 128 * (block's first work item) - (its list offset)
+  uint32_t* err;       // [0] error bits, [1] total work items      } zeroed before
+  int32_t* done;       // units: chunks counted so far                } the stage
+  int32_t* cursor;     // units * nb: entries of each block so far    }
+  int32_t* chunk_rel;  // units * chunks * nb: start of (chunk, block) within the block's list
+  int32_t* offsets;    // units * nb: a block's first position in its unit's list
+  int32_t* item_row;   // units * nb: 128 * (a block's first work item)
   int4* items;         // units * max_items_per_unit
   int32_t* lists;      // units * N * k: query rows grouped by block
   int32_t* inv;        // units * N * k: (query, slot) -> partial row
   __nv_bfloat16* part_o;  // 128 rows per work item, D columns
   float2* part_ml;     // 128 rows per work item
-  size_t zero_bytes;   // the error word, at the start of the region
+  size_t zero_bytes;   // err, done and cursor, at the start of the region
   int64_t part_rows;   // rows of part_o / part_ml
   size_t total;
 };
@@ -106,9 +110,12 @@ static FineWs fine_ws_layout(const Shape& s, unsigned char* base) {
   };
   w.part_rows = (int64_t)U * max_items_per_unit(s) * kTileRows;
   w.err = (uint32_t*)take(16);
+  w.done = (int32_t*)take(4 * U);
+  w.cursor = (int32_t*)take(4 * U * nb);
   w.zero_bytes = off;
-  w.chunk_hist = (int32_t*)take(4 * U * (size_t)bucket_geom(s).chunks * nb);
-  w.inv_base = (int32_t*)take(4 * U * nb);
+  w.chunk_rel = (int32_t*)take(4 * U * (size_t)bucket_geom(s).chunks * nb);
+  w.offsets = (int32_t*)take(4 * U * nb);
+  w.item_row = (int32_t*)take(4 * U * nb);
   w.items = (int4*)take(16 * U * (size_t)max_items_per_unit(s));
   w.lists = (int32_t*)take(4 * (U * Nk + 256));   // slack for aligned list-slice copies
   w.inv = (int32_t*)take(4 * U * Nk);
@@ -190,14 +197,29 @@ __device__ __forceinline__ int block_exclusive_scan(int x, int* warp_sums, int* 
   return before + inc - x;
 }
 
-// 1. Per chunk of a unit's rows: how many of its selections pick each block.
+// 1. Per chunk of a unit's rows: how many of its selections pick each block,
+//    and where the chunk's entries of block j start within j's list (an
+//    atomic on the block's cursor, so the chunks of a list come in any
+//    order; every row's result is the same whichever work item holds it).
+//    The unit's last chunk to finish -- a ticket taken after a device-wide
+//    fence -- then lays out the unit: block counts (the cursors), list
+//    offsets (an exclusive scan over blocks), and work items of at most 128
+//    queries per block.  Thread t handles blocks t, t + kBucketThreads, ...,
+//    and the scan runs over blocks in that thread-major order: list ranges
+//    only need to be disjoint, and items of one block adjacent (the fine
+//    kernel reuses a K/V tile across consecutive items of a block).
 template <bool VEC>
 __global__ void __launch_bounds__(kBucketThreads, 2)
-bucket_count_kernel(const int32_t* __restrict__ idx, int32_t* __restrict__ chunk_hist, Shape s,
-                    BucketGeom g) {
+bucket_count_kernel(const int32_t* __restrict__ idx, int32_t* __restrict__ cursor,
+                    int32_t* __restrict__ chunk_rel, int32_t* __restrict__ done,
+                    int32_t* __restrict__ offsets, int32_t* __restrict__ item_row,
+                    int4* __restrict__ items, uint32_t* __restrict__ err, Shape s, BucketGeom g) {
   extern __shared__ int32_t hist[];
+  __shared__ int32_t wsum_c[kBucketThreads / 32], wsum_t[kBucketThreads / 32];
+  __shared__ int32_t ticket, item_base;
   const int u = blockIdx.y, chunk = blockIdx.x;
-  for (int j = threadIdx.x; j < s.nb; j += kBucketThreads) hist[j] = 0;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int j = tid; j < s.nb; j += kBucketThreads) hist[j] = 0;
   __syncthreads();
   const int row_end = min(s.N, (chunk + 1) * g.chunk_rows);
   for (int row0 = chunk * g.chunk_rows; row0 < row_end; row0 += g.rows_batch) {
@@ -209,52 +231,43 @@ bucket_count_kernel(const int32_t* __restrict__ idx, int32_t* __restrict__ chunk
       if (v[i] >= 0) atomicAdd(&hist[v[i]], 1);
   }
   __syncthreads();
-  int32_t* out = chunk_hist + ((int64_t)u * g.chunks + chunk) * s.nb;
-  for (int j = threadIdx.x; j < s.nb; j += kBucketThreads) out[j] = hist[j];
-}
+  int32_t* cur = cursor + (int64_t)u * s.nb;
+  int32_t* rel = chunk_rel + ((int64_t)u * g.chunks + chunk) * s.nb;
+  for (int j = tid; j < s.nb; j += kBucketThreads) {
+    const int c = hist[j];
+    rel[j] = c ? atomicAdd(&cur[j], c) : 0;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) ticket = atomicAdd(&done[u], 1);
+  __syncthreads();
+  if (ticket != g.chunks - 1) return;
+  __threadfence();   // every chunk's cursor update is visible from here on
 
-// 2. Per unit: block counts (sums over chunks), list offsets (an exclusive
-//    scan over blocks), work items of at most 128 queries per block, each
-//    block's inv_base, and, in place of each chunk's count, the position in
-//    the unit's list where that chunk's entries of the block start.  One CTA
-//    of 1024 threads per unit.  Thread t handles blocks t, t + 1024, ...; the
-//    scan runs over blocks in that thread-major order -- list ranges only
-//    need to be disjoint, and items of one block adjacent (the fine kernel
-//    reuses a K/V tile across consecutive items of a block).
-__global__ void __launch_bounds__(1024)
-bucket_scan_kernel(int32_t* __restrict__ chunk_hist, int32_t* __restrict__ inv_base,
-                   int4* __restrict__ items, uint32_t* __restrict__ err, Shape s, int chunks) {
-  __shared__ int32_t wsum_c[32], wsum_t[32];
-  __shared__ int32_t item_base;
-  const int u = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  int32_t* h = chunk_hist + (int64_t)u * chunks * s.nb;   // [chunk][block]
   int sc = 0, st = 0;
-  for (int j = tid; j < s.nb; j += blockDim.x) {
-    int cj = 0;
-#pragma unroll 8
-    for (int ch = 0; ch < chunks; ++ch) cj += h[(int64_t)ch * s.nb + j];
+  for (int j = tid; j < s.nb; j += kBucketThreads) {
+    const int cj = __ldcg(cur + j);
     sc += cj;
     st += (cj + kTileRows - 1) / kTileRows;
   }
   int ic = sc, it = st;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    int a = __shfl_up_sync(0xffffffffu, ic, o), b = __shfl_up_sync(0xffffffffu, it, o);
+    const int a = __shfl_up_sync(0xffffffffu, ic, o), b = __shfl_up_sync(0xffffffffu, it, o);
     if (lane >= o) { ic += a; it += b; }
   }
   if (lane == 31) { wsum_c[warp] = ic; wsum_t[warp] = it; }
   __syncthreads();
   if (warp == 0) {
-    int a = wsum_c[lane], b = wsum_t[lane];
+    constexpr int W = kBucketThreads / 32;
+    const int a = lane < W ? wsum_c[lane] : 0, b = lane < W ? wsum_t[lane] : 0;
     int ia = a, ib = b;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      int x = __shfl_up_sync(0xffffffffu, ia, o), y = __shfl_up_sync(0xffffffffu, ib, o);
+      const int x = __shfl_up_sync(0xffffffffu, ia, o), y = __shfl_up_sync(0xffffffffu, ib, o);
       if (lane >= o) { ia += x; ib += y; }
     }
-    wsum_c[lane] = ia - a;
-    wsum_t[lane] = ib - b;
+    if (lane < W) { wsum_c[lane] = ia - a; wsum_t[lane] = ib - b; }
     if (lane == 31) item_base = (int)atomicAdd(&err[1], (uint32_t)ib);
   }
   __syncthreads();
@@ -262,25 +275,18 @@ bucket_scan_kernel(int32_t* __restrict__ chunk_hist, int32_t* __restrict__ inv_b
   int ot = wsum_t[warp] + it - st;
   const int64_t list_base = (int64_t)u * s.N * s.k;
   int4* out = items + item_base;
-  for (int j = tid; j < s.nb; j += blockDim.x) {
-    inv_base[(int64_t)u * s.nb + j] = (item_base + ot) * kTileRows - oc;
-    int pos = oc;
-#pragma unroll 8
-    for (int ch = 0; ch < chunks; ++ch) {
-      int32_t* hc = h + (int64_t)ch * s.nb + j;
-      const int n = *hc;
-      *hc = pos;
-      pos += n;
-    }
-    const int cj = pos - oc;
+  for (int j = tid; j < s.nb; j += kBucketThreads) {
+    const int cj = __ldcg(cur + j);
+    offsets[(int64_t)u * s.nb + j] = oc;
+    item_row[(int64_t)u * s.nb + j] = (item_base + ot) * kTileRows;
     for (int t = 0; t * kTileRows < cj; ++t)
       out[ot++] = make_int4(u, j, (int)(list_base + oc + t * kTileRows),
                             min(kTileRows, cj - t * kTileRows));
-    oc = pos;
+    oc += cj;
   }
 }
 
-// 3. Per block, the query rows that picked it (its list), and for every
+// 2. Per block, the query rows that picked it (its list), and for every
 //    (query, slot) the partial row its result goes to -- work item i owns
 //    partial rows [128 i, 128 i + 128), one per list entry of the item --
 //    or -1 for an empty slot.
@@ -288,27 +294,31 @@ bucket_scan_kernel(int32_t* __restrict__ chunk_hist, int32_t* __restrict__ inv_b
 //    Per batch of entries: a histogram in shared memory, its exclusive scan
 //    (a local layout with each block's entries contiguous), a second pass
 //    that places every entry in that layout, then one coalesced copy of the
-//    layout to the list, block by block.  cur[j] - pre[j] is kept in `gap`,
-//    so local position p of block j goes to list position gap[j] + p.
+//    layout to the list, block by block.  With cur[j] the block's next list
+//    position relative to its offset, gap[j] = cur[j] - pre[j]: local
+//    position p of block j goes to list position offsets[j] + gap[j] + p and
+//    is partial row item_row[j] + gap[j] + p.
 template <bool VEC>
 __global__ void __launch_bounds__(kBucketThreads, 2)
-bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ chunk_hist,
-                      const int32_t* __restrict__ inv_base, int32_t* __restrict__ lists,
-                      int32_t* __restrict__ inv, Shape s, BucketGeom g, float inv_k) {
+bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ chunk_rel,
+                      const int32_t* __restrict__ offsets, const int32_t* __restrict__ item_row,
+                      int32_t* __restrict__ lists, int32_t* __restrict__ inv, Shape s,
+                      BucketGeom g, float inv_k) {
   extern __shared__ int32_t smem_i[];
   int32_t* cnt = smem_i;                 // nb: batch counts -> local prefix -> local cursor
-  int32_t* gap = smem_i + s.nb;          // nb: list cursor of the block minus its local prefix
+  int32_t* gap = smem_i + s.nb;          // nb: the block's cursor minus its local prefix
   int32_t* stage = smem_i + 2 * s.nb;    // kBucketBatch staged entries
   __shared__ int32_t warp_sums[kBucketThreads / 32];
   const int u = blockIdx.y, chunk = blockIdx.x;
   const int t = threadIdx.x;
   const int per = (s.nb + kBucketThreads - 1) / kBucketThreads;
   // Thread t owns blocks t + kBucketThreads m (the layout is in that order).
-  const int32_t* start = chunk_hist + ((int64_t)u * g.chunks + chunk) * s.nb;
+  const int32_t* start = chunk_rel + ((int64_t)u * g.chunks + chunk) * s.nb;
   for (int j = t; j < s.nb; j += kBucketThreads) { gap[j] = start[j]; cnt[j] = 0; }
   __syncthreads();
   int32_t* ul = lists + (int64_t)u * s.N * s.k;
-  const int32_t* ib = inv_base + (int64_t)u * s.nb;
+  const int32_t* lo = offsets + (int64_t)u * s.nb;
+  const int32_t* ir = item_row + (int64_t)u * s.nb;
   const int row_end = min(s.N, (chunk + 1) * g.chunk_rows);
   for (int row0 = chunk * g.chunk_rows; row0 < row_end; row0 += g.rows_batch) {
     const int n = min(g.rows_batch, row_end - row0) * s.k;
@@ -348,7 +358,7 @@ bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict
         // while (e + 1/2) / k sits at least 1 / 128 away from an integer.
         const int r = __float2int_rz(((float)batch_entry<VEC>(i) + 0.5f) * inv_k);
         stage[lp] = (j << kRowBits) | r;
-        v[i] = ib[j] + gap[j] + lp;
+        v[i] = ir[j] + gap[j] + lp;
       }
     }
     if constexpr (VEC) {
@@ -368,7 +378,8 @@ bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict
     __syncthreads();
     for (int p = t; p < total; p += kBucketThreads) {
       const int w = stage[p];
-      ul[gap[w >> kRowBits] + p] = row0 + (w & ((1 << kRowBits) - 1));
+      const int j = w >> kRowBits;
+      ul[lo[j] + gap[j] + p] = row0 + (w & ((1 << kRowBits) - 1));
     }
     __syncthreads();
     for (int j = t; j < s.nb; j += kBucketThreads) { gap[j] += cnt[j]; cnt[j] = 0; }
@@ -481,7 +492,7 @@ constexpr int kMetaKv = kTileRows + 4;   // int offset of the word in the stage 
 struct FineKvParams {
   const int4* items;
   const int32_t* lists;
-  const uint32_t* total_items;  // device word written by bucket_scan
+  const uint32_t* total_items;  // device word written by bucket_count's layout step
   float2* part_ml;
   uint32_t* err;
   Shape s;
@@ -1158,11 +1169,10 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
   if ((e = cudaFuncSetAttribute(scatter_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)scatter_smem)) != cudaSuccess)
     return e;
-  count_k<<<bgrid, kBucketThreads, count_smem, st>>>(idx, w.chunk_hist, s, g);
-  bucket_scan_kernel<<<s.units, 1024, 0, st>>>(w.chunk_hist, w.inv_base, w.items, w.err, s,
-                                               g.chunks);
-  scatter_k<<<bgrid, kBucketThreads, scatter_smem, st>>>(idx, w.chunk_hist, w.inv_base, w.lists,
-                                                         w.inv, s, g, 1.0f / (float)s.k);
+  count_k<<<bgrid, kBucketThreads, count_smem, st>>>(idx, w.cursor, w.chunk_rel, w.done,
+                                                     w.offsets, w.item_row, w.items, w.err, s, g);
+  scatter_k<<<bgrid, kBucketThreads, scatter_smem, st>>>(idx, w.chunk_rel, w.offsets, w.item_row,
+                                                         w.lists, w.inv, s, g, 1.0f / (float)s.k);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   mark(2);
   if (s.bs == 64 && s.D == 64) e = launch_kv_kernel<64, 64>(Q, K, V, w, s, st);
@@ -1175,7 +1185,7 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
   else launch_combine<128>(w, O, s, st);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   mark(4);
-  *n_launches = 5;
+  *n_launches = 4;
   return cudaSuccess;
 }
 

@@ -41,13 +41,22 @@ pool_k_kernel(const __nv_bfloat16* __restrict__ K, float* __restrict__ K_repr,
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
 
   if (active) {
-#pragma unroll 8
-    for (int r = g; r < s.bs; r += rows_per_iter) {
-      uint4 v = __ldg(src + (int64_t)r * chunks + c);
-      acc[0] += bf16_lo(v.x); acc[1] += bf16_hi(v.x);
-      acc[2] += bf16_lo(v.y); acc[3] += bf16_hi(v.y);
-      acc[4] += bf16_lo(v.z); acc[5] += bf16_hi(v.z);
-      acc[6] += bf16_lo(v.w); acc[7] += bf16_hi(v.w);
+    // Batches of 16 loads issued before any is summed (a whole 64-key block
+    // per batch at head_dim 64): one memory round trip per batch.
+    for (int r0 = g; r0 < s.bs; r0 += 16 * rows_per_iter) {
+      uint4 v[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const int r = r0 + q * rows_per_iter;
+        v[q] = r < s.bs ? __ldg(src + (int64_t)r * chunks + c) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        acc[0] += bf16_lo(v[q].x); acc[1] += bf16_hi(v[q].x);
+        acc[2] += bf16_lo(v[q].y); acc[3] += bf16_hi(v[q].y);
+        acc[4] += bf16_lo(v[q].z); acc[5] += bf16_hi(v[q].z);
+        acc[6] += bf16_lo(v[q].w); acc[7] += bf16_hi(v[q].w);
+      }
     }
   }
   // Reduce over row groups (lanes that differ in the row-group bits).

@@ -90,6 +90,28 @@ int bsa_forward_ex(const bsa_problem* p, const void* Q, const void* K, const voi
                    void* O, void* workspace, size_t workspace_bytes, void* stream,
                    void* const* events, int n_events, int* n_launches);
 
+/* Bytes of device workspace bsa_forward_host needs with `units_per_chunk`
+ * (batch*head) units per chunk (<= 0: the default, a quarter of the units
+ * rounded up): two device copies of one chunk's Q, K, V and O, and the
+ * bsa_forward workspace of one chunk. */
+size_t bsa_host_workspace_bytes(const bsa_problem* p, int64_t units_per_chunk);
+
+/* The forward pass on HOST buffers: Q_host, K_host, V_host and O_host are
+ * (B, H, N, D) bf16 in host memory (page-locked memory lets the copies run
+ * asynchronously; pageable memory works, slower).  The caller of the
+ * reference moves tensors to the device and back around
+ * block_indexer_triton.attention (block_indexer_triton.py:86-146); here the
+ * (batch, head) units travel in chunks of `units_per_chunk` (<= 0: the
+ * default) and the host->device copy of chunk i+1, the forward of chunk i and
+ * the device->host copy of chunk i-1 run at once on three streams the
+ * library keeps per device, over two device copies of each chunk buffer.
+ * The work is ordered after earlier work on `stream`, and `stream` waits for
+ * all of it: O_host is complete once `stream` has been synchronised.  Calls
+ * from several host threads on one device are serialised. */
+int bsa_forward_host(const bsa_problem* p, const void* Q_host, const void* K_host,
+                     const void* V_host, void* O_host, int64_t units_per_chunk,
+                     void* device_workspace, size_t workspace_bytes, void* stream);
+
 /* Stage 1 alone (block_indexer_triton.py:120, block_indexer.py:33).
  * K_repr: (B*H, nb, D) fp32 block means.  K_split: NULL, or (2, B*H, nb, D)
  * bf16, the high and low bf16 parts of K_repr * scale (hi + lo equals it to

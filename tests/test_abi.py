@@ -75,3 +75,31 @@ def test_forward_rejects_bad_arguments_without_touching_the_gpu():
     assert st == _lib.BSA_ERR_WORKSPACE
     bad = prob(N=100)
     assert L.bsa_forward(ctypes.byref(bad), al, al, al, al, al, 1 << 20, null) == _lib.BSA_ERR_INVALID
+
+
+def test_forward_host_checks_arguments_without_touching_the_gpu():
+    """bsa_forward_host validates the problem, its buffers and the size of the
+    device workspace (two copies of a chunk's Q, K, V, O plus one chunk's
+    forward workspace) before any CUDA call."""
+    L = _lib.lib()
+    p = prob(B=1, H=8, N=4096, D=64, block_size=64, top_k=16)
+    per_unit = 4096 * 64 * 2
+    one = L.bsa_host_workspace_bytes(ctypes.byref(p), 1)
+    c1 = prob(B=1, H=1, N=4096, D=64, block_size=64, top_k=16)
+    assert one == 8 * per_unit + L.bsa_workspace_bytes(ctypes.byref(c1), 0)
+    # default chunk: a quarter of the 8 units
+    c2 = prob(B=1, H=2, N=4096, D=64, block_size=64, top_k=16)
+    assert L.bsa_host_workspace_bytes(ctypes.byref(p), 0) == \
+        8 * 2 * per_unit + L.bsa_workspace_bytes(ctypes.byref(c2), 0)
+    c4 = prob(B=1, H=4, N=4096, D=64, block_size=64, top_k=16)
+    assert L.bsa_host_workspace_bytes(ctypes.byref(p), 4) == \
+        8 * 4 * per_unit + L.bsa_workspace_bytes(ctypes.byref(c4), 0)
+    assert L.bsa_host_workspace_bytes(ctypes.byref(prob(N=1000)), 1) == 0
+    null = ctypes.c_void_p(0)
+    al = ctypes.c_void_p(4096)
+    mis = ctypes.c_void_p(4104)
+    call = L.bsa_forward_host
+    assert call(ctypes.byref(p), null, al, al, al, 1, al, one, null) == _lib.BSA_ERR_INVALID
+    assert call(ctypes.byref(p), al, al, al, al, 1, mis, one, null) == _lib.BSA_ERR_ALIGNMENT
+    assert call(ctypes.byref(p), al, al, al, al, 1, al, one - 1, null) == _lib.BSA_ERR_WORKSPACE
+    assert call(ctypes.byref(prob(N=100)), al, al, al, al, 1, al, one, null) == _lib.BSA_ERR_INVALID

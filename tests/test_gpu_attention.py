@@ -1,6 +1,7 @@
 """End-to-end parity of the variant API against the oracle on the benchmark
 workloads, plus the reference's own GPU tests restated (GPU only)."""
 
+import ctypes
 import numpy as np
 import pytest
 import torch
@@ -154,6 +155,28 @@ def test_attention_from_host_matches_device(cuda, shape):
                                  units_per_chunk=g)
     assert got.device.type == "cpu" and got.shape == want.shape
     assert torch.equal(got, want)
+
+
+def test_forward_host_pageable_memory_on_a_side_stream(cuda):
+    """bsa_forward_host through the C ABI with pageable host buffers, issued on
+    a non-default stream: once that stream is synchronised the host output
+    equals the device entry point's."""
+    L = _lib.lib()
+    B_, H_, N_, D_ = 1, 3, 4096, 64
+    gen = torch.Generator().manual_seed(11)
+    Qh, Kh, Vh = (torch.randn(B_, H_, N_, D_, generator=gen).to(torch.bfloat16) for _ in range(3))
+    want = bi.attention(Qh.cuda(), Kh.cuda(), Vh.cuda(), causal=True).cpu()
+    Oh = torch.full_like(Qh, 7.0)
+    p = bi.problem(B_, H_, N_, D_, True, 64, 16)
+    nbytes = L.bsa_host_workspace_bytes(ctypes.byref(p), 2)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    st = L.bsa_forward_host(ctypes.byref(p), bi._ptr(Qh), bi._ptr(Kh), bi._ptr(Vh), bi._ptr(Oh), 2,
+                            bi._ptr(ws), ctypes.c_size_t(nbytes), ctypes.c_void_p(side.cuda_stream))
+    assert st == _lib.BSA_OK, L.bsa_last_error()
+    side.synchronize()
+    assert torch.equal(Oh, want)
 
 
 def test_attention_from_host_rejects_device_tensors(cuda):
