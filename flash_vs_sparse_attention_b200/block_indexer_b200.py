@@ -219,3 +219,99 @@ def fine(Q, K, V, idx, causal=False, block_size=64, *, flags=0, check_errors=Tru
         if check_errors:
             _raise_on_kernel_error(L, p, ws, False)
     return O
+
+
+# ---------------------------------------------------------------------------
+# Decode-time reuse: block means kept beside a KV cache.  The reference has
+# no decode path (its stated future work); these evaluate its algorithm
+# (block_indexer.py:33-84) for new query rows against a cache.
+
+def pool_k_blocks(K, K_repr, block_begin, block_end, kv_len, block_size=64, K_split=None):
+    """Incremental stage 1: pool blocks ``[block_begin, block_end)`` of a cache.
+
+    K: (B, H, capacity, D) bf16 CUDA tensor holding keys ``[0, kv_len)``;
+    K_repr: (B, H, capacity // block_size, D) fp32, written in place (a block
+    only partly filled becomes the mean of its present keys; a full block what
+    ``pool_k`` computes); K_split: optional (2, B, H, nb, D) bf16 hi/lo split.
+    """
+    L = _require_backend()
+    B, H, N, D = K.shape
+    p = problem(B, H, N, D, False, block_size, 1)
+    split = _ptr(K_split) if K_split is not None else ctypes.c_void_p(0)
+    with torch.cuda.device(K.device):
+        _lib.check(L.bsa_pool_k_blocks(ctypes.byref(p), _ptr(K), _ptr(K_repr), split,
+                                       int(block_begin), int(block_end), int(kv_len),
+                                       _stream(K.device)), VARIANT)
+    return K_repr
+
+
+def decode(Q_new, q_pos, K, V, K_repr, causal=True, block_size=64, top_k=16, *,
+           return_indices=False):
+    """Attention of new query rows over a KV cache and its block means.
+
+    Q_new: (B, H, q_len, D) bf16 at positions ``q_pos .. q_pos + q_len - 1``;
+    K, V: (B, H, capacity, D) bf16 caches whose first ``q_pos + q_len`` keys
+    are valid; K_repr: the cache's block means (``pool_k`` / ``pool_k_blocks``,
+    current up to the block of the last new key).  Returns (B, H, q_len, D)
+    bf16.  Causal rows see the blocks starting at or before their position
+    and the keys up to it; with a key count that is a multiple of
+    ``block_size`` a row equals the whole-sequence forward's row on the
+    CUDA-core path.  ``return_indices``: also return the selected blocks,
+    (B, H, q_len, top_k) int32 in ascending order, -1 in empty slots.
+    """
+    L = _require_backend()
+    B, H, q_len, D = Q_new.shape
+    N = K.shape[2]
+    if K.shape != V.shape or K.shape[:2] != (B, H) or K.shape[3] != D:
+        raise ValueError(f"{VARIANT}: cache K, V must be (B, H, capacity, D) matching Q's B, H, D")
+    p = problem(B, H, N, D, causal, block_size, top_k)
+    Qc = Q_new.contiguous()
+    with torch.cuda.device(Q_new.device):
+        O = torch.empty_like(Qc)
+        nbytes = L.bsa_decode_workspace_bytes(ctypes.byref(p), q_len)
+        ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=Q_new.device)
+        _lib.check(L.bsa_decode(ctypes.byref(p), _ptr(Qc), q_len, int(q_pos), _ptr(K), _ptr(V),
+                                _ptr(K_repr), _ptr(O), _ptr(ws), ctypes.c_size_t(ws.numel()),
+                                _stream(Q_new.device)), VARIANT)
+    if return_indices:
+        idx = ws[:4 * B * H * q_len * top_k].view(torch.int32).view(B, H, q_len, top_k).clone()
+        return O, idx
+    return O
+
+
+class DecodeCache:
+    """A KV cache with its block means, grown token by token or in chunks.
+
+    ``append(K_new, V_new)`` writes the new keys and values and re-pools only
+    the blocks they touch; ``attend(Q_new)`` runs the new rows (the last
+    ``q_len`` positions) against everything cached so far.
+    """
+
+    def __init__(self, batch, heads, capacity, head_dim, block_size=64, top_k=16,
+                 device=None):
+        _require_backend()
+        if capacity % block_size != 0:
+            raise ValueError(f"{VARIANT}: capacity {capacity} must be a multiple of block_size")
+        dev = torch.device(device) if device is not None else torch.device("cuda")
+        shape = (batch, heads, capacity, head_dim)
+        self.K = torch.zeros(shape, dtype=torch.bfloat16, device=dev)
+        self.V = torch.zeros(shape, dtype=torch.bfloat16, device=dev)
+        self.K_repr = torch.zeros(batch, heads, capacity // block_size, head_dim,
+                                  dtype=torch.float32, device=dev)
+        self.block_size, self.top_k, self.length = block_size, top_k, 0
+
+    def append(self, K_new, V_new):
+        t = K_new.shape[2]
+        end = self.length + t
+        if end > self.K.shape[2]:
+            raise ValueError(f"{VARIANT}: cache capacity {self.K.shape[2]} exceeded")
+        self.K[:, :, self.length:end] = K_new
+        self.V[:, :, self.length:end] = V_new
+        bs = self.block_size
+        pool_k_blocks(self.K, self.K_repr, self.length // bs, -(-end // bs), end, bs)
+        self.length = end
+
+    def attend(self, Q_new, causal=True):
+        q_len = Q_new.shape[2]
+        return decode(Q_new, self.length - q_len, self.K, self.V, self.K_repr, causal,
+                      self.block_size, self.top_k)

@@ -62,6 +62,9 @@ static Shape make_shape(const bsa_problem* p, int units) {
   s.k = p->top_k;
   s.causal = p->causal;
   s.scale = p->scale > 0.f ? p->scale : 1.0f / sqrtf((float)p->head_dim);
+  s.Nq = s.N;
+  s.q0 = 0;
+  s.kv = s.N;
   return s;
 }
 
@@ -347,6 +350,62 @@ int bsa_pool_k(const bsa_problem* p, const void* K, float* K_repr, void* K_split
   __nv_bfloat16* lo = hi ? hi + (size_t)s.units * s.nb * s.D : nullptr;
   cudaError_t e = launch_pool_k((const __nv_bfloat16*)K, K_repr, hi, lo, s, (cudaStream_t)stream);
   return e == cudaSuccess ? BSA_OK : cuda_fail(e, "pool_k launch");
+}
+
+int bsa_pool_k_blocks(const bsa_problem* p, const void* K, float* K_repr, void* K_split,
+                      int block_begin, int block_end, int kv_len, void* stream) {
+  g_last_error.clear();
+  int st = check(p);
+  if (st != BSA_OK) return st;
+  if (kv_len < 0 || kv_len > p->seq_len)
+    return fail(BSA_ERR_INVALID, "kv_len %d outside [0, %d]", kv_len, p->seq_len);
+  const int nb_kv = (kv_len + p->block_size - 1) / p->block_size;
+  if (block_begin < 0 || block_begin > block_end || block_end > nb_kv)
+    return fail(BSA_ERR_INVALID, "block range [%d, %d) outside the %d blocks holding keys",
+                block_begin, block_end, nb_kv);
+  if (!aligned16(K) || !aligned16(K_repr) || !aligned16(K_split))
+    return fail(BSA_ERR_ALIGNMENT, "K, K_repr and K_split must be 16-byte aligned");
+  Shape s = make_shape(p, (int)total_units(p));
+  s.kv = kv_len;
+  __nv_bfloat16* hi = (__nv_bfloat16*)K_split;
+  __nv_bfloat16* lo = hi ? hi + (size_t)s.units * s.nb * s.D : nullptr;
+  cudaError_t e = launch_pool_k((const __nv_bfloat16*)K, K_repr, hi, lo, s, (cudaStream_t)stream,
+                                nullptr, 0, block_begin, block_end);
+  return e == cudaSuccess ? BSA_OK : cuda_fail(e, "pool_k launch");
+}
+
+size_t bsa_decode_workspace_bytes(const bsa_problem* p, int q_len) {
+  if (check(p) != BSA_OK || q_len < 1) return 0;
+  return align256(sizeof(int32_t) * (size_t)total_units(p) * q_len * p->top_k);
+}
+
+int bsa_decode(const bsa_problem* p, const void* Q, int q_len, int q_pos, const void* K,
+               const void* V, const float* K_repr, void* O, void* workspace,
+               size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  int st = check(p);
+  if (st != BSA_OK) return st;
+  if (q_len < 1 || q_pos < 0 || (int64_t)q_pos + q_len > p->seq_len)
+    return fail(BSA_ERR_INVALID, "new rows [%d, %d) outside the cache of %d", q_pos,
+                q_pos + q_len, p->seq_len);
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(K_repr) || !aligned16(O) ||
+      !aligned16(workspace))
+    return fail(BSA_ERR_ALIGNMENT, "Q, K, V, K_repr, O and workspace must be 16-byte aligned");
+  const size_t need = bsa_decode_workspace_bytes(p, q_len);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(BSA_ERR_WORKSPACE, "decode needs %zu bytes of workspace, got %zu", need,
+                workspace_bytes);
+  Shape s = make_shape(p, (int)total_units(p));
+  s.Nq = q_len;
+  s.q0 = q_pos;
+  s.kv = q_pos + q_len;
+  int32_t* idx = (int32_t*)workspace;
+  cudaStream_t s_ = (cudaStream_t)stream;
+  cudaError_t e = launch_decode_select((const __nv_bfloat16*)Q, K_repr, idx, s, s_);
+  if (e != cudaSuccess) return cuda_fail(e, "decode select launch");
+  e = launch_fine_simt((const __nv_bfloat16*)Q, (const __nv_bfloat16*)K, (const __nv_bfloat16*)V,
+                       idx, (__nv_bfloat16*)O, s, s_);
+  return e == cudaSuccess ? BSA_OK : cuda_fail(e, "decode fine launch");
 }
 
 int bsa_select_blocks(const bsa_problem* p, const void* Q, const float* K_repr,

@@ -51,13 +51,20 @@ constexpr float kLog2e = 1.4426950408889634f;
 // Problem shape derived once on the host and passed by value to kernels.
 struct Shape {
   int32_t units;       // batch * heads processed by this launch
-  int32_t N;           // seq_len
+  int32_t N;           // seq_len (of K and V; for decode, the cache capacity)
   int32_t D;           // head_dim
   int32_t bs;          // block_size
   int32_t nb;          // N / bs
   int32_t k;           // top_k
   int32_t causal;
   float scale;
+  // Query rows and the valid key prefix.  The full forward has Nq = N,
+  // q0 = 0, kv = N; decode has Nq new rows at positions q0 .. q0 + Nq - 1
+  // against the first kv = q0 + Nq keys.  Only the CUDA-core kernels and the
+  // decode selection read these; the tensor-core kernels run full forwards.
+  int32_t Nq;          // query rows per unit (Q, O and idx unit stride)
+  int32_t q0;          // position of query row 0
+  int32_t kv;          // keys [0, kv) exist
 };
 
 }  // namespace bsa

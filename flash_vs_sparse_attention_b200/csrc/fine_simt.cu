@@ -7,7 +7,9 @@
 // 16-byte-vector dot product, the warp folds the 32 scores into an online
 // softmax (running max / sum, FA2 rescaling), and every lane accumulates
 // D/32 output dims from the block's V rows (coalesced across lanes).  Output
-// is acc / l rounded to bf16 (round-to-nearest-even).
+// is acc / l rounded to bf16 (round-to-nearest-even).  Query row r of a unit
+// sits at position s.q0 + r and sees keys below s.kv (the full forward: row
+// r at position r, all N keys; decode: new rows against a cache prefix).
 #include "common.cuh"
 
 namespace bsa {
@@ -21,9 +23,9 @@ fine_simt_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __res
   const int wib = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t gw = (int64_t)blockIdx.x * 8 + wib;
-  if (gw >= (int64_t)s.units * s.N) return;
-  const int64_t unit = gw / s.N;
-  const int row = (int)(gw % s.N);
+  if (gw >= (int64_t)s.units * s.Nq) return;
+  const int64_t unit = gw / s.Nq;
+  const int row = s.q0 + (int)(gw % s.Nq);   // the query's position
   const __nv_bfloat16* q = Q + gw * s.D;
   for (int d = lane; d < s.D; d += 32) qs[wib][d] = __bfloat162float(q[d]);
   __syncwarp();
@@ -44,9 +46,9 @@ fine_simt_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __res
     if (j < 0) continue;
     for (int kc = 0; kc < s.bs; kc += 32) {
       const int64_t key0 = (int64_t)j * s.bs + kc;
-      if (s.causal && key0 > row) break;  // every later key is masked too
+      if ((s.causal && key0 > row) || key0 >= s.kv) break;  // every later key is masked too
       const int key = (int)key0 + lane;
-      const bool valid = (kc + lane < s.bs) && (!s.causal || key <= row);
+      const bool valid = (kc + lane < s.bs) && key < s.kv && (!s.causal || key <= row);
       float sc = -INFINITY;
       if (valid) {
         const uint4* kr = reinterpret_cast<const uint4*>(Ku + (int64_t)key * s.D);
@@ -68,7 +70,7 @@ fine_simt_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __res
       l = l * corr + warp_sum(p);
 #pragma unroll
       for (int i = 0; i < DPL; ++i) acc[i] *= corr;
-      const int nk = min(32, s.bs - kc);
+      const int nk = (int)min((int64_t)min(32, s.bs - kc), (int64_t)s.kv - key0);
       for (int tk = 0; tk < nk; ++tk) {
         const float pt = __shfl_sync(0xffffffffu, p, tk);
         if (pt != 0.f) {
@@ -95,7 +97,7 @@ fine_simt_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __res
 cudaError_t launch_fine_simt(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                              const __nv_bfloat16* V, const int32_t* idx, __nv_bfloat16* O,
                              const Shape& s, cudaStream_t st) {
-  const int64_t warps = (int64_t)s.units * s.N;
+  const int64_t warps = (int64_t)s.units * s.Nq;
   const unsigned blocks = (unsigned)((warps + 7) / 8);
   if (s.D <= 32) fine_simt_kernel<1><<<blocks, 256, 0, st>>>(Q, K, V, idx, O, s);
   else if (s.D <= 64) fine_simt_kernel<2><<<blocks, 256, 0, st>>>(Q, K, V, idx, O, s);

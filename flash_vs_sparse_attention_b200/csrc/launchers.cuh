@@ -5,13 +5,15 @@
 
 namespace bsa {
 
-// Stage 1 (pool.cu).
+// Stage 1 (pool.cu): blocks [block_begin, block_end) of every unit (end < 0:
+// all nb), each the mean of its keys below s.kv.
 // `zero`/`zero_bytes` (optional): a 16-byte-aligned region the kernel clears
 // on the way (the fine stage's error word and work-item counter), saving a
 // memset launch.
 cudaError_t launch_pool_k(const __nv_bfloat16* K, float* K_repr, __nv_bfloat16* K_hi,
                           __nv_bfloat16* K_lo, const Shape& s, cudaStream_t st,
-                          void* zero = nullptr, size_t zero_bytes = 0);
+                          void* zero = nullptr, size_t zero_bytes = 0, int block_begin = 0,
+                          int block_end = -1);
 
 // Stages 2-3 (select_simt.cu, select_tc.cu).
 cudaError_t launch_select_simt(const __nv_bfloat16* Q, const float* K_repr, int32_t* idx,
@@ -33,6 +35,11 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                            const __nv_bfloat16* V, const int32_t* idx, __nv_bfloat16* O,
                            unsigned char* ws, const Shape& s, cudaStream_t st, int* n_launches,
                            void* const* events, int n_events, bool pre_zeroed);
+
+// Decode (decode.cu): per new query row, the top-k cached blocks (a warp per
+// row; exact top-k, lowest index on ties, ascending order, -1 padded).
+cudaError_t launch_decode_select(const __nv_bfloat16* Q, const float* K_repr, int32_t* idx,
+                                 const Shape& s, cudaStream_t st);
 
 // Dispatchers (dispatch.cu).
 bool select_uses_tensor_cores(const Shape& s, uint32_t flags);

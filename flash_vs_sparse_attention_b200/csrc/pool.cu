@@ -3,7 +3,10 @@
 // One warp per (unit, block).  The warp reads the block's bs x D bf16 keys as
 // 16-byte vectors (8 bf16 per lane, a full 128-byte line per 8 lanes when
 // D = 64), so a block of 64 keys is 16 fully coalesced vector loads per lane.
-// Sums are fp32; the mean is sum / bs as torch's mean computes it.  Besides
+// Sums are fp32; the mean is sum / bs as torch's mean computes it.  For a
+// growing KV cache the kernel pools a range of blocks over the keys present
+// (s.kv of them): a block that is only partly filled is the mean of its
+// present keys, a full block exactly what the whole-sequence pass gives.  Besides
 // the fp32 means the kernel writes the split of mean * scale into two bf16
 // terms (hi = bf16(m), lo = bf16(m - hi)) for the tensor-core scorer, whose
 // bf16 MMAs then reproduce the scaled fp32 coarse scores to ~2^-17 relative.
@@ -16,7 +19,8 @@ namespace bsa {
 __global__ void __launch_bounds__(256)
 pool_k_kernel(const __nv_bfloat16* __restrict__ K, float* __restrict__ K_repr,
               __nv_bfloat16* __restrict__ K_hi, __nv_bfloat16* __restrict__ K_lo,
-              Shape s, int lanes_per_row, uint4* __restrict__ zero, int64_t zero_words) {
+              Shape s, int lanes_per_row, int block_begin, int n_blocks,
+              uint4* __restrict__ zero, int64_t zero_words) {
   {
     const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < zero_words; i += nthreads)
@@ -24,7 +28,7 @@ pool_k_kernel(const __nv_bfloat16* __restrict__ K, float* __restrict__ K_repr,
   }
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t total = (int64_t)s.units * s.nb;
+  const int64_t total = (int64_t)s.units * n_blocks;
   if (warp >= total) return;
   const int chunks = s.D >> 3;                 // 16-byte chunks per key row
   const int rows_per_iter = 32 / lanes_per_row;
@@ -32,9 +36,11 @@ pool_k_kernel(const __nv_bfloat16* __restrict__ K, float* __restrict__ K_repr,
   const int c = lane % lanes_per_row;          // chunk within the row
   const bool active = c < chunks;
 
-  const int64_t unit = warp / s.nb;
-  const int64_t blk = warp % s.nb;
+  const int64_t unit = warp / n_blocks;
+  const int64_t blk = block_begin + warp % n_blocks;
   const uint4* src = reinterpret_cast<const uint4*>(K + (unit * s.N + blk * s.bs) * (int64_t)s.D);
+  // Keys of this block that exist (all bs of them outside a growing cache).
+  const int rows = (int)min((int64_t)s.bs, (int64_t)s.kv - blk * s.bs);
 
   float acc[8];
 #pragma unroll
@@ -43,12 +49,12 @@ pool_k_kernel(const __nv_bfloat16* __restrict__ K, float* __restrict__ K_repr,
   if (active) {
     // Batches of 16 loads issued before any is summed (a whole 64-key block
     // per batch at head_dim 64): one memory round trip per batch.
-    for (int r0 = g; r0 < s.bs; r0 += 16 * rows_per_iter) {
+    for (int r0 = g; r0 < rows; r0 += 16 * rows_per_iter) {
       uint4 v[16];
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
         const int r = r0 + q * rows_per_iter;
-        v[q] = r < s.bs ? __ldg(src + (int64_t)r * chunks + c) : make_uint4(0u, 0u, 0u, 0u);
+        v[q] = r < rows ? __ldg(src + (int64_t)r * chunks + c) : make_uint4(0u, 0u, 0u, 0u);
       }
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
@@ -65,7 +71,7 @@ pool_k_kernel(const __nv_bfloat16* __restrict__ K, float* __restrict__ K_repr,
     for (int i = 0; i < 8; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
   }
   if (g == 0 && active) {
-    const float den = (float)s.bs;
+    const float den = (float)rows;
     float m[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) m[i] = acc[i] / den;
@@ -93,15 +99,19 @@ pool_k_kernel(const __nv_bfloat16* __restrict__ K, float* __restrict__ K_repr,
 
 cudaError_t launch_pool_k(const __nv_bfloat16* K, float* K_repr, __nv_bfloat16* K_hi,
                           __nv_bfloat16* K_lo, const Shape& s, cudaStream_t st, void* zero,
-                          size_t zero_bytes) {
+                          size_t zero_bytes, int block_begin, int block_end) {
   int chunks = s.D >> 3;
   int lpr = 1;
   while (lpr < chunks) lpr <<= 1;
-  const int64_t warps = (int64_t)s.units * s.nb;
+  const int end = block_end < 0 ? s.nb : block_end;
+  const int n_blocks = end - block_begin;
+  if (n_blocks <= 0) return cudaSuccess;   // (the whole-sequence pass always has blocks)
+  const int64_t warps = (int64_t)s.units * n_blocks;
   const int threads = 256;
   const int64_t blocks = (warps * 32 + threads - 1) / threads;
-  pool_k_kernel<<<(unsigned)blocks, threads, 0, st>>>(K, K_repr, K_hi, K_lo, s, lpr,
-                                                       (uint4*)zero, (int64_t)(zero_bytes / 16));
+  pool_k_kernel<<<(unsigned)blocks, threads, 0, st>>>(K, K_repr, K_hi, K_lo, s, lpr, block_begin,
+                                                       n_blocks, (uint4*)zero,
+                                                       (int64_t)(zero_bytes / 16));
   return cudaGetLastError();
 }
 

@@ -118,6 +118,36 @@ int bsa_forward_host(const bsa_problem* p, const void* Q_host, const void* K_hos
  * about 2^-17 relative) used by the tensor-core scorer. */
 int bsa_pool_k(const bsa_problem* p, const void* K, float* K_repr, void* K_split, void* stream);
 
+/* Decode-time reuse: the block means live beside a KV cache and grow with it.
+ * No counterpart in the reference (decode is its stated future work); these
+ * evaluate block_indexer.py:33-84 for new query rows against a cache.
+ *
+ * Incremental stage 1: p->seq_len is the cache capacity (a multiple of
+ * block_size) and K (B, H, capacity, D) holds keys [0, kv_len).  Pools
+ * blocks [block_begin, block_end) of every unit into K_repr (B*H, capacity /
+ * block_size, D) fp32 (and K_split as bsa_pool_k, or NULL); block_end is at
+ * most ceil(kv_len / block_size).  A block partly filled is the mean of its
+ * present keys; a full block is what bsa_pool_k writes. */
+int bsa_pool_k_blocks(const bsa_problem* p, const void* K, float* K_repr, void* K_split,
+                      int block_begin, int block_end, int kv_len, void* stream);
+
+/* Workspace bytes of bsa_decode for q_len new rows per unit. */
+size_t bsa_decode_workspace_bytes(const bsa_problem* p, int q_len);
+
+/* Attention of q_len new query rows per unit, at positions q_pos ..
+ * q_pos + q_len - 1, over the first kv_len = q_pos + q_len keys of the cache
+ * (K, V: (B, H, capacity, D) bf16, p->seq_len = capacity) with the cached
+ * block means K_repr (blocks up to ceil(kv_len / block_size) current, e.g.
+ * by bsa_pool_k_blocks).  Q, O: (B, H, q_len, D) bf16.  Causal rows see the
+ * blocks starting at or before their position and the keys up to it;
+ * non-causal rows see every cached key.  With kv_len a multiple of
+ * block_size, row r equals row q_pos + r of the whole-sequence forward over
+ * the first kv_len keys on the CUDA-core path (BSA_FLAG_SIMT_SELECT |
+ * BSA_FLAG_SIMT_FINE).  Runs on CUDA cores (a warp per new row). */
+int bsa_decode(const bsa_problem* p, const void* Q, int q_len, int q_pos, const void* K,
+               const void* V, const float* K_repr, void* O, void* workspace,
+               size_t workspace_bytes, void* stream);
+
 /* Stages 2-3 alone (block_indexer_triton.py:121-129, block_indexer.py:44-53):
  * writes idx (B*H, N, top_k) int32, each row's selected blocks in ascending
  * block order, then -1 in slots left empty because fewer than top_k blocks
