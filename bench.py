@@ -24,6 +24,13 @@ are quoted on).  Rank 0 prints one JSON line.
 ``--impl reference`` times the reference algorithm on the host cores (the
 oracle port of attention/block_indexer.py) on the same workload and prints
 the same line with ``"impl": "reference"``.
+
+``--mode decode`` measures decode-time reuse instead (its own JSON line):
+one step appends one token per (batch, head) unit to a KV cache of the
+workload's shape that is nearly full, re-pools the block it lands in
+(``bsa_pool_k_blocks``) and attends the new row over the cache
+(``bsa_decode``); ``value`` is milliseconds per step, with the roofline of
+the step's HBM bytes and the decode oracle timed on the host beside it.
 """
 
 from __future__ import annotations
@@ -437,6 +444,103 @@ def run_reference(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------
+DECODE_METRIC = "block-sparse decode step ms (1 new token per head, KV cache N=32k)"
+
+
+def run_decode(args, cfg):
+    """One step = append one token per unit to a cache of N keys (the step's K
+    and V rows copied in), re-pool the block it lands in, attend the new row
+    over the cache.  L2 is flushed before every step, outside the events."""
+    import numpy as np
+    import torch
+
+    from flash_vs_sparse_attention_b200 import _lib
+    from flash_vs_sparse_attention_b200 import block_indexer_b200 as bi
+
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        raise SystemExit("--mode decode runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    U, N, D, bs, k = cfg["B"] * cfg["H"], cfg["N"], cfg["D"], cfg["block_size"], cfg["top_k"]
+    n_new = args.warmup + args.steps
+    Q, K, V = gpu_inputs(cfg, U, seed=7, device=dev)       # positions [0, N)
+    start = N - n_new                                      # cache length before the first step
+    L = _lib.lib()
+    p = bi.problem(1, U, N, D, True, bs, k)
+    K_repr = torch.zeros(1, U, N // bs, D, dtype=torch.float32, device=dev)
+    Kc, Vc = torch.zeros_like(K), torch.zeros_like(V)
+    Kc[:, :, :start], Vc[:, :, :start] = K[:, :, :start], V[:, :, :start]
+    bi.pool_k_blocks(Kc, K_repr, 0, -(-start // bs), start, bs)
+    O = torch.empty(1, U, 1, D, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(L.bsa_decode_workspace_bytes(ctypes.byref(p), 1), dtype=torch.uint8, device=dev)
+    Qrows = [Q[:, :, t:t + 1].contiguous() for t in range(start, N)]
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    sp = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+    def step(i):
+        t = start + i
+        Kc[:, :, t] = K[:, :, t]
+        Vc[:, :, t] = V[:, :, t]
+        _lib.check(L.bsa_pool_k_blocks(ctypes.byref(p), bi._ptr(Kc), bi._ptr(K_repr), None,
+                                       t // bs, t // bs + 1, t + 1, sp), "bsa_pool_k_blocks")
+        _lib.check(L.bsa_decode(ctypes.byref(p), bi._ptr(Qrows[i]), 1, t, bi._ptr(Kc), bi._ptr(Vc),
+                                bi._ptr(K_repr), bi._ptr(O), bi._ptr(ws), ctypes.c_size_t(ws.numel()),
+                                sp), "bsa_decode")
+
+    for i in range(args.warmup):
+        flush.zero_()
+        step(i)
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(0) as clk:
+        for j in range(args.steps):
+            flush.zero_()
+            starts[j].record()
+            step(args.warmup + j)
+            ends[j].record()
+        torch.cuda.synchronize()
+    ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    ms_step = sum(ms) / len(ms)
+    # HBM bytes a step must move: the visible block means (fp32), the top_k
+    # selected blocks' K and V, the new row's Q, K, V in and O out, and the
+    # re-pooled block (its keys in, its mean out).
+    nbv = N // bs
+    step_bytes = U * (nbv * D * 4 + k * bs * D * 2 * 2 + 4 * D * 2 + bs * D * 2 + D * 4)
+    peaks, peak_kind = load_peaks()
+    achieved = step_bytes / (ms_step * 1e-3) / 1e9
+    # The decode oracle on the host for one step (all units, 1 thread).
+    from oracle import decode_rows
+    Qn, Kn, Vn = (t[0].float().cpu().numpy() for t in (Q, K, V))
+    t_last = N - 1
+    t0 = time.perf_counter()
+    for u in range(U):
+        decode_rows(Qn[u, t_last:t_last + 1], t_last, Kn[u], Vn[u], True, bs, k)
+    cpu_ms = (time.perf_counter() - t0) * 1e3
+    line = {
+        "metric": DECODE_METRIC, "value": round(ms_step, 5), "unit": "ms", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": f"decode step {workload_name(cfg)}: 1 new row per unit, cache of "
+                               f"{start}..{N - 1} keys", "units": U,
+                   "l2": f"flushed before every step ({L2_FLUSH_BYTES >> 20} MiB write, outside the events)"},
+        "tokens_per_s": round(U / (ms_step * 1e-3), 1),
+        "roofline": {"kernel": "decode step (pool_k_blocks + decode select + fine)", "bound": "hbm",
+                     "achieved": round(achieved, 2), "peak": float(peaks["hbm_gbs"]), "unit": "GB/s",
+                     "frac": round(achieved / float(peaks["hbm_gbs"]), 5),
+                     "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
+                     "bytes_per_step": step_bytes,
+                     "note": "three dependent launches per step; at a few MB the step is launch-latency bound"},
+        "clocks": clk.summary(), "gpu_launches": 3 * args.steps,
+        "cpu_baseline": {"value": round(cpu_ms, 3), "unit": "ms", "cores": 1, "kind": "port",
+                         "sample": f"one decode step of all {U} units (the last position) through the "
+                                   "numpy decode oracle, 1 thread"},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -449,11 +553,15 @@ def main(argv=None):
     ap.add_argument("--cpu-rows", type=int, default=16384, help="query rows in the CPU sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", default="forward", choices=["forward", "decode"],
+                    help="decode: one-token decode steps over a KV cache (its own JSON line)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
     cfg = WORKLOADS[args.config]
-    if args.impl == "reference":
+    if args.mode == "decode":
+        run_decode(args, cfg)
+    elif args.impl == "reference":
         run_reference(args, cfg)
     else:
         run_ours(args, cfg)

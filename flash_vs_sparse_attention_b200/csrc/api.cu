@@ -403,8 +403,12 @@ int bsa_decode(const bsa_problem* p, const void* Q, int q_len, int q_pos, const 
   cudaStream_t s_ = (cudaStream_t)stream;
   cudaError_t e = launch_decode_select((const __nv_bfloat16*)Q, K_repr, idx, s, s_);
   if (e != cudaSuccess) return cuda_fail(e, "decode select launch");
-  e = launch_fine_simt((const __nv_bfloat16*)Q, (const __nv_bfloat16*)K, (const __nv_bfloat16*)V,
-                       idx, (__nv_bfloat16*)O, s, s_);
+  if (decode_fine_supported(s))
+    e = launch_decode_fine((const __nv_bfloat16*)Q, (const __nv_bfloat16*)K,
+                           (const __nv_bfloat16*)V, idx, (__nv_bfloat16*)O, s, s_);
+  else
+    e = launch_fine_simt((const __nv_bfloat16*)Q, (const __nv_bfloat16*)K,
+                         (const __nv_bfloat16*)V, idx, (__nv_bfloat16*)O, s, s_);
   return e == cudaSuccess ? BSA_OK : cuda_fail(e, "decode fine launch");
 }
 

@@ -40,6 +40,12 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
 // row; exact top-k, lowest index on ties, ascending order, -1 padded).
 cudaError_t launch_decode_select(const __nv_bfloat16* Q, const float* K_repr, int32_t* idx,
                                  const Shape& s, cudaStream_t st);
+// Decode fine stage, a CTA per new row split over its selected blocks
+// (block_size 32/64/128, head_dim 64/128; decode_fine_supported).
+bool decode_fine_supported(const Shape& s);
+cudaError_t launch_decode_fine(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                               const __nv_bfloat16* V, const int32_t* idx, __nv_bfloat16* O,
+                               const Shape& s, cudaStream_t st);
 
 // Dispatchers (dispatch.cu).
 bool select_uses_tensor_cores(const Shape& s, uint32_t flags);

@@ -83,20 +83,27 @@ def test_pool_k_blocks_matches_whole_pool_and_partial_means(cuda):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("q_len,causal", [(1, True), (37, True), (64, False), (5, False)])
-def test_decode_rows_equal_the_whole_sequence_cuda_core_rows(cuda, q_len, causal):
-    """kv_len a multiple of block_size: decode row r is bit-identical to row
-    q_pos + r of the whole-sequence forward over the first kv_len keys on the
-    CUDA-core path (same scores, same selection, same fine arithmetic)."""
+def test_decode_rows_match_the_whole_sequence_rows(cuda, q_len, causal):
+    """kv_len a multiple of block_size: decode row r selects exactly the blocks
+    the whole-sequence CUDA-core selection picks for row q_pos + r (same fp32
+    scores, same tie rule), and its output matches that forward's row (the
+    decode fine stage splits the blocks over warps, so the fp32 sums
+    associate differently)."""
     B, H, cap, D, bs, k = 1, 2, 4096, 64, 64, 16
     kv_len = 3072
     q_pos = kv_len - q_len
     Q, K, V = (torch.from_numpy(_rand((B, H, cap, D), s)).to(cuda, torch.bfloat16) for s in (6, 7, 8))
     K_repr, _ = bi.pool_k(K, bs)
-    got = bi.decode(Q[:, :, q_pos:kv_len], q_pos, K, V, K_repr, causal, bs, k)
-    whole = bi.attention(Q[:, :, :kv_len].contiguous(), K[:, :, :kv_len].contiguous(),
-                         V[:, :, :kv_len].contiguous(), causal=causal, block_size=bs, top_k=k,
-                         flags=SIMT)
-    assert torch.equal(got, whole[:, :, q_pos:kv_len])
+    got, idx = bi.decode(Q[:, :, q_pos:kv_len], q_pos, K, V, K_repr, causal, bs, k,
+                         return_indices=True)
+    head = [t[:, :, :kv_len].contiguous() for t in (Q, K, V)]
+    whole_idx = bi.select_blocks(head[0], head[1], causal=causal, block_size=bs, top_k=k,
+                                 flags=_lib.BSA_FLAG_SIMT_SELECT)
+    assert torch.equal(idx, whole_idx[:, :, q_pos:kv_len])
+    whole = bi.attention(*head, causal=causal, block_size=bs, top_k=k, flags=SIMT)
+    for u in range(H):
+        assert_close_out(got[0, u].float().cpu().numpy(),
+                         whole[0, u, q_pos:kv_len].float().cpu().numpy(), f"unit {u}")
 
 
 @pytest.mark.gpu
@@ -105,6 +112,8 @@ def test_decode_rows_equal_the_whole_sequence_cuda_core_rows(cuda, q_len, causal
     (2000, 24, True, 64, 16),    # a chunk of new rows reaching into the partial block
     (777, 9, False, 32, 8),      # non-causal, smaller blocks
     (300, 3, True, 64, 16),      # fewer cached blocks (5) than top_k: empty slots
+    (500, 4, True, 16, 8),       # block_size 16: the general CUDA-core fine kernel
+    (1500, 2, True, 128, 8),     # block_size 128
 ])
 def test_decode_matches_the_decode_oracle(cuda, kv_len, q_len, causal, bs, k):
     B, H, cap, D = 1, 2, 2048, 64
