@@ -23,6 +23,7 @@ BSA_ERR_CUDA = 5
 
 BSA_FLAG_SIMT_SELECT = 1
 BSA_FLAG_SIMT_FINE = 2
+BSA_FLAG_QBLOCK = 4
 
 # Every function include/bsattn.h declares, with its ctypes signature.
 _c = ctypes

@@ -118,6 +118,18 @@ def attention(Q, K, V, causal=False, block_size=64, top_k=16, *, flags=0,
     return O
 
 
+def attention_qblock(Q, K, V, causal=False, block_size=64, top_k=16, *, flags=0,
+                     workspace_cap=DEFAULT_WORKSPACE_CAP, check_errors=False):
+    """Per-query-block selection, a labelled variant (not the reference's
+    per-token semantics): Q is mean-pooled per block like K; each query block
+    of ``block_size`` rows takes the ``top_k`` key blocks of its pooled score
+    (causal: blocks up to its own, ties to the lower index); every query of
+    the block attends to those blocks' keys with the usual token-level causal
+    mask.  Same signature and layout as ``attention``."""
+    return attention(Q, K, V, causal, block_size, top_k, flags=flags | _lib.BSA_FLAG_QBLOCK,
+                     workspace_cap=workspace_cap, check_errors=check_errors)
+
+
 def attention_from_host(Q, K, V, causal=False, block_size=64, top_k=16, *, device=None,
                         out=None, units_per_chunk=None, flags=0):
     """``attention`` for inputs in host memory, returning host memory.

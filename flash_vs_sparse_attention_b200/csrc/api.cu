@@ -77,6 +77,7 @@ static bool aligned16(const void* ptr) { return ((uintptr_t)ptr & 15u) == 0; }
 struct Layout {
   size_t krepr, khi, klo, idx, fine, total;
   size_t fine_bytes;
+  size_t qrepr, bidx;   // BSA_FLAG_QBLOCK only: Q block means, per-block picks
 };
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -89,6 +90,11 @@ static Layout layout_for(const bsa_problem* p, int64_t units) {
   L.khi = off;   off = align256(off + 2 * (size_t)units * s.nb * s.D);
   L.klo = off;   off = align256(off + 2 * (size_t)units * s.nb * s.D);
   L.idx = off;   off = align256(off + sizeof(int32_t) * (size_t)units * s.N * s.k);
+  L.qrepr = L.bidx = 0;
+  if (p->flags & BSA_FLAG_QBLOCK) {
+    L.qrepr = off; off = align256(off + sizeof(float) * units * s.nb * s.D);
+    L.bidx = off;  off = align256(off + sizeof(int32_t) * (size_t)units * s.nb * s.k);
+  }
   L.fine_bytes = fine_workspace_bytes(s, p->flags);
   L.fine = off;  off = align256(off + L.fine_bytes);
   L.total = off;
@@ -238,12 +244,26 @@ int bsa_forward_ex(const bsa_problem* p, const void* Q, const void* K, const voi
     void* zero = kv ? (void*)(ws + L.fine) : nullptr;
     const size_t zero_bytes = kv ? fine_kv_zero_bytes(s) : 0;
     uint32_t* err = kv ? (uint32_t*)(ws + L.fine + fine_kv_error_offset(s)) : nullptr;
-    cudaError_t e = launch_pool_k(k, krepr, khi, klo, s, s_, zero, zero_bytes);
+    const bool qblock = (p->flags & BSA_FLAG_QBLOCK) != 0;
+    cudaError_t e;
+    if (qblock) {   // Q block means too (no bf16 split: the block scorer is fp32)
+      e = launch_pool_k(q, (float*)(ws + L.qrepr), nullptr, nullptr, s, s_);
+      if (e != cudaSuccess) return cuda_fail(e, "pool_q launch");
+      ++launches;
+    }
+    e = launch_pool_k(k, krepr, qblock ? nullptr : khi, qblock ? nullptr : klo, s, s_, zero,
+                      zero_bytes);
     if (e != cudaSuccess) return cuda_fail(e, "pool_k launch");
     ++launches;
     mark(0);
     int nl = 0;
-    e = launch_select(q, krepr, khi, klo, idx, err, s, p->flags, s_, &nl);
+    if (qblock) {
+      e = launch_qblock_select((const float*)(ws + L.qrepr), krepr, (int32_t*)(ws + L.bidx), idx,
+                               s, s_);
+      nl = 2;
+    } else {
+      e = launch_select(q, krepr, khi, klo, idx, err, s, p->flags, s_, &nl);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "select launch");
     launches += nl;
     mark(1);
@@ -419,6 +439,8 @@ int bsa_select_blocks(const bsa_problem* p, const void* Q, const float* K_repr,
   if (st != BSA_OK) return st;
   if (!aligned16(Q) || !aligned16(K_repr) || !aligned16(K_split) || !aligned16(idx))
     return fail(BSA_ERR_ALIGNMENT, "Q, K_repr, K_split and idx must be 16-byte aligned");
+  if (p->flags & BSA_FLAG_QBLOCK)
+    return fail(BSA_ERR_UNSUPPORTED, "per-query-block selection runs inside bsa_forward");
   Shape s = make_shape(p, (int)total_units(p));
   const __nv_bfloat16* hi = (const __nv_bfloat16*)K_split;
   const __nv_bfloat16* lo = hi ? hi + (size_t)s.units * s.nb * s.D : nullptr;

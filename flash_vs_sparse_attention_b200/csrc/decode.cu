@@ -26,8 +26,11 @@ namespace bsa {
 
 constexpr int kDecSelThreads = 256;
 
+// POOLED: the rows are per-query-block means (fp32, one per block; row r
+// stands for block r and sits at that block's last position).
+template <bool POOLED>
 __global__ void __launch_bounds__(kDecSelThreads)
-decode_select_kernel(const __nv_bfloat16* __restrict__ Q, const float* __restrict__ K_repr,
+decode_select_kernel(const void* __restrict__ Qv, const float* __restrict__ K_repr,
                      int32_t* __restrict__ idx, Shape s) {
   extern __shared__ __align__(16) float dsm[];
   float* qs = dsm;                       // head_dim
@@ -37,8 +40,11 @@ decode_select_kernel(const __nv_bfloat16* __restrict__ Q, const float* __restric
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t gr = blockIdx.x;         // unit * Nq + row
   const int64_t unit = gr / s.Nq;
-  const int pos = s.q0 + (int)(gr % s.Nq);
-  for (int d = tid; d < s.D; d += kDecSelThreads) qs[d] = __bfloat162float(Q[gr * s.D + d]);
+  const int r = (int)(gr % s.Nq);
+  const int pos = POOLED ? (r + 1) * s.bs - 1 : s.q0 + r;
+  for (int d = tid; d < s.D; d += kDecSelThreads)
+    qs[d] = POOLED ? reinterpret_cast<const float*>(Qv)[gr * s.D + d]
+                   : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(Qv)[gr * s.D + d]);
   __syncthreads();
   const int nb_kv = (s.kv + s.bs - 1) / s.bs;
   const int lim = s.causal ? min(nb_kv, pos / s.bs + 1) : nb_kv;   // eligible: [0, lim)
@@ -105,17 +111,55 @@ decode_select_kernel(const __nv_bfloat16* __restrict__ Q, const float* __restric
   }
 }
 
-cudaError_t launch_decode_select(const __nv_bfloat16* Q, const float* K_repr, int32_t* idx,
-                                 const Shape& s, cudaStream_t st) {
+template <bool POOLED>
+static cudaError_t launch_select_rows(const void* Q, const float* K_repr, int32_t* idx,
+                                      const Shape& s, cudaStream_t st) {
   const size_t smem = sizeof(float) * ((size_t)s.D + s.nb) + sizeof(int32_t) * s.k;
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(decode_select_kernel,
+    cudaError_t e = cudaFuncSetAttribute(decode_select_kernel<POOLED>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
   const int64_t rows = (int64_t)s.units * s.Nq;
   if (rows == 0) return cudaSuccess;
-  decode_select_kernel<<<(unsigned)rows, kDecSelThreads, smem, st>>>(Q, K_repr, idx, s);
+  decode_select_kernel<POOLED><<<(unsigned)rows, kDecSelThreads, smem, st>>>(Q, K_repr, idx, s);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_decode_select(const __nv_bfloat16* Q, const float* K_repr, int32_t* idx,
+                                 const Shape& s, cudaStream_t st) {
+  return launch_select_rows<false>(Q, K_repr, idx, s, st);
+}
+
+// Per-query-block selection: block i of every unit (its pooled row Q_repr)
+// picks the top-k key blocks j <= i (causal) or of all blocks; then every
+// query row of block i gets block i's picks.
+__global__ void __launch_bounds__(256)
+expand_block_selection_kernel(const int32_t* __restrict__ bidx, int32_t* __restrict__ idx,
+                              Shape s) {
+  const int64_t total = (int64_t)s.units * s.N * s.k;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = e / s.k;          // unit * N + r
+    const int slot = (int)(e % s.k);
+    const int64_t unit = row / s.N;
+    const int blk = (int)(row % s.N) / s.bs;
+    idx[e] = bidx[(unit * s.nb + blk) * s.k + slot];
+  }
+}
+
+cudaError_t launch_qblock_select(const float* Q_repr, const float* K_repr, int32_t* bidx,
+                                 int32_t* idx, const Shape& s, cudaStream_t st) {
+  Shape sb = s;
+  sb.Nq = s.nb;     // one pooled row per query block
+  sb.q0 = 0;
+  sb.kv = s.N;
+  cudaError_t e = launch_select_rows<true>(Q_repr, K_repr, bidx, sb, st);
+  if (e != cudaSuccess) return e;
+  const int64_t total = (int64_t)s.units * s.N * s.k;
+  const int64_t blocks = (total + 255) / 256;
+  expand_block_selection_kernel<<<(unsigned)(blocks < 148 * 64 ? blocks : 148 * 64), 256, 0, st>>>(
+      bidx, idx, s);
   return cudaGetLastError();
 }
 

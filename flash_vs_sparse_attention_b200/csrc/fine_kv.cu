@@ -390,17 +390,20 @@ bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict
 // ---------------------------------------------------------------------------
 // 4. The tensor-core fine kernel.
 //
-// Warps (NWG = 3 softmax warpgroups when TMEM holds three (S, O) pairs, else 2):
+// Warps (NWG = 3 softmax warpgroups when TMEM holds three (S, P, O) sets,
+// else 2):
 //   0 .. 4*NWG-1  warpgroup w takes the items t with t % NWG == w and owns
-//                 TMEM columns S[w] (P overwrites them as bf16 pairs) and
-//                 O[w].  Per item: softmax of S(t) into P(t); the group's
-//                 first warp then issues PV(t) and, right behind it,
-//                 S(t + NWG) for the group's next item, so the tensor core
-//                 works on the next tile while the group writes this one's
-//                 output.  Each warp stores its own 32 output rows.  Each warpgroup issues its own MMAs: one thread's
-//                 chain of commit-and-wait steps is latency-bound (~500
-//                 cycles per commit at these tile sizes), and independent
-//                 issuers overlap.
+//                 separate TMEM columns S[w], P[w] (bf16 pairs) and O[w].
+//                 Per item: S(t) into registers (its columns are then free,
+//                 and the group's third warp issues S(t + NWG) at once if its
+//                 queries and K/V are already there), P(t) into the P
+//                 columns once PV(t - NWG) is done, the epilogue of item
+//                 t - NWG (each warp stores its own 32 output rows), then the
+//                 group's first warp issues PV(t), which runs while the group
+//                 works on its next item.  Each warpgroup issues its own
+//                 MMAs: one thread's chain of commit-and-wait steps is
+//                 latency-bound (~500 cycles per commit at these tile
+//                 sizes), and independent issuers overlap.
 //   4*NWG .. +NG-1  NG gather warps, item t to warp t % NG: one bulk copy
 //                 brings the item's list slice (query rows) into a small
 //                 per-warp ring two of the warp's items ahead; the warp then

@@ -40,6 +40,11 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
 // row; exact top-k, lowest index on ties, ascending order, -1 padded).
 cudaError_t launch_decode_select(const __nv_bfloat16* Q, const float* K_repr, int32_t* idx,
                                  const Shape& s, cudaStream_t st);
+// Per-query-block selection (BSA_FLAG_QBLOCK): Q_repr (units, nb, D) fp32
+// block means of Q; bidx (units, nb, k) the picks of each query block; idx
+// (units, N, k) those picks repeated for every row of the block.
+cudaError_t launch_qblock_select(const float* Q_repr, const float* K_repr, int32_t* bidx,
+                                 int32_t* idx, const Shape& s, cudaStream_t st);
 // Decode fine stage, a CTA per new row split over its selected blocks
 // (block_size 32/64/128, head_dim 64/128; decode_fine_supported).
 bool decode_fine_supported(const Shape& s);

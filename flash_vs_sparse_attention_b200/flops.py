@@ -14,6 +14,8 @@ counts exactly like ``block_indexer`` / ``block_indexer_triton``
 from __future__ import annotations
 
 SPARSE_VARIANTS = ("block_indexer", "block_indexer_triton", "block_indexer_b200")
+# This build's per-query-block selection variant (not in the reference).
+QBLOCK_VARIANT = "block_indexer_b200_qblock"
 
 
 def compute_flops(batch, heads, seq_len, head_dim, variant="dense", block_size=64, top_k=16):
@@ -28,6 +30,13 @@ def compute_flops(batch, heads, seq_len, head_dim, variant="dense", block_size=6
         return coarse + fine_matmul + fine_softmax
     if variant == "flex_attn":
         return 4 * B * H * N * top_k * block_size * D + 5 * B * H * N * top_k * block_size
+    if variant == QBLOCK_VARIANT:
+        # pooled scores per query block instead of per query token
+        nb = N // block_size
+        coarse = 2 * B * H * nb * nb * D
+        fine_matmul = 4 * B * H * N * top_k * block_size * D
+        fine_softmax = 5 * B * H * N * top_k * block_size
+        return coarse + fine_matmul + fine_softmax
     raise ValueError(f"Unknown variant: {variant}")
 
 
@@ -43,6 +52,9 @@ def compute_io_bytes(batch, heads, seq_len, head_dim, variant="naive", bytes_per
         return qkv + out
     if variant in SPARSE_VARIANTS:
         return qkv + 2 * B * H * N * (N // block_size) * e + out
+    if variant == QBLOCK_VARIANT:
+        nb = N // block_size
+        return qkv + 2 * B * H * nb * nb * e + out
     raise ValueError(f"Unknown variant: {variant}")
 
 

@@ -4,8 +4,10 @@ Mirrors ``benchmark/runner.py`` (its grid ``SEQ_LENS`` x causal, B=1 H=8
 D=64 bf16, ``runner.py:22-27``; its CSV columns, ``runner.py:29-35``; its
 timing protocol, ``benchmark/timer.py:21-43``: 10 warm-up calls, then 50
 calls each bracketed by CUDA events; its peak-memory reading,
-``benchmark/memory.py:4-16``) for the ``block_indexer_b200`` variant, and
-adds the columns the reference's CSV lacks:
+``benchmark/memory.py:4-16``) for the ``block_indexer_b200`` variant and
+its per-query-block selection variant ``block_indexer_b200_qblock`` (a
+labelled variant, not the reference's semantics), and adds the columns the
+reference's CSV lacks:
 
 * ``effective_tflops`` -- ``theoretical_flops`` (``flops.compute_flops``,
   the reference's FLOP model) / ``mean_ms``;
@@ -38,6 +40,9 @@ from . import block_indexer_b200, flops
 
 VARIANTS = {
     "block_indexer_b200": functools.partial(block_indexer_b200.attention, block_size=64, top_k=16),
+    # per-query-block selection: a labelled variant, not the reference's semantics
+    flops.QBLOCK_VARIANT: functools.partial(block_indexer_b200.attention_qblock, block_size=64,
+                                            top_k=16),
 }
 
 SEQ_LENS = [512, 1024, 2048, 4096, 8192, 16384, 32768]

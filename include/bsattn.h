@@ -46,6 +46,12 @@ typedef enum bsa_status {
 /* Implementation choices a caller may force (tests compare the two). */
 #define BSA_FLAG_SIMT_SELECT 1u  /* CUDA-core coarse scoring + top-k */
 #define BSA_FLAG_SIMT_FINE 2u    /* query-stationary CUDA-core fine stage */
+/* Per-query-block selection (not the reference's semantics; a labelled
+ * variant): Q is mean-pooled per block like K, each query block of
+ * block_size rows takes the top_k key blocks of its pooled score (causal:
+ * blocks j <= its own), and every query of the block attends to those
+ * blocks' keys (token-level causal mask as usual). */
+#define BSA_FLAG_QBLOCK 4u
 
 typedef struct bsa_problem {
   int32_t batch;       /* B */

@@ -22,4 +22,5 @@ from .block_indexer_np import (  # noqa: F401
     index_parity,
 )
 from .decode_np import decode_rows, pool_k_prefix  # noqa: F401
+from .qblock_np import qblock_attention_unit, qblock_scores  # noqa: F401
 from .inputs import CONFIGS, unit_inputs, make_inputs, round_to_bf16  # noqa: F401

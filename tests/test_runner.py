@@ -25,7 +25,8 @@ def test_csv_keeps_the_reference_columns_first():
 def test_without_a_gpu_the_row_records_the_variant_error(tmp_path):
     out = tmp_path / "sweep.csv"
     path, rows = runner.run(smoke=True, out=str(out))
-    assert len(rows) == 1 and "block_indexer_b200" in rows[0]["error"]
+    assert [r["variant"] for r in rows] == ["block_indexer_b200", "block_indexer_b200_qblock"]
+    assert all("block_indexer_b200" in r["error"] for r in rows)
     with open(path) as f:
         r = list(csv.DictReader(f))
     assert list(r[0].keys()) == runner.CSV_FIELDS
@@ -36,12 +37,12 @@ def test_without_a_gpu_the_row_records_the_variant_error(tmp_path):
 def test_sweep_rows_on_the_gpu(tmp_path):
     out = tmp_path / "sweep.csv"
     path, rows = runner.run(out=str(out), seq_lens=[512, 2048], n_warmup=2, n_trials=3)
-    assert len(rows) == 4
+    assert len(rows) == 8
     small = [r for r in rows if r["seq_len"] == 512]
     assert all("top_k" in r["error"] for r in small)          # 8 blocks < top_k 16
     for r in rows:
         if r["seq_len"] == 2048:
             assert not r.get("error")
             assert r["mean_ms"] > 0 and r["effective_tflops"] > 0 and r["hbm_gbs"] > 0
-            assert r["theoretical_flops"] == runner.flops.compute_flops(1, 8, 2048, 64, "block_indexer_b200")
+            assert r["theoretical_flops"] == runner.flops.compute_flops(1, 8, 2048, 64, r["variant"])
             assert r["peak_source"] == "nominal"
