@@ -109,8 +109,9 @@ static int64_t total_units(const bsa_problem* p) { return (int64_t)p->batch * p-
 // process, used under the device's mutex).
 static int64_t host_chunk_units(const bsa_problem* p, int64_t units_per_chunk) {
   const int64_t U = total_units(p);
-  // Default: four chunks (measured on the 8-unit headline workload: 2.39 ms
-  // end to end against 2.52 ms with eight chunks and 2.98 ms with one).
+  // Default: a quarter of the units per chunk (the 8-unit headline workload:
+  // chunks of 2, 2, 2, 1, 1 units, 2.33 ms end to end; one unit per chunk
+  // takes 2.53 ms).
   const int64_t g = units_per_chunk > 0 ? units_per_chunk : (U + 3) / 4;
   return g < U ? g : U;
 }
@@ -321,8 +322,17 @@ int bsa_forward_host(const bsa_problem* p, const void* Q_host, const void* K_hos
     if ((e = cudaStreamWaitEvent(s_, P.start, 0)) != cudaSuccess) return cuda_fail(e, "stream wait");
   const void* src[3] = {Q_host, K_host, V_host};
   int last = 0;
-  for (int64_t i = 0, u0 = 0; u0 < U; ++i, u0 += g) {
-    const int64_t gu = (U - u0) < g ? (U - u0) : g;
+  // Chunk sizes: g units each until g or fewer are left, then halving
+  // chunks (g=2: 2, 2, 2, 1, 1 for 8 units; g=4: 4, 2, 1, 1), so the
+  // pipeline drains -- the last forward and copy back, which nothing
+  // overlaps -- on a single unit.
+  auto chunk_units = [&](int64_t u0) {
+    const int64_t left = U - u0;
+    if (left > g) return g;
+    return left >= 2 ? (left + 1) / 2 : left;
+  };
+  for (int64_t i = 0, u0 = 0, gu = 0; u0 < U; ++i, u0 += gu) {
+    gu = chunk_units(u0);
     const int b = (int)(i & 1);
     const size_t off = (size_t)u0 * unit_bytes, bytes = (size_t)gu * unit_bytes;
     // Host -> device: buffer b is free once the forward of chunk i - 2 is done.
