@@ -56,7 +56,7 @@ constexpr int kRowBits = 14;   // staged entry: block << kRowBits | row in batch
 // Error codes ORed into the workspace error word.
 enum : uint32_t {
   kErrWaitQ = 1u, kErrWaitS = 2u, kErrWaitP = 4u, kErrWaitO = 8u, kErrWaitFree = 16u,
-  kErrWaitDrain = 32u, kErrWaitStaged = 64u, kErrWaitKV = 128u, kErrWaitEnt = 256u
+  kErrWaitDrain = 32u, kErrWaitKV = 128u, kErrWaitEnt = 256u
 };
 
 struct FineWs {

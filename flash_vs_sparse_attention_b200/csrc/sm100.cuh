@@ -90,19 +90,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// Gather four rows y0..y3 (box one row high, `box_x` elements wide starting
-// at x) into four consecutive smem rows.
-__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, uint64_t* bar,
-                                            int32_t x, int32_t y0, int32_t y1, int32_t y2,
-                                            int32_t y3) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y0), "r"(y1),
-      "r"(y2), "r"(y3)
-      : "memory");
-}
-
 // gather4 with an L2 eviction policy.
 __device__ __forceinline__ void tma_gather4_hint(void* dst, const CUtensorMap* map, uint64_t* bar,
                                                  int32_t x, int32_t y0, int32_t y1, int32_t y2,
@@ -190,27 +177,6 @@ __device__ __forceinline__ int ld_acquire_shared(const int* p) {
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
-// 16-byte global -> shared copy through the LSU (L1 bypass), completing
-// asynchronously; pair with cp_async_arrive_noinc.
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
-               : "memory");
-}
-
-// cp_async16 with an L2 eviction policy.
-__device__ __forceinline__ void cp_async16_hint(void* dst, const void* src, uint64_t policy) {
-  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)),
-               "l"(src), "l"(policy)
-               : "memory");
-}
-
-// Arrive on `bar` once every cp.async this thread issued so far has landed
-// (the arrival is pre-counted in the barrier's expected count).
-__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
 }
 
 // Non-blocking probe of an mbarrier phase.
@@ -342,21 +308,6 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
       "tcgen05.wait::ld.sync.aligned;"
       : BSA_R32(r, 0), BSA_R32(r, 32)
       : "r"(taddr), "r"(taddr + 32)
-      : "memory");
-}
-
-// Store 32 consecutive 32-bit columns of this warp's 32 TMEM lanes, then wait
-// until the stores are complete.
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n"
-      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
-      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
-      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
-      "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
 
