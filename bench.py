@@ -27,10 +27,10 @@ the same line with ``"impl": "reference"``.
 
 ``--mode decode`` measures decode-time reuse instead (its own JSON line):
 one step appends one token per (batch, head) unit to a KV cache of the
-workload's shape that is nearly full, re-pools the block it lands in
-(``bsa_pool_k_blocks``) and attends the new row over the cache
-(``bsa_decode``); ``value`` is milliseconds per step, with the roofline of
-the step's HBM bytes and the decode oracle timed on the host beside it.
+workload's shape that is nearly full, re-pools the block it lands in and
+attends the new row over the cache, all in one launch
+(``bsa_decode_step``); ``value`` is milliseconds per step, with the roofline
+of the step's HBM bytes and the decode oracle timed on the host beside it.
 """
 
 from __future__ import annotations
@@ -459,8 +459,9 @@ DECODE_METRIC = "block-sparse decode step ms (1 new token per head, KV cache N=3
 
 def run_decode(args, cfg):
     """One step = append one token per unit to a cache of N keys (the step's K
-    and V rows copied in), re-pool the block it lands in, attend the new row
-    over the cache.  L2 is flushed before every step, outside the events."""
+    and V rows written in), re-pool the block it lands in, attend the new row
+    over the cache: one bsa_decode_step launch.  L2 is flushed before every
+    step, outside the events."""
     import numpy as np
     import torch
 
@@ -482,20 +483,14 @@ def run_decode(args, cfg):
     Kc[:, :, :start], Vc[:, :, :start] = K[:, :, :start], V[:, :, :start]
     bi.pool_k_blocks(Kc, K_repr, 0, -(-start // bs), start, bs)
     O = torch.empty(1, U, 1, D, dtype=torch.bfloat16, device=dev)
-    ws = torch.empty(L.bsa_decode_workspace_bytes(ctypes.byref(p), 1), dtype=torch.uint8, device=dev)
-    Qrows = [Q[:, :, t:t + 1].contiguous() for t in range(start, N)]
+    rows = [[t_[:, :, t:t + 1].contiguous() for t in range(start, N)] for t_ in (Q, K, V)]
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     sp = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
 
     def step(i):
-        t = start + i
-        Kc[:, :, t] = K[:, :, t]
-        Vc[:, :, t] = V[:, :, t]
-        _lib.check(L.bsa_pool_k_blocks(ctypes.byref(p), bi._ptr(Kc), bi._ptr(K_repr), None,
-                                       t // bs, t // bs + 1, t + 1, sp), "bsa_pool_k_blocks")
-        _lib.check(L.bsa_decode(ctypes.byref(p), bi._ptr(Qrows[i]), 1, t, bi._ptr(Kc), bi._ptr(Vc),
-                                bi._ptr(K_repr), bi._ptr(O), bi._ptr(ws), ctypes.c_size_t(ws.numel()),
-                                sp), "bsa_decode")
+        _lib.check(L.bsa_decode_step(ctypes.byref(p), bi._ptr(rows[0][i]), bi._ptr(rows[1][i]),
+                                     bi._ptr(rows[2][i]), start + i, bi._ptr(Kc), bi._ptr(Vc),
+                                     bi._ptr(K_repr), bi._ptr(O), sp), "bsa_decode_step")
 
     for i in range(args.warmup):
         flush.zero_()
@@ -536,13 +531,13 @@ def run_decode(args, cfg):
                                f"{start}..{N - 1} keys", "units": U,
                    "l2": f"flushed before every step ({L2_FLUSH_BYTES >> 20} MiB write, outside the events)"},
         "tokens_per_s": round(U / (ms_step * 1e-3), 1),
-        "roofline": {"kernel": "decode step (pool_k_blocks + decode select + fine)", "bound": "hbm",
+        "roofline": {"kernel": "decode step (append, re-pool, select, attend: one launch)", "bound": "hbm",
                      "achieved": round(achieved, 2), "peak": float(peaks["hbm_gbs"]), "unit": "GB/s",
                      "frac": round(achieved / float(peaks["hbm_gbs"]), 5),
                      "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
                      "bytes_per_step": step_bytes,
-                     "note": "three dependent launches per step; at a few MB the step is launch-latency bound"},
-        "clocks": clk.summary(), "gpu_launches": 3 * args.steps,
+                     "note": "one launch of 8 CTAs per step; at a few MB the step is launch-latency bound"},
+        "clocks": clk.summary(), "gpu_launches": args.steps,
         "cpu_baseline": {"value": round(cpu_ms, 3), "unit": "ms", "cores": 1, "kind": "port",
                          "sample": f"one decode step of all {U} units (the last position) through the "
                                    "numpy decode oracle, 1 thread"},

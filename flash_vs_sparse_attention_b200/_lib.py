@@ -68,6 +68,7 @@ SIGNATURES = {
     "bsa_pool_k_blocks": (_c.c_int, [_PP, _P, _P, _P, _c.c_int, _c.c_int, _c.c_int, _P]),
     "bsa_decode_workspace_bytes": (_c.c_size_t, [_PP, _c.c_int]),
     "bsa_decode": (_c.c_int, [_PP, _P, _c.c_int, _c.c_int, _P, _P, _P, _P, _P, _c.c_size_t, _P]),
+    "bsa_decode_step": (_c.c_int, [_PP, _P, _P, _P, _c.c_int, _P, _P, _P, _P, _P]),
 }
 
 ABI_VERSION = 1

@@ -296,7 +296,8 @@ class DecodeCache:
 
     ``append(K_new, V_new)`` writes the new keys and values and re-pools only
     the blocks they touch; ``attend(Q_new)`` runs the new rows (the last
-    ``q_len`` positions) against everything cached so far.
+    ``q_len`` positions) against everything cached so far; ``step(q, k, v)``
+    does both for one token in a single launch.
     """
 
     def __init__(self, batch, heads, capacity, head_dim, block_size=64, top_k=16,
@@ -322,6 +323,31 @@ class DecodeCache:
         bs = self.block_size
         pool_k_blocks(self.K, self.K_repr, self.length // bs, -(-end // bs), end, bs)
         self.length = end
+
+    def step(self, q, k, v):
+        """Append one token (k, v: (B, H, 1, D) bf16) and attend its query row
+        q (B, H, 1, D) over the whole cache: one launch (``bsa_decode_step``)
+        where the shape allows, else ``append`` then ``attend``.  Returns
+        (B, H, 1, D) bf16."""
+        B, H, cap, D = self.K.shape
+        if k.shape != (B, H, 1, D) or v.shape != k.shape or q.shape != k.shape:
+            raise ValueError(f"{VARIANT}: step takes one (B, H, 1, D) row each of q, k, v")
+        if self.length >= cap:
+            raise ValueError(f"{VARIANT}: cache capacity {cap} exceeded")
+        if self.block_size not in (32, 64, 128) or D not in (64, 128):
+            self.append(k, v)
+            return self.attend(q)
+        L = _require_backend()
+        p = problem(B, H, cap, D, True, self.block_size, self.top_k)
+        qc, kc, vc = (t.contiguous() for t in (q, k, v))
+        with torch.cuda.device(self.K.device):
+            O = torch.empty_like(qc)
+            _lib.check(L.bsa_decode_step(ctypes.byref(p), _ptr(qc), _ptr(kc), _ptr(vc),
+                                         self.length, _ptr(self.K), _ptr(self.V),
+                                         _ptr(self.K_repr), _ptr(O), _stream(self.K.device)),
+                       VARIANT)
+        self.length += 1
+        return O
 
     def attend(self, Q_new, causal=True):
         q_len = Q_new.shape[2]

@@ -442,6 +442,32 @@ int bsa_decode(const bsa_problem* p, const void* Q, int q_len, int q_pos, const 
   return e == cudaSuccess ? BSA_OK : cuda_fail(e, "decode fine launch");
 }
 
+int bsa_decode_step(const bsa_problem* p, const void* q_new, const void* k_new,
+                    const void* v_new, int pos, void* K, void* V, float* K_repr, void* O,
+                    void* stream) {
+  g_last_error.clear();
+  int st = check(p);
+  if (st != BSA_OK) return st;
+  if (pos < 0 || pos >= p->seq_len)
+    return fail(BSA_ERR_INVALID, "position %d outside the cache of %d", pos, p->seq_len);
+  if (!aligned16(q_new) || !aligned16(k_new) || !aligned16(v_new) || !aligned16(K) ||
+      !aligned16(V) || !aligned16(K_repr) || !aligned16(O))
+    return fail(BSA_ERR_ALIGNMENT, "every pointer must be 16-byte aligned");
+  Shape s = make_shape(p, (int)total_units(p));
+  s.Nq = 1;
+  s.q0 = pos;
+  s.kv = pos + 1;
+  if (!decode_fine_supported(s))
+    return fail(BSA_ERR_UNSUPPORTED,
+                "one-launch decode step covers block_size 32/64/128 and head_dim 64/128; "
+                "use bsa_pool_k_blocks and bsa_decode");
+  cudaError_t e = launch_decode_step((const __nv_bfloat16*)q_new, (const __nv_bfloat16*)k_new,
+                                     (const __nv_bfloat16*)v_new, (__nv_bfloat16*)K,
+                                     (__nv_bfloat16*)V, K_repr, (__nv_bfloat16*)O, s,
+                                     (cudaStream_t)stream);
+  return e == cudaSuccess ? BSA_OK : cuda_fail(e, "decode step launch");
+}
+
 int bsa_select_blocks(const bsa_problem* p, const void* Q, const float* K_repr,
                       const void* K_split, int32_t* idx, void* stream) {
   g_last_error.clear();

@@ -48,6 +48,13 @@ cudaError_t launch_qblock_select(const float* Q_repr, const float* K_repr, int32
 // Decode fine stage, a CTA per new row split over its selected blocks
 // (block_size 32/64/128, head_dim 64/128; decode_fine_supported).
 bool decode_fine_supported(const Shape& s);
+// One decode step in one launch (the shapes decode_fine_supported accepts):
+// append the new K/V rows at position s.q0, re-pool their block, select and
+// attend the new row (s.Nq = 1, s.kv = s.q0 + 1).
+cudaError_t launch_decode_step(const __nv_bfloat16* q_new, const __nv_bfloat16* k_new,
+                               const __nv_bfloat16* v_new, __nv_bfloat16* K, __nv_bfloat16* V,
+                               float* K_repr, __nv_bfloat16* O, const Shape& s,
+                               cudaStream_t st);
 cudaError_t launch_decode_fine(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                                const __nv_bfloat16* V, const int32_t* idx, __nv_bfloat16* O,
                                const Shape& s, cudaStream_t st);

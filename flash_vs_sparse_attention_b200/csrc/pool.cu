@@ -13,6 +13,7 @@
 //
 // HBM-bound: reads N*D*2 bytes per unit, writes nb*D*(4+2+2).
 #include "common.cuh"
+#include "rowops.cuh"
 
 namespace bsa {
 
@@ -30,71 +31,9 @@ pool_k_kernel(const __nv_bfloat16* __restrict__ K, float* __restrict__ K_repr,
   const int lane = threadIdx.x & 31;
   const int64_t total = (int64_t)s.units * n_blocks;
   if (warp >= total) return;
-  const int chunks = s.D >> 3;                 // 16-byte chunks per key row
-  const int rows_per_iter = 32 / lanes_per_row;
-  const int g = lane / lanes_per_row;          // row group
-  const int c = lane % lanes_per_row;          // chunk within the row
-  const bool active = c < chunks;
-
   const int64_t unit = warp / n_blocks;
   const int64_t blk = block_begin + warp % n_blocks;
-  const uint4* src = reinterpret_cast<const uint4*>(K + (unit * s.N + blk * s.bs) * (int64_t)s.D);
-  // Keys of this block that exist (all bs of them outside a growing cache).
-  const int rows = (int)min((int64_t)s.bs, (int64_t)s.kv - blk * s.bs);
-
-  float acc[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-
-  if (active) {
-    // Batches of 16 loads issued before any is summed (a whole 64-key block
-    // per batch at head_dim 64): one memory round trip per batch.
-    for (int r0 = g; r0 < rows; r0 += 16 * rows_per_iter) {
-      uint4 v[16];
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const int r = r0 + q * rows_per_iter;
-        v[q] = r < rows ? __ldg(src + (int64_t)r * chunks + c) : make_uint4(0u, 0u, 0u, 0u);
-      }
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        acc[0] += bf16_lo(v[q].x); acc[1] += bf16_hi(v[q].x);
-        acc[2] += bf16_lo(v[q].y); acc[3] += bf16_hi(v[q].y);
-        acc[4] += bf16_lo(v[q].z); acc[5] += bf16_hi(v[q].z);
-        acc[6] += bf16_lo(v[q].w); acc[7] += bf16_hi(v[q].w);
-      }
-    }
-  }
-  // Reduce over row groups (lanes that differ in the row-group bits).
-  for (int o = lanes_per_row; o < 32; o <<= 1) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
-  }
-  if (g == 0 && active) {
-    const float den = (float)rows;
-    float m[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) m[i] = acc[i] / den;
-    const int64_t off = (unit * s.nb + blk) * (int64_t)s.D + c * 8;
-    float4* dst = reinterpret_cast<float4*>(K_repr + off);
-    dst[0] = make_float4(m[0], m[1], m[2], m[3]);
-    dst[1] = make_float4(m[4], m[5], m[6], m[7]);
-    if (K_hi != nullptr) {
-      uint32_t hi[4], lo[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float a0 = m[2 * i] * s.scale, a1 = m[2 * i + 1] * s.scale;
-        __nv_bfloat16 h0 = __float2bfloat16_rn(a0);
-        __nv_bfloat16 h1 = __float2bfloat16_rn(a1);
-        float r0 = a0 - __bfloat162float(h0);
-        float r1 = a1 - __bfloat162float(h1);
-        hi[i] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
-        lo[i] = pack_bf16x2(r0, r1);
-      }
-      *reinterpret_cast<uint4*>(K_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-      *reinterpret_cast<uint4*>(K_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    }
-  }
+  pool_block_warp<true>(K, K_repr, K_hi, K_lo, s, lanes_per_row, unit, blk, lane);
 }
 
 cudaError_t launch_pool_k(const __nv_bfloat16* K, float* K_repr, __nv_bfloat16* K_hi,

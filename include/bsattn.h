@@ -154,6 +154,19 @@ int bsa_decode(const bsa_problem* p, const void* Q, int q_len, int q_pos, const 
                const void* V, const float* K_repr, void* O, void* workspace,
                size_t workspace_bytes, void* stream);
 
+/* One decode step in one launch: for every unit, write the new token's key
+ * and value rows k_new, v_new (B, H, 1, D) into the cache K, V (B, H,
+ * capacity, D; p->seq_len = capacity) at position pos, re-pool the block
+ * they land in (K_repr as bsa_pool_k_blocks keeps it, blocks before it
+ * current), and attend the new query row q_new (B, H, 1, D) over keys
+ * [0, pos] into O (B, H, 1, D).  Same results as bsa_pool_k_blocks (that
+ * block, kv_len = pos + 1) followed by bsa_decode (q_len 1 at pos), which
+ * remain the path for block_size outside 32/64/128 or head_dim outside
+ * 64/128 (BSA_ERR_UNSUPPORTED here).  No workspace. */
+int bsa_decode_step(const bsa_problem* p, const void* q_new, const void* k_new,
+                    const void* v_new, int pos, void* K, void* V, float* K_repr, void* O,
+                    void* stream);
+
 /* Stages 2-3 alone (block_indexer_triton.py:121-129, block_indexer.py:44-53):
  * writes idx (B*H, N, top_k) int32, each row's selected blocks in ascending
  * block order, then -1 in slots left empty because fewer than top_k blocks

@@ -61,7 +61,44 @@ def test_decode_entry_points_check_arguments_without_touching_the_gpu():
     assert pk(ctypes.byref(p), mis, al, null, 0, 1, 64, null) == _lib.BSA_ERR_ALIGNMENT
 
 
+def test_decode_step_checks_arguments_without_touching_the_gpu():
+    L = _lib.lib()
+    p = bi.problem(1, 2, 1024, 64, True, 64, 4)
+    null, al, mis = ctypes.c_void_p(0), ctypes.c_void_p(4096), ctypes.c_void_p(4100)
+    step = L.bsa_decode_step
+    assert step(ctypes.byref(p), al, al, al, 1024, al, al, al, al, null) == _lib.BSA_ERR_INVALID
+    assert step(ctypes.byref(p), al, al, al, -1, al, al, al, al, null) == _lib.BSA_ERR_INVALID
+    assert step(ctypes.byref(p), al, mis, al, 5, al, al, al, al, null) == _lib.BSA_ERR_ALIGNMENT
+    p16 = bi.problem(1, 2, 1024, 64, True, 16, 4)     # block_size 16: the two-call path
+    assert step(ctypes.byref(p16), al, al, al, 5, al, al, al, al, null) == _lib.BSA_ERR_UNSUPPORTED
+
+
 # ---------------------------------------------------------------- GPU
+@pytest.mark.gpu
+@pytest.mark.parametrize("bs,D,k", [(64, 64, 16), (128, 64, 8), (32, 128, 16)])
+def test_decode_step_equals_append_then_attend(cuda, bs, D, k):
+    """The one-launch step leaves the cache, its block means and the output
+    exactly as append (re-pool) followed by attend does, token after token
+    across block boundaries."""
+    B, H, cap = 1, 3, 1024
+    n0, steps = 250, 40
+    Qn, Kn, Vn = (_rand((B, H, n0 + steps, D), s) for s in (15, 16, 17))
+    Q, K, V = to_gpu(Qn, Kn, Vn)
+    a = bi.DecodeCache(B, H, cap, D, bs, k)
+    b = bi.DecodeCache(B, H, cap, D, bs, k)
+    for c in (a, b):
+        c.append(K[:, :, :n0], V[:, :, :n0])
+    for t in range(n0, n0 + steps):
+        row = lambda x: x[:, :, t:t + 1].contiguous()   # noqa: E731
+        got = a.step(row(Q), row(K), row(V))
+        b.append(row(K), row(V))
+        want = b.attend(row(Q))
+        assert torch.equal(got, want), f"step at position {t}"
+    assert a.length == b.length == n0 + steps
+    assert torch.equal(a.K, b.K) and torch.equal(a.V, b.V)
+    assert torch.equal(a.K_repr, b.K_repr)
+
+
 @pytest.mark.gpu
 def test_pool_k_blocks_matches_whole_pool_and_partial_means(cuda):
     B, H, N, D, bs = 1, 3, 2048, 64, 64
