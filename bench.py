@@ -11,7 +11,12 @@ are quoted on).  Rank 0 prints one JSON line.
 * ``value``: effective TFLOP/s (FLOPs of the reference's benchmark/flops.py
   model, summed over every unit all ranks processed, divided by the max over
   ranks of the CUDA-event time of K steps), inputs resident in HBM, L2
-  flushed before every step.
+  flushed before every step.  With N GPUs the workload's (batch, head) units
+  are split over the ranks (``--scaling strong``, the default; ``weak`` runs
+  the whole workload on every rank); ``with_gather`` then times the forward
+  plus the NCCL all-gather that assembles the whole output on every rank.
+* ``stages`` / ``roofline_path``: per-stage and whole-path algorithmic bytes
+  and FLOPs against the measured HBM and bf16 peaks.
 * ``e2e``: the same metric through the public host-memory entry point
   (``attention_from_host``) with pinned host buffers: the host->device copies
   of Q, K, V and the device->host copy of O are inside the timed region
@@ -22,8 +27,9 @@ are quoted on).  Rank 0 prints one JSON line.
   timed on this host's cores on a bounded sample (rank 0, N=1 only).
 
 ``--impl reference`` times the reference algorithm on the host cores (the
-oracle port of attention/block_indexer.py) on the same workload and prints
-the same line with ``"impl": "reference"``.
+oracle port of attention/block_indexer.py) on the same workload -- every
+unit and every query row per step -- and prints the same line with
+``"impl": "reference"``.
 
 ``--mode decode`` measures decode-time reuse instead (its own JSON line):
 one step appends one token per (batch, head) unit to a KV cache of the
@@ -204,6 +210,8 @@ def run_ours(args, cfg):
                                 device_id=dev)
 
     U = cfg["B"] * cfg["H"]
+    if args.scaling is None:
+        args.scaling = "strong"   # one problem's (batch, head) units split over the ranks
     if args.scaling == "weak":
         my_units = U
         total_units = U * world
@@ -319,6 +327,40 @@ def run_ours(args, cfg):
                "d2h_bytes_per_step": O.numel() * O.element_size()}
         del Qh, Kh, Vh, Oh
 
+    # ---- the head-sharded output gathered on every rank (N > 1) ----
+    # The same forward followed by the all-gather of every rank's units
+    # (sharding.gather_units: one all_gather_into_tensor over NCCL), timed as
+    # its own region: the latency a caller that wants the whole output sees.
+    with_gather = None
+    if world > 1 and args.scaling == "strong":
+        from flash_vs_sparse_attention_b200.sharding import gather_units
+        for _ in range(args.warmup):
+            flush.zero_()
+            forward()
+            gather_units(O, U)
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        gs, ge = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g_ms = 0.0
+        for _ in range(args.steps):
+            flush.zero_()
+            gs.record(stream)
+            forward()
+            gather_units(O, U)
+            ge.record(stream)
+            torch.cuda.synchronize()
+            g_ms += gs.elapsed_time(ge)
+        t = torch.tensor([g_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        per = -(-U // world)
+        shard_bytes = per * cfg["N"] * cfg["D"] * 2
+        with_gather = {"ms_per_step": round(t.item() / args.steps, 4),
+                       "value": round(flops_step * args.steps / (t.item() * 1e-3) / 1e12, 4),
+                       "unit": "TFLOP/s",
+                       "collective": "all_gather_into_tensor (NCCL) of the (batch, head) shards",
+                       "bytes_per_rank": shard_bytes, "bytes_total": shard_bytes * world}
+
     # ---- roofline of the fine-stage kernel ----
     # The stage events cover the first pass of the forward; a workload whose
     # units do not fit one workspace runs in passes of `pass_units` (the
@@ -339,6 +381,20 @@ def run_ours(args, cfg):
             traffic = json.load(open(tpath)).get(f"config{args.config}", {}).get("fine")
         except (OSError, ValueError):
             traffic = None
+    stages = stage_model(cfg, pass_units, {k: statistics.mean(v) for k, v in stage_ms.items()},
+                         peaks, peak_kind)
+    path_flops = F.compute_flops(1, my_units, cfg["N"], cfg["D"], "block_indexer_b200",
+                                 cfg["block_size"], cfg["top_k"])
+    path_tflops = path_flops * args.steps / (total_ms * 1e-3) / 1e12
+    roofline_path = {
+        "tflops": round(path_tflops, 2),
+        "tensor_frac": round(path_tflops / float(peaks["bf16_tflops"]), 4),
+        "hbm_gbs": round(F.min_hbm_bytes(1, my_units, cfg["N"], cfg["D"]) * args.steps
+                         / (total_ms * 1e-3) / 1e9, 2),
+        "hbm_frac": round(F.min_hbm_bytes(1, my_units, cfg["N"], cfg["D"]) * args.steps
+                          / (total_ms * 1e-3) / 1e9 / float(peaks["hbm_gbs"]), 4),
+        "note": "per rank: flops.py FLOPs and compulsory bytes (Q, K, V in, O out) over the "
+                "step time, against the measured bf16 GEMM and copy peaks"}
     roofline = {"kernel": "fine (tensor-core, key-block-stationary)", "bound": "tensor",
                 "achieved": round(achieved, 2) if achieved else None, "peak": peak,
                 "unit": "TFLOP/s", "frac": round(achieved / peak, 4) if achieved else None,
@@ -366,6 +422,9 @@ def run_ours(args, cfg):
             "hbm_gbs_note": "compulsory bytes (read Q,K,V + write O) / step time",
             "stages_ms": {k: round(statistics.mean(v), 4) for k, v in stage_ms.items()},
             "stages_units": pass_units,
+            "stages": stages,
+            "roofline_path": roofline_path,
+            "with_gather": with_gather,
             "roofline": roofline, "clocks": clk.summary(), "e2e": e2e,
             "gpu_launches": launches,
         }
@@ -374,6 +433,49 @@ def run_ours(args, cfg):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def stage_model(cfg, units, stage_ms, peaks, peak_kind):
+    """Per stage of one pass of ``units`` units: its algorithmic HBM bytes (and
+    FLOPs), what bounds it, and the achieved fraction of that bound from the
+    stage's CUDA-event time.  Bytes per unit (N rows, D, k, nb blocks):
+      pool    K in, block means out (fp32 + bf16 hi/lo)    N D 2 + nb D 8
+      select  Q and the hi/lo means in, idx out            N D 2 + nb D 4 + N k 4
+              (+ 2 * 2 N nb D FLOP on tensor cores, half with causal skipping)
+      bucket  idx in twice, V in (block max), lists and
+              (query, slot) map out                         4 N k 4 + N D 2
+      fine    Q, K, V in, partials out (fp16 O + m, l)     3 N D 2 + N k (2 D + 8)
+              (+ 4 N k bs D FLOP: the flops.py fine-matmul term)
+      combine partials and map in, O out                   N k (2 D + 8) + N k 4 + N D 2
+    """
+    from flash_vs_sparse_attention_b200 import flops as F
+    N, D, k, bs = cfg["N"], cfg["D"], cfg["top_k"], cfg["block_size"]
+    nb = N // bs
+    u = units
+    part = N * k * (2 * D + 8)
+    model = {
+        "pool": (u * (N * D * 2 + nb * D * 8), 0),
+        "select": (u * (N * D * 2 + nb * D * 4 + N * k * 4),
+                   u * 2 * 2 * N * nb * D // (2 if cfg["causal"] else 1)),
+        "bucket": (u * (4 * N * k * 4 + N * D * 2), 0),
+        "fine": (u * (3 * N * D * 2 + part), F.fine_matmul_flops(1, u, N, D, bs, k)),
+        "combine": (u * (part + N * k * 4 + N * D * 2), 0),
+    }
+    hbm, tc = float(peaks["hbm_gbs"]), float(peaks["bf16_tflops"])
+    out = {}
+    for name, (nbytes, nflop) in model.items():
+        ms = stage_ms.get(name, 0.0)
+        if ms <= 0:
+            continue
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        d = {"ms": round(ms, 4), "bytes": nbytes, "gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4)}
+        if nflop:
+            tf = nflop / (ms * 1e-3) / 1e12
+            d.update({"flops": nflop, "tflops": round(tf, 2), "tensor_frac": round(tf / tc, 4)})
+        d["bound"] = "tensor" if name == "fine" else "hbm"
+        out[name] = d
+    out["peaks"] = f"{peak_kind} hbm_gbs {hbm}, bf16_tflops {tc} (burst)"
+    return out
 
 
 # --------------------------------------------------------------------------
@@ -410,7 +512,7 @@ def time_oracle(cfg, q, k, v, rows_list, threads):
 
 def cpu_baseline(cfg, args):
     threads = os.cpu_count() or 1
-    q, k, v, rows = cpu_sample(cfg, args.cpu_rows)
+    q, k, v, rows = cpu_sample(cfg, args.cpu_rows or cfg["N"])
     n = sum(len(r) for r in rows)
     time_oracle(cfg, q, k, v, rows[:1], threads)  # warm-up
     secs = time_oracle(cfg, q, k, v, rows, threads)
@@ -422,29 +524,49 @@ def cpu_baseline(cfg, args):
 
 
 def run_reference(args, cfg):
+    """The reference algorithm (the oracle port of attention/block_indexer.py)
+    on the host cores, on the same workload as our arm: every (batch, head)
+    unit and every query row per timed step (``--cpu-rows R`` instead times R
+    rows of unit 0).  Warm-up steps run one 512-row chunk each."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    import numpy as np
+    from oracle import unit_inputs
     threads = os.cpu_count() or 1
-    q, k, v, rows = cpu_sample(cfg, args.cpu_rows)
-    n = sum(len(r) for r in rows)
+    U, N = cfg["B"] * cfg["H"], cfg["N"]
+    if args.cpu_rows:
+        q, k, v, rows = cpu_sample(cfg, args.cpu_rows)
+        units = [(q, k, v, rows)]
+        sample = (f"{sum(len(r) for r in rows)} query rows of unit 0 per step, numpy restatement "
+                  f"of attention/block_indexer.py, {threads} host threads")
+    else:
+        units = []
+        for u in range(U):
+            q, k, v = unit_inputs(cfg, u, 0)
+            units.append((q, k, v, [list(range(s0, min(N, s0 + 512))) for s0 in range(0, N, 512)]))
+        sample = (f"the whole workload per step: all {U} units x {N} query rows, numpy "
+                  f"restatement of attention/block_indexer.py, {threads} host threads")
+    n = sum(len(r) for (_, _, _, rs) in units for r in rs)
     fl = per_query_flops(cfg) * n
+    q0, k0, v0, r0 = units[0]
     for _ in range(args.warmup):
-        time_oracle(cfg, q, k, v, rows, threads)
-    times = [time_oracle(cfg, q, k, v, rows, threads) for _ in range(args.steps)]
+        time_oracle(cfg, q0, k0, v0, r0[:1], threads)
+    times = []
+    for _ in range(args.steps):
+        times.append(sum(time_oracle(cfg, q, k, v, rs, threads) for (q, k, v, rs) in units))
     total = sum(times)
     value = fl * args.steps / total / 1e12
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    sample = (f"{n} query rows of unit 0 per step ({len(rows)} chunks of 512 spread over N), numpy "
-              f"restatement of attention/block_indexer.py, {threads} host threads")
     line = {
         "metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total / args.steps * 1e3, 3),
-        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "impl": "reference",
-        "config": {"workload": workload_name(cfg), "seq_len": cfg["N"], "head_dim": cfg["D"],
+        "higher_is_better": True, "scaling": args.scaling or "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": workload_name(cfg), "total_units": U, "global_batch": cfg["B"],
+                   "heads": cfg["H"], "seq_len": N, "head_dim": cfg["D"],
                    "block_size": cfg["block_size"], "top_k": cfg["top_k"], "causal": cfg["causal"],
-                   "parallelism": "host cores of rank 0", "sample_rows": n},
+                   "rows_per_step": n, "parallelism": f"{threads} host threads of rank 0"},
         "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -552,9 +674,12 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=3, choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
-                    help="weak: every GPU runs the whole workload's units; strong: the units are split")
-    ap.add_argument("--cpu-rows", type=int, default=16384, help="query rows in the CPU sample")
+    ap.add_argument("--scaling", default=None, choices=["weak", "strong"],
+                    help="strong (default): the workload's (batch, head) units are split over "
+                         "the GPUs; weak: every GPU runs all of them")
+    ap.add_argument("--cpu-rows", type=int, default=0,
+                    help="query rows of unit 0 in the CPU timings (0: one whole unit for the "
+                         "cpu_baseline key, the whole workload for --impl reference)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mode", default="forward", choices=["forward", "decode"],

@@ -63,6 +63,7 @@ SIGNATURES = {
     "bsa_fine_workspace_bytes": (_c.c_size_t, [_PP]),
     "bsa_workspace_error": (_c.c_int, [_PP, _P, _c.c_size_t, _c.c_int, _c.POINTER(_c.c_uint32)]),
     "bsa_forward_noalloc": (_c.c_int, [_PP, _P, _P, _P, _P, _P]),
+    "bsa_noalloc_error": (_c.c_int, [_PP, _c.POINTER(_c.c_uint32)]),
     "bsa_host_workspace_bytes": (_c.c_size_t, [_PP, _c.c_int64]),
     "bsa_forward_host": (_c.c_int, [_PP, _P, _P, _P, _P, _c.c_int64, _P, _c.c_size_t, _P]),
     "bsa_pool_k_blocks": (_c.c_int, [_PP, _P, _P, _P, _c.c_int, _c.c_int, _c.c_int, _P]),

@@ -239,11 +239,13 @@ int bsa_forward_ex(const bsa_problem* p, const void* Q, const void* K, const voi
       if (first && events != nullptr && stage < n_events && events[stage] != nullptr)
         cudaEventRecord((cudaEvent_t)events[stage], s_);
     };
-    // The pool kernel also clears the fine stage's error word and work-item
-    // counter, and the scorer reports into that error word.
+    // The pool kernel also clears the fine stage's counters, and on the first
+    // pass its error word, so a timeout in any pass stays visible after the
+    // call; the scorer reports into that error word.
     const bool kv = fine_uses_tensor_cores(s, p->flags);
-    void* zero = kv ? (void*)(ws + L.fine) : nullptr;
-    const size_t zero_bytes = kv ? fine_kv_zero_bytes(s) : 0;
+    const size_t zero_from = first ? 0 : fine_kv_counters_offset(s);
+    void* zero = kv ? (void*)(ws + L.fine + zero_from) : nullptr;
+    const size_t zero_bytes = kv ? fine_kv_zero_bytes(s) - zero_from : 0;
     uint32_t* err = kv ? (uint32_t*)(ws + L.fine + fine_kv_error_offset(s)) : nullptr;
     const bool qblock = (p->flags & BSA_FLAG_QBLOCK) != 0;
     cudaError_t e;

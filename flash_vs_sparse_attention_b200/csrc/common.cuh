@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -18,6 +19,16 @@ __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Pack two floats to fp16x2 with round-to-nearest-even (low half = a).
+__device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float2 unpack_f16x2(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -37,6 +48,15 @@ __device__ __forceinline__ float fast_exp2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+
+__device__ __forceinline__ float fast_log2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 2^e for an integer e in [-126, 127], built from its exponent bits.
+__device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) << 23); }
 
 // max of three floats in one instruction (sm_100).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {

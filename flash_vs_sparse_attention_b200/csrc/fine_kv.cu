@@ -23,10 +23,20 @@
 //                    computes S = Q K^T into TMEM, a softmax warpgroup turns
 //                    it into P (bf16, TMEM) with each row's max m and sum l,
 //                    tcgen05 computes O = P V into TMEM, and the warpgroup
-//                    stores the item's partial tile (O as bf16, m, l) with
+//                    stores the item's partial tile (O as fp16, m, l) with
 //                    TMA stores: 128 contiguous rows per item.
 //  5. combine        per query: log-sum-exp merge of its top_k partials,
 //                    rounded to bf16 once.
+//
+// Partial outputs are fp16 with a power-of-two scale per key block: 2^e with
+// bs * max|V of the block| * 2^e <= 2^14, so |O 2^e| <= 2^14 for any row
+// (P <= 1).  The scale is folded into the softmax shift (P 2^e costs no extra
+// instruction) and into the stored m and l, so the combine needs no
+// per-partial exponent.  fp16 keeps 11 significant bits where bf16 keeps 8:
+// the output is then rounded to bf16 essentially once, as in the reference's
+// single bf16 store (block_indexer_triton.py:81-83).  bucket_count computes
+// the per-block exponents (max|V| over the block's bs x D values) as a side
+// job of its CTAs.
 //
 // All waits are bounded (a stuck pipeline ends with an error word, not a
 // hang).  Warp roles and the barrier discipline are described at KvCfg.
@@ -60,18 +70,23 @@ enum : uint32_t {
 };
 
 struct FineWs {
-  uint32_t* err;       // [0] error bits, [1] total work items      } zeroed before
+  uint32_t* err;       // [0] error bits (16 bytes)                  } zeroed before
+  uint32_t* ctr;       // [0] total work items (16 bytes)             } the stage (the
+                       //                                                error word only
+                       //                                                before the first
+                       //                                                pass of a call)
   int32_t* done;       // units: chunks counted so far                } the stage
   int32_t* cursor;     // units * nb: entries of each block so far    }
   int32_t* chunk_rel;  // units * chunks * nb: start of (chunk, block) within the block's list
   int32_t* offsets;    // units * nb: a block's first position in its unit's list
   int32_t* item_row;   // units * nb: 128 * (a block's first work item)
+  int32_t* vexp;       // units * nb: the block's partial-output scale exponent
   int4* items;         // units * max_items_per_unit
   int32_t* lists;      // units * N * k: query rows grouped by block
   int32_t* inv;        // units * N * k: (query, slot) -> partial row
-  __nv_bfloat16* part_o;  // 128 rows per work item, D columns
+  __half* part_o;      // 128 rows per work item, D columns (fp16, scaled)
   float2* part_ml;     // 128 rows per work item
-  size_t zero_bytes;   // err, done and cursor, at the start of the region
+  size_t zero_bytes;   // err, ctr, done and cursor, at the start of the region
   int64_t part_rows;   // rows of part_o / part_ml
   size_t total;
 };
@@ -110,16 +125,18 @@ static FineWs fine_ws_layout(const Shape& s, unsigned char* base) {
   };
   w.part_rows = (int64_t)U * max_items_per_unit(s) * kTileRows;
   w.err = (uint32_t*)take(16);
+  w.ctr = (uint32_t*)take(16);
   w.done = (int32_t*)take(4 * U);
   w.cursor = (int32_t*)take(4 * U * nb);
   w.zero_bytes = off;
   w.chunk_rel = (int32_t*)take(4 * U * (size_t)bucket_geom(s).chunks * nb);
   w.offsets = (int32_t*)take(4 * U * nb);
   w.item_row = (int32_t*)take(4 * U * nb);
+  w.vexp = (int32_t*)take(4 * U * nb);
   w.items = (int4*)take(16 * U * (size_t)max_items_per_unit(s));
   w.lists = (int32_t*)take(4 * (U * Nk + 256));   // slack for aligned list-slice copies
   w.inv = (int32_t*)take(4 * U * Nk);
-  w.part_o = (__nv_bfloat16*)take(2 * (size_t)w.part_rows * s.D);
+  w.part_o = (__half*)take(2 * (size_t)w.part_rows * s.D);
   w.part_ml = (float2*)take(8 * (size_t)w.part_rows);
   w.total = off;
   return w;
@@ -138,6 +155,10 @@ size_t fine_kv_workspace_bytes(const Shape& s) { return fine_ws_layout(s, nullpt
 size_t fine_kv_zero_bytes(const Shape& s) { return fine_ws_layout(s, nullptr).zero_bytes; }
 
 size_t fine_kv_error_offset(const Shape&) { return 0; }   // the error word leads the region
+
+// The per-pass counters follow the error word's region: a later pass of one
+// call clears from here, so an earlier pass's error bits survive to the end.
+size_t fine_kv_counters_offset(const Shape&) { return a256(16); }   // err takes 16 bytes
 
 // ---------------------------------------------------------------------------
 // Bucket helpers.
@@ -197,6 +218,50 @@ __device__ __forceinline__ int block_exclusive_scan(int x, int* warp_sums, int* 
   return before + inc - x;
 }
 
+// Scale exponents of the partial outputs (see the top of the file): for key
+// block j of unit u the largest e in [kMinVexp, kMaxVexp] with
+// bs * max|V_j| * 2^e <= 2^14, from the bf16 bit patterns (max|v| < 2^(E+1),
+// E the unbiased exponent of the largest |v|).  One warp per block, 16-byte
+// loads.  Of e, the part at or above kMinShiftExp is folded into the softmax
+// shift; the rest (blocks with max|v| above ~2^64) scales the epilogue.
+constexpr int kMinVexp = -120, kMaxVexp = 60, kMinShiftExp = -56;
+
+__device__ __forceinline__ void vexp_block_warp(const __nv_bfloat16* __restrict__ V,
+                                                int32_t* __restrict__ vexp, const Shape& s, int u,
+                                                int j, int lane) {
+  const uint4* src =
+      reinterpret_cast<const uint4*>(V + ((int64_t)u * s.N + (int64_t)j * s.bs) * s.D);
+  const int n16 = s.bs * s.D / 8;   // 16-byte chunks of the block
+  uint32_t mx = 0;                  // per-halfword max of |bf16| bit patterns
+  for (int i0 = 0; i0 < n16; i0 += 32 * 8) {
+    uint4 v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int i = i0 + q * 32 + lane;
+      v[q] = i < n16 ? __ldg(src + i) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      mx = __vmaxu2(mx, v[q].x & 0x7fff7fffu);
+      mx = __vmaxu2(mx, v[q].y & 0x7fff7fffu);
+      mx = __vmaxu2(mx, v[q].z & 0x7fff7fffu);
+      mx = __vmaxu2(mx, v[q].w & 0x7fff7fffu);
+    }
+  }
+  mx = __vmaxu2(mx, mx >> 16) & 0xffffu;   // non-negative bf16: bit order = value order
+  mx = __reduce_max_sync(0xffffffffu, mx);
+  if (lane == 0) {
+    int e = kMaxVexp;
+    if (mx != 0) {
+      const int be = (int)(mx >> 7) & 0xff;   // biased exponent (0: subnormal)
+      const int E = (be == 0 ? 1 : be) - 127;
+      e = 13 - (31 - __clz(s.bs)) - E;        // 14 - log2(bs) - (E + 1)
+      e = min(kMaxVexp, max(kMinVexp, e));
+    }
+    vexp[(int64_t)u * s.nb + j] = e;
+  }
+}
+
 // 1. Per chunk of a unit's rows: how many of its selections pick each block,
 //    and where the chunk's entries of block j start within j's list (an
 //    atomic on the block's cursor, so the chunks of a list come in any
@@ -213,12 +278,22 @@ __global__ void __launch_bounds__(kBucketThreads, 2)
 bucket_count_kernel(const int32_t* __restrict__ idx, int32_t* __restrict__ cursor,
                     int32_t* __restrict__ chunk_rel, int32_t* __restrict__ done,
                     int32_t* __restrict__ offsets, int32_t* __restrict__ item_row,
-                    int4* __restrict__ items, uint32_t* __restrict__ err, Shape s, BucketGeom g) {
+                    int4* __restrict__ items, uint32_t* __restrict__ ctr,
+                    const __nv_bfloat16* __restrict__ V, int32_t* __restrict__ vexp, Shape s,
+                    BucketGeom g) {
   extern __shared__ int32_t hist[];
   __shared__ int32_t wsum_c[kBucketThreads / 32], wsum_t[kBucketThreads / 32];
   __shared__ int32_t ticket, item_base;
   const int u = blockIdx.y, chunk = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  {
+    // Side job: the partial-output scale exponents of this chunk's share of
+    // the unit's key blocks.
+    const int bpc = (s.nb + g.chunks - 1) / g.chunks;
+    const int j1 = min(s.nb, (chunk + 1) * bpc);
+    for (int j = chunk * bpc + warp; j < j1; j += kBucketThreads / 32)
+      vexp_block_warp(V, vexp, s, u, j, lane);
+  }
   for (int j = tid; j < s.nb; j += kBucketThreads) hist[j] = 0;
   __syncthreads();
   const int row_end = min(s.N, (chunk + 1) * g.chunk_rows);
@@ -268,7 +343,7 @@ bucket_count_kernel(const int32_t* __restrict__ idx, int32_t* __restrict__ curso
       if (lane >= o) { ia += x; ib += y; }
     }
     if (lane < W) { wsum_c[lane] = ia - a; wsum_t[lane] = ib - b; }
-    if (lane == 31) item_base = (int)atomicAdd(&err[1], (uint32_t)ib);
+    if (lane == 31) item_base = (int)atomicAdd(&ctr[0], (uint32_t)ib);
   }
   __syncthreads();
   int oc = wsum_c[warp] + ic - sc;   // exclusive prefix of this thread's blocks
@@ -495,6 +570,7 @@ constexpr int kMetaKv = kTileRows + 4;   // int offset of the word in the stage 
 struct FineKvParams {
   const int4* items;
   const int32_t* lists;
+  const int32_t* vexp;          // per (unit, block): partial-output scale exponent
   const uint32_t* total_items;  // device word written by bucket_count's layout step
   float2* part_ml;
   uint32_t* err;
@@ -797,31 +873,38 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
       return ready;
     };
     // Epilogue of item tp, the group's np-th, whose O is complete: O (not
-    // yet divided by l; the combine folds 1 / l into its weights) as bf16
-    // into this warp's 32 rows of the group's output tile (row r,
-    // 16-byte chunk c at the 128-byte swizzled place the TMA store expects),
-    // (m, l) per row, and the warp's own TMA store of its rows.  Each warp
-    // only waits for its own previous store to have read its rows.
-    auto epilogue = [&](int tp, int np, float mp, float lp) {
+    // yet divided by l; the combine folds 1 / l into its weights), already
+    // scaled by 2^e1 through the shift, times 2^e2 (e2 = e - e1, 0 unless the
+    // block's max|v| exceeds ~2^64; the same for the whole item), as fp16
+    // into this warp's 32 rows of the group's output tile (row r, 16-byte
+    // chunk c at the 128-byte swizzled place the TMA store expects), (m, l)
+    // per row, and the warp's own TMA store of its rows.  Each warp only
+    // waits for its own previous store to have read its rows.
+    auto epilogue = [&](int tp, int np, float mp, float lp, int e2) {
       if (np >= 1 && lane == 0) bulk_wait_group_read0();
       __syncwarp();
+      const float f2 = exp2i(e2);
 #pragma unroll
       for (int c0 = 0; c0 < HD; c0 += 64) {
         float ov[64];
         tmem_ld64(o_addr + c0, ov);
+        if (e2 != 0) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) ov[c] *= f2;
+        }
 #pragma unroll
         for (int c = 0; c < 64; c += 8) {
           const int ch = c >> 3;
           *reinterpret_cast<uint4*>(out + (c0 >> 6) * (kTileRows * 128) + r * 128 +
                                     ((ch ^ (r & 7)) << 4)) =
-              make_uint4(pack_bf16x2(ov[c], ov[c + 1]), pack_bf16x2(ov[c + 2], ov[c + 3]),
-                         pack_bf16x2(ov[c + 4], ov[c + 5]), pack_bf16x2(ov[c + 6], ov[c + 7]));
+              make_uint4(pack_f16x2(ov[c], ov[c + 1]), pack_f16x2(ov[c + 2], ov[c + 3]),
+                         pack_f16x2(ov[c + 4], ov[c + 5]), pack_f16x2(ov[c + 6], ov[c + 7]));
         }
       }
       // Work item gi owns partial rows [128 gi, 128 gi + 128); rows past the
       // item's count hold values that are never read.
       const int gi = (int)t_begin + tp;
-      prm.part_ml[(int64_t)gi * kTileRows + r] = make_float2(mp, lp);
+      prm.part_ml[(int64_t)gi * kTileRows + r] = make_float2(mp, lp * f2);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -839,8 +922,8 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
     };
 
     if (s_issuer && wg < T && !issue_s(wg)) *abort_flag = 1;
-    int n = 0, tp = -1;
-    float mp = 0.f, lp = 1.f;   // the previous item's row max (scaled) and sum
+    int n = 0, tp = -1, ep = 0;
+    float mp = 0.f, lp = 1.f;   // the previous item's stored m, its row sum, its e2
     bool ok = true;
     for (int t = wg; t < T; t += NWG, ++n) {
       const int st = t % NQ;
@@ -848,8 +931,13 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
       ok = __all_sync(0xffffffffu, ok);
       if (!ok || *abort_flag) { ok = false; break; }
       const int32_t* m = meta(st);
-      const int j = reinterpret_cast<const int4*>(m + kTileRows)[0].y;
+      const int4 itm = reinterpret_cast<const int4*>(m + kTileRows)[0];
+      const int j = itm.y;
       const int kv = m[kMetaKv];
+      // The block's partial-output exponent e; e1 = max(e, kMinShiftExp) goes
+      // into the shift, e2 = e - e1 into the epilogue.
+      const int ve = __ldg(prm.vexp + (int64_t)itm.x * s.nb + j);
+      const int ve1 = max(ve, kMinShiftExp);
       const int qrow = m[r];   // rows past the item's count repeat its first query
 
       ok = mbar_wait(&s_full[wg], n & 1, prm.err, kErrWaitS);
@@ -861,23 +949,24 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
       if (lane == 0) mbar_arrive(&q_empty[st]);
       const int key0 = j * BS;
       const bool diag = s.causal && key0 + BS - 1 > qrow;
-      float sv[64];
-      auto load_s = [&](int c0) {
-        tmem_ld64(s_addr + c0, sv);
-        // Token-level causal mask (block_indexer.py:73-81): key > query -> -inf.
-        if (diag) {
+      // The whole S row is read from TMEM once; the row max and every p
+      // come from these registers, so the shift and the stored (m, l, O)
+      // always describe the same scores.
+      float sv[BS];
 #pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (key0 + c0 + c > qrow) sv[c] = -INFINITY;
-        }
-      };
+      for (int c0 = 0; c0 < BS; c0 += 64) tmem_ld64(s_addr + c0, sv + c0);
+      // Token-level causal mask (block_indexer.py:73-81): key > query -> -inf.
+      if (diag) {
+#pragma unroll
+        for (int c = 0; c < BS; ++c)
+          if (key0 + c > qrow) sv[c] = -INFINITY;
+      }
       float mx = -INFINITY;
 #pragma unroll
       for (int c0 = 0; c0 < BS; c0 += 64) {
-        load_s(c0);
-        float m0 = sv[0], m1 = sv[1], m2 = sv[2], m3 = sv[3];
+        float m0 = sv[c0], m1 = sv[c0 + 1], m2 = sv[c0 + 2], m3 = sv[c0 + 3];
 #pragma unroll
-        for (int c = 4; c < 64; c += 8) {
+        for (int c = c0 + 4; c < c0 + 64; c += 8) {
           m0 = fmax3(m0, sv[c], sv[c + 1]);
           m1 = fmax3(m1, sv[c + 2], sv[c + 3]);
           m2 = fmax3(m2, sv[c + 4], sv[c + 5]);
@@ -885,12 +974,12 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
         }
         mx = fmax3(mx, fmax3(m0, m1, m2), m3);
       }
-      if (BS == 64) {   // S(t) is all in registers: its columns are free
-        tc_fence_before();
-        mbar_arrive(&s_free[wg]);
-      }
+      // S(t) is all in registers: its columns are free for S(t + NWG).
+      tc_fence_before();
+      mbar_arrive(&s_free[wg]);
       // Padding rows of a short item can be fully masked; keep them finite.
       const float msc = (mx == -INFINITY) ? 0.f : mx * sc;
+      const float msh = msc - (float)ve1;   // p 2^e1 = 2^(s sc - msh)
       if (n >= 1) {
         // PV(t - NWG) done: the P columns are free and O(t - NWG) is final.
         ok = mbar_wait(&o_full[wg], (n - 1) & 1, prm.err, kErrWaitO);
@@ -903,24 +992,19 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
       float l0 = 0.f, l1 = 0.f;
 #pragma unroll
       for (int c0 = 0; c0 < BS; c0 += 64) {
-        if (BS > 64) load_s(c0);   // with one chunk the values are still in sv
 #pragma unroll
         for (int h = 0; h < 64; h += 32) {   // 16 P columns at a time
           uint32_t pk[16];
 #pragma unroll
           for (int c = 0; c < 32; c += 2) {
-            const float p0 = fast_exp2(fmaf(sv[h + c], sc, -msc));
-            const float p1 = fast_exp2(fmaf(sv[h + c + 1], sc, -msc));
+            const float p0 = fast_exp2(fmaf(sv[c0 + h + c], sc, -msh));
+            const float p1 = fast_exp2(fmaf(sv[c0 + h + c + 1], sc, -msh));
             l0 += p0;
             l1 += p1;
             pk[c >> 1] = pack_bf16x2(p0, p1);
           }
           tmem_st16(p_addr + ((c0 + h) >> 1), pk);
         }
-      }
-      if (BS > 64) {
-        tc_fence_before();
-        mbar_arrive(&s_free[wg]);
       }
       const float l = l0 + l1;
       bool issued_next = false;
@@ -934,7 +1018,7 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
         if (!ok) { *abort_flag = 1; break; }
         issued_next = try_issue_s(t + NWG);
       }
-      if (n >= 1) epilogue(tp, n - 1, mp, lp);
+      if (n >= 1) epilogue(tp, n - 1, mp, lp, ep);
       tc_fence_before();   // P(t) stored, O(t - NWG) read out
       mbar_arrive(&p_full[wg]);
       if (issuer) {
@@ -964,8 +1048,9 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
         }
       }
       tp = t;
-      mp = msc;
+      mp = msc - (float)ve;   // stored m: weights 2^(m - M) then carry 2^-e
       lp = l;
+      ep = ve - ve1;
     }
     if (!ok) *abort_flag = 1;
     if (ok && tp >= 0) {
@@ -975,7 +1060,7 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
       if (ok) {
         tc_fence_after();
         if (storer) publish_o_done(tp);
-        epilogue(tp, n - 1, mp, lp);
+        epilogue(tp, n - 1, mp, lp, ep);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -993,19 +1078,25 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
   if (warp == 0) tmem_dealloc(tbase, C::kTmemCols);
 }
 
-// 5. Per query: merge its partials (m in the base-2 domain, l, and O = sum of
-//    2^(s - m) v, not divided by l), found through the (query, slot) ->
-//    partial row map (-1 for an empty slot).  CH = HD / 8 threads per query
-//    row, one 16-byte chunk of the output each.  The row's slot metadata
-//    (partial row, m, l) is loaded once, spread over the CH threads (slot q by thread
-//    q % CH) and shared by shuffles; every partial chunk load of the row is
-//    issued before the first is used, so a thread keeps up to KMAX loads in
-//    flight instead of a chain of dependent ones.
+// 5. Per query: merge its partials, found through the (query, slot) ->
+//    partial row map (-1 for an empty slot).  Partial j holds (m_j, l_j, O_j)
+//    with O_j = 2^e sum 2^(s sc - m) v, l_j = 2^e sum 2^(s sc - m) and m_j =
+//    m - e (m the row max in the base-2 domain, e the block's exponent), so
+//    with a_j = m_j and b_j = m_j + log2 l_j (the partial's true log-weight):
+//        O = 2^(A - B) (sum_j 2^(a_j - A) O_j) / (sum_j 2^(b_j - B)),
+//    A = max a_j, B = max b_j.  Each sum is formed against its own maximum,
+//    so no weight underflows whatever the blocks' exponents.  CH = HD / 8
+//    threads per query row, one 16-byte chunk (8 fp16) of the output each.
+//    The row's slot metadata (partial row, m, l) is loaded once, spread over
+//    the CH threads (slot q by thread q % CH) and shared by shuffles; every
+//    partial chunk load of the row is issued before the first is used, so a
+//    thread keeps up to KMAX loads in flight instead of a chain of dependent
+//    ones.
 template <int HD, int KMAX>
 __global__ void __launch_bounds__(256)
 combine_kernel(const int32_t* __restrict__ inv,
-               const __nv_bfloat16* __restrict__ part_o, const float2* __restrict__ part_ml,
-               __nv_bfloat16* __restrict__ O, Shape s) {
+               const __half* __restrict__ part_o, const float2* __restrict__ part_ml,
+               const uint32_t* __restrict__ err, __nv_bfloat16* __restrict__ O, Shape s) {
   constexpr int CH = HD / 8;           // threads per row (8 or 16), a power of two <= 32
   constexpr int PER = (KMAX + CH - 1) / CH;   // slots whose metadata one thread loads
   const int64_t rows = (int64_t)s.units * s.N;
@@ -1016,29 +1107,36 @@ combine_kernel(const int32_t* __restrict__ inv,
   const int lane = threadIdx.x & 31, base = lane & ~(CH - 1);
   const int32_t* prow = inv + R * s.k;   // -1: empty slot
   int32_t pr[PER];
-  float m[PER], l[PER];
+  float a[PER], b[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int q = c + i * CH;
     pr[i] = q < s.k ? __ldg(prow + q) : -1;
   }
-  float M = -INFINITY;
+  float A = -INFINITY, B = -INFINITY;
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
-    float2 ml = make_float2(-INFINITY, 0.f);
-    if (pr[i] >= 0) ml = __ldcs(&part_ml[pr[i]]);
-    m[i] = ml.x;
-    l[i] = ml.y;
-    M = fmaxf(M, ml.x);
+    a[i] = -INFINITY;
+    b[i] = -INFINITY;
+    if (pr[i] >= 0) {
+      const float2 ml = __ldcs(&part_ml[pr[i]]);
+      a[i] = ml.x;
+      b[i] = ml.x + fast_log2(ml.y);
+    }
+    A = fmaxf(A, a[i]);
+    B = fmaxf(B, b[i]);
   }
 #pragma unroll
-  for (int o = CH / 2; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  for (int o = CH / 2; o > 0; o >>= 1) {
+    A = fmaxf(A, __shfl_xor_sync(0xffffffffu, A, o));
+    B = fmaxf(B, __shfl_xor_sync(0xffffffffu, B, o));
+  }
   float L = 0.f;
   float w[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
-    w[i] = pr[i] >= 0 ? fast_exp2(m[i] - M) : 0.f;
-    L = fmaf(l[i], w[i], L);
+    w[i] = pr[i] >= 0 ? fast_exp2(a[i] - A) : 0.f;
+    L += pr[i] >= 0 ? fast_exp2(b[i] - B) : 0.f;
   }
 #pragma unroll
   for (int o = CH / 2; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
@@ -1058,16 +1156,25 @@ combine_kernel(const int32_t* __restrict__ inv,
 #pragma unroll
   for (int q = 0; q < KMAX; ++q) {
     const float wt = wq[q];
-    acc[0] = fmaf(wt, bf16_lo(v[q].x), acc[0]); acc[1] = fmaf(wt, bf16_hi(v[q].x), acc[1]);
-    acc[2] = fmaf(wt, bf16_lo(v[q].y), acc[2]); acc[3] = fmaf(wt, bf16_hi(v[q].y), acc[3]);
-    acc[4] = fmaf(wt, bf16_lo(v[q].z), acc[4]); acc[5] = fmaf(wt, bf16_hi(v[q].z), acc[5]);
-    acc[6] = fmaf(wt, bf16_lo(v[q].w), acc[6]); acc[7] = fmaf(wt, bf16_hi(v[q].w), acc[7]);
+    const float2 x0 = unpack_f16x2(v[q].x), x1 = unpack_f16x2(v[q].y);
+    const float2 x2 = unpack_f16x2(v[q].z), x3 = unpack_f16x2(v[q].w);
+    acc[0] = fmaf(wt, x0.x, acc[0]); acc[1] = fmaf(wt, x0.y, acc[1]);
+    acc[2] = fmaf(wt, x1.x, acc[2]); acc[3] = fmaf(wt, x1.y, acc[3]);
+    acc[4] = fmaf(wt, x2.x, acc[4]); acc[5] = fmaf(wt, x2.y, acc[5]);
+    acc[6] = fmaf(wt, x3.x, acc[6]); acc[7] = fmaf(wt, x3.y, acc[7]);
   }
   if (!live) return;
-  const float rl = 1.f / L;
+  // 2^(A - B) / L in two factors, each well inside the float range.  If a
+  // pipeline wait of this call timed out (error word set), the partials may
+  // be stale: the output becomes NaN rather than plausible numbers.
+  const float h = 0.5f * (A - B);
+  const float f1 = fast_exp2(h), f2 = *err != 0u ? __int_as_float(0x7fc00000) : fast_exp2((A - B) - h) / L;
+  float o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = (acc[i] * f1) * f2;
   reinterpret_cast<uint4*>(O + R * HD)[c] =
-      make_uint4(pack_bf16x2(acc[0] * rl, acc[1] * rl), pack_bf16x2(acc[2] * rl, acc[3] * rl),
-                 pack_bf16x2(acc[4] * rl, acc[5] * rl), pack_bf16x2(acc[6] * rl, acc[7] * rl));
+      make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                 pack_bf16x2(o[6], o[7]));
 }
 
 template <int HD>
@@ -1075,11 +1182,11 @@ static void launch_combine(const FineWs& w, __nv_bfloat16* O, const Shape& s, cu
   const int64_t threads = (int64_t)s.units * s.N * (HD / 8);
   const unsigned blocks = (unsigned)((threads + 255) / 256);
   if (s.k <= 16)
-    combine_kernel<HD, 16><<<blocks, 256, 0, st>>>(w.inv, w.part_o, w.part_ml, O, s);
+    combine_kernel<HD, 16><<<blocks, 256, 0, st>>>(w.inv, w.part_o, w.part_ml, w.err, O, s);
   else if (s.k <= 32)
-    combine_kernel<HD, 32><<<blocks, 256, 0, st>>>(w.inv, w.part_o, w.part_ml, O, s);
+    combine_kernel<HD, 32><<<blocks, 256, 0, st>>>(w.inv, w.part_o, w.part_ml, w.err, O, s);
   else
-    combine_kernel<HD, 64><<<blocks, 256, 0, st>>>(w.inv, w.part_o, w.part_ml, O, s);
+    combine_kernel<HD, 64><<<blocks, 256, 0, st>>>(w.inv, w.part_o, w.part_ml, w.err, O, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -1097,17 +1204,18 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-// 2-D bf16 tensor map over a row-major (rows, cols) matrix, 128-byte swizzle,
-// box of 64 columns x box_rows rows.
+// 2-D tensor map of 16-bit elements (bf16 unless given) over a row-major
+// (rows, cols) matrix, 128-byte swizzle, box of 64 columns x box_rows rows.
 static bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols,
-                     uint32_t box_rows) {
+                     uint32_t box_rows,
+                     CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   auto enc = get_encode();
   if (!enc) return false;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {cols * 2};
   cuuint32_t box[2] = {64, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+  CUresult r = enc(m, dtype, 2, const_cast<void*>(base), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
@@ -1134,7 +1242,7 @@ static cudaError_t launch_kv_kernel(const __nv_bfloat16* Q, const __nv_bfloat16*
   CUtensorMap mq, mo;
   if (!make_map(&mq, Q, rows, HD, 1) || !make_map(&mk, K, rows, HD, BS) ||
       !make_map(&mv, V, rows, HD, BS) ||
-      !make_map(&mo, w.part_o, (uint64_t)w.part_rows, HD, 32))
+      !make_map(&mo, w.part_o, (uint64_t)w.part_rows, HD, 32, CU_TENSOR_MAP_DATA_TYPE_FLOAT16))
     return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(fine_kv_kernel<BS, HD>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
@@ -1142,7 +1250,8 @@ static cudaError_t launch_kv_kernel(const __nv_bfloat16* Q, const __nv_bfloat16*
   FineKvParams prm;
   prm.items = w.items;
   prm.lists = w.lists;
-  prm.total_items = w.err + 1;
+  prm.vexp = w.vexp;
+  prm.total_items = w.ctr;
   prm.part_ml = w.part_ml;
   prm.err = w.err;
   prm.s = s;
@@ -1177,7 +1286,8 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                                 (int)scatter_smem)) != cudaSuccess)
     return e;
   count_k<<<bgrid, kBucketThreads, count_smem, st>>>(idx, w.cursor, w.chunk_rel, w.done,
-                                                     w.offsets, w.item_row, w.items, w.err, s, g);
+                                                     w.offsets, w.item_row, w.items, w.ctr, V,
+                                                     w.vexp, s, g);
   scatter_k<<<bgrid, kBucketThreads, scatter_smem, st>>>(idx, w.chunk_rel, w.offsets, w.item_row,
                                                          w.lists, w.inv, s, g, 1.0f / (float)s.k);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;

@@ -30,6 +30,7 @@ cudaError_t launch_fine_simt(const __nv_bfloat16* Q, const __nv_bfloat16* K,
 bool fine_kv_supported(const Shape& s);
 size_t fine_kv_workspace_bytes(const Shape& s);
 size_t fine_kv_error_offset(const Shape& s);  // byte offset of the error word
+size_t fine_kv_counters_offset(const Shape& s);  // byte offset of the per-pass counters
 size_t fine_kv_zero_bytes(const Shape& s);    // bytes to clear at the start of the region
 cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                            const __nv_bfloat16* V, const int32_t* idx, __nv_bfloat16* O,

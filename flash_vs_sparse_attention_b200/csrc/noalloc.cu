@@ -13,7 +13,7 @@
 //    unit needs more is rejected with BSA_ERR_WORKSPACE.
 //  * Every call on a device uses the same array, and the array keeps the last
 //    call's contents.  The forward clears what must start at zero (its
-//    error word and work-item counter) at the start of every pass, so
+//    counters at every pass, its error word at the first pass of a call), so
 //    back-to-back calls are independent -- but two calls whose GPU work
 //    overlaps (different streams, no ordering between them) race on the
 //    array and produce garbage.
@@ -22,7 +22,14 @@
 //    point's first call on that GPU).
 //  * The first call on a device resolves the array's device address there
 //    (cudaGetSymbolAddress, host-side set-up); make that first call before
-//    any stream capture.
+//    any stream capture.  The address is cached per device together with the
+//    context it was resolved in, and resolved again when the calling thread's
+//    current context is another one (after cudaDeviceReset the module is
+//    loaded anew and the old address is gone).
+//  * A pipeline wait that times out leaves bits in the array's error word
+//    (and NaN in O); bsa_noalloc_error reads them.
+#include <cuda.h>
+
 #include <cstdio>
 #include <mutex>
 
@@ -40,6 +47,54 @@ namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 void* g_scratch_dev_ptr[kMaxDevices] = {};
+CUcontext g_scratch_ctx[kMaxDevices] = {};
+
+// The calling thread's current context (null if none), through the driver
+// entry point the runtime exposes.
+CUcontext current_context() {
+  using Fn = CUresult (*)(CUcontext*);
+  static Fn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<Fn>(f);
+  });
+  CUcontext c = nullptr;
+  if (fn == nullptr || fn(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
+
+// The scratch array's device address on the current device: cached, and
+// resolved on the first call there or when the current context changed.
+// nullptr on error, with the message set.
+void* scratch_address() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_last_error_message("bsa_forward_noalloc: no usable current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_mu);
+  const CUcontext ctx = current_context();
+  if (g_scratch_dev_ptr[dev] != nullptr && ctx != nullptr && g_scratch_ctx[dev] == ctx)
+    return g_scratch_dev_ptr[dev];
+  // Host code must not pass g_noalloc_scratch itself to a kernel: in host
+  // code the name refers to a host-side stand-in, not device memory.
+  void* ptr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess || ptr == nullptr) {
+    char msg[256];
+    snprintf(msg, sizeof(msg), "bsa_forward_noalloc: cudaGetSymbolAddress failed: %s",
+             cudaGetErrorString(e));
+    set_last_error_message(msg);
+    return nullptr;
+  }
+  g_scratch_dev_ptr[dev] = ptr;
+  g_scratch_ctx[dev] = current_context();   // the lookup made the primary context current
+  return ptr;
+}
 }  // namespace
 
 }  // namespace bsa
@@ -62,30 +117,21 @@ int bsa_forward_noalloc(const bsa_problem* p, const void* Q, const void* K, cons
     set_last_error_message(msg);
     return BSA_ERR_WORKSPACE;
   }
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
-    set_last_error_message("bsa_forward_noalloc: no usable current CUDA device");
-    return BSA_ERR_CUDA;
-  }
-  void* ptr = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(g_mu);
-    ptr = g_scratch_dev_ptr[dev];
-    if (ptr == nullptr) {
-      // Host code must not pass g_noalloc_scratch itself to a kernel: in host
-      // code the name refers to a host-side stand-in, not device memory.
-      cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-      if (e != cudaSuccess || ptr == nullptr) {
-        char msg[256];
-        snprintf(msg, sizeof(msg), "bsa_forward_noalloc: cudaGetSymbolAddress failed: %s",
-                 cudaGetErrorString(e));
-        set_last_error_message(msg);
-        return BSA_ERR_CUDA;
-      }
-      g_scratch_dev_ptr[dev] = ptr;
-    }
-  }
+  void* ptr = scratch_address();
+  if (ptr == nullptr) return BSA_ERR_CUDA;
   return bsa_forward(p, Q, K, V, O, ptr, kNoAllocScratchBytes, stream);
+}
+
+int bsa_noalloc_error(const bsa_problem* p, uint32_t* error_bits) {
+  int st = bsa_check_problem(p);
+  if (st != BSA_OK) return st;
+  if (error_bits == nullptr) {
+    set_last_error_message("bsa_noalloc_error: error_bits is NULL");
+    return BSA_ERR_INVALID;
+  }
+  void* ptr = scratch_address();
+  if (ptr == nullptr) return BSA_ERR_CUDA;
+  return bsa_workspace_error(p, ptr, kNoAllocScratchBytes, 1, error_bits);
 }
 
 }  // extern "C"

@@ -262,7 +262,10 @@ __device__ __forceinline__ void fine_row(const __nv_bfloat16* __restrict__ q,
     }
     ps = warp_sum(ps);
     // P V for this lane's columns [CPL * lane, CPL * lane + CPL): one load of
-    // CPL bf16 per key, all independent.
+    // CPL bf16 per key, all independent.  Keys at or past `lim` (not in the
+    // cache yet, or after the row's position) are skipped, not multiplied by
+    // p = 0: their V rows may hold anything, NaN included.
+    const int64_t lim = s.causal ? min((int64_t)s.kv, (int64_t)pos + 1) : (int64_t)s.kv;
     float ob[CPL];
 #pragma unroll
     for (int i = 0; i < CPL; ++i) ob[i] = 0.f;
@@ -271,6 +274,7 @@ __device__ __forceinline__ void fine_row(const __nv_bfloat16* __restrict__ q,
 #pragma unroll 8
       for (int kk = 0; kk < 32; ++kk) {
         const float p = __shfl_sync(0xffffffffu, pl[t], kk);
+        if (key0 + 32 * t + kk >= lim) continue;   // the same for every lane
         const __nv_bfloat16* vr = Vu + (key0 + 32 * t + kk) * D + CPL * lane;
         if constexpr (CPL == 2) {
           const uint32_t w = ld_ro<NC>(reinterpret_cast<const uint32_t*>(vr));

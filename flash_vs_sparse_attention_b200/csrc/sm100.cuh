@@ -278,6 +278,13 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// The tcgen05.ld / tcgen05.st forms below are .sync.aligned: every thread of
+// the warp must execute them together.  Code before them is often divergent
+// (one lane arrives on a barrier or publishes progress), and a warp need not
+// have reconverged when the next instruction issues, so each helper starts
+// with __syncwarp(); without it a load could deliver another phase's columns
+// to some lanes depending on how the compiler schedules the branch.
+//
 // Load 32 consecutive fp32 columns of this warp's 32 TMEM lanes (thread i gets
 // lane base+i) and wait for the load in the same asm block, so no use of the
 // registers can be scheduled before the data has arrived.
@@ -292,6 +299,7 @@ __device__ __forceinline__ void tc_fence_after() {
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  __syncwarp();
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
       "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
@@ -304,6 +312,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 // Two 32-column loads (columns c and c+32) behind one wait.
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
   uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  __syncwarp();
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
       "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n"
@@ -319,6 +328,7 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
 // Store 16 consecutive 32-bit columns of this warp's 32 TMEM lanes, then wait
 // until the stores are complete.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  __syncwarp();
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
       "%14,%15,%16};\n"

@@ -187,7 +187,8 @@ size_t bsa_fine_workspace_bytes(const bsa_problem* p);
 
 /* Error bits the tensor-core fine stage left in a workspace (0 = clean; a
  * set bit names a pipeline wait that timed out and made the kernel stop
- * early).  `from_forward` selects a bsa_forward workspace (its last pass)
+ * early; the output of such a call is NaN, never stale numbers).
+ * `from_forward` selects a bsa_forward workspace (the bits of all its passes)
  * rather than a bsa_fine one.  Synchronises with the device. */
 int bsa_workspace_error(const bsa_problem* p, const void* workspace, size_t workspace_bytes,
                         int from_forward, uint32_t* error_bits);
@@ -201,7 +202,8 @@ int bsa_workspace_error(const bsa_problem* p, const void* workspace, size_t work
  * problem whose single (batch, head) unit needs more is rejected with
  * BSA_ERR_WORKSPACE (one unit needs about N*top_k*(2*D + 16) bytes, e.g.
  * N <= 16384 at D = 64, top_k = 16).  No cudaMalloc or other allocation.
- * The first call on a device looks up the array's device address (host-side
+ * The first call on a device (and the first after its context is replaced,
+ * e.g. by cudaDeviceReset) looks up the array's device address (host-side
  * set-up): make it before any stream capture.  All calls on a device share
  * the array: each call clears what must start at zero, but calls whose GPU
  * work overlaps (unordered streams) race on it.  Every GPU that loads this
@@ -210,6 +212,13 @@ int bsa_workspace_error(const bsa_problem* p, const void* workspace, size_t work
  * that GPU). */
 int bsa_forward_noalloc(const bsa_problem* p, const void* Q, const void* K, const void* V,
                         void* O, void* stream);
+
+/* The error bits of the last bsa_forward_noalloc call on the current device
+ * for problem p (as bsa_workspace_error reports them for a bsa_forward
+ * workspace; p must be the problem of that call).  Synchronises with the
+ * device.  Companion of bsa_forward_noalloc, likewise without a counterpart
+ * in the reference. */
+int bsa_noalloc_error(const bsa_problem* p, uint32_t* error_bits);
 
 #ifdef __cplusplus
 }

@@ -7,14 +7,15 @@ from oracle import CONFIGS, index_parity, make_inputs
 from oracle.block_indexer_np import _fine_rows, pool_k
 
 # Output tolerance of the bf16 path against the fp32 oracle: max-abs 2e-2 and
-# mean-abs 2e-3, where the max-abs bound widens to two bf16 units in the last
-# place (2**-7 * |O|) for |O| above ~2.6.  A bf16 output alone is off by up to
-# half an ulp (2**-9 * |O|), so at |O| in [8, 16) -- early causal rows of the
-# block-scaled workload -- no bf16 result, the reference's Triton variant's
-# included (block_indexer_triton.py:167), can meet a fixed 2e-2.
+# mean-abs 2e-3.  A bf16 result is off by up to half a unit in the last place
+# of |O| by its final rounding alone; below |O| = 8 that is at most 2^-6 and
+# the fixed 2e-2 holds, while at |O| >= 8 (early causal rows of the
+# block-scaled workload) half an ulp is already 2^-5 and no bf16 output -- the
+# reference Triton variant's single bf16 store (block_indexer_triton.py:81-83)
+# included -- can meet 2e-2.  There the bound is half an ulp plus 2^-10 |O|.
 MAX_ABS = 2e-2
-MAX_REL = 2.0 ** -7
 MEAN_ABS = 2e-3
+WIDEN_FROM = 8.0
 TAU = 1e-5
 
 
@@ -54,14 +55,23 @@ def oracle_fine(q, k, v, idx_rows, rows, block_size, causal):
                       np.asarray(idx_rows, np.int64), np.asarray(rows), causal, D ** -0.5)
 
 
+def max_abs_bound(want):
+    """Per-element max-abs bound: 2e-2, or at |O| >= 8 half a bf16 ulp of |O|
+    plus 2^-10 |O|."""
+    a = np.abs(np.asarray(want, np.float32))
+    half_ulp = np.exp2(np.floor(np.log2(np.maximum(a, WIDEN_FROM))) - 8.0)
+    return np.where(a >= WIDEN_FROM, np.maximum(MAX_ABS, half_ulp + a / 1024.0), MAX_ABS)
+
+
 def assert_close_out(got, want, what=""):
     got = np.asarray(got, np.float32)
     want = np.asarray(want, np.float32)
     err = np.abs(got - want)
     assert np.isfinite(got).all(), f"{what}: non-finite output"
-    bound = np.maximum(MAX_ABS, MAX_REL * np.abs(want))
+    bound = max_abs_bound(want)
     worst = np.unravel_index(np.argmax(err - bound), err.shape) if err.size else ()
     assert np.all(err <= bound), (f"{what}: error {err[worst]:.3e} at |O| = {abs(want[worst]):.3f} "
-                                  f"exceeds max(2e-2, 2^-7 |O|)")
+                                  f"exceeds its bound {bound[worst]:.3e}")
     assert err.mean() <= MEAN_ABS, f"{what}: mean-abs {err.mean():.3e} > {MEAN_ABS}"
-    return float(err.max()), float(err.mean())
+    wide = int(np.any(err > MAX_ABS, axis=-1).sum()) if err.ndim == 2 else int((err > MAX_ABS).sum())
+    return float(err.max()), float(err.mean()), wide

@@ -197,3 +197,40 @@ def test_decode_cache_grows_token_by_token(cuda):
         want = np.concatenate([decode_rows(Qn[0, u, t:t + 1], t, Kn[0, u], Vn[0, u], True, bs, k)
                                for t in range(1000, 1070)])
         assert_close_out(got[0, u], want, f"cache unit {u}")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bs", [64, 128])
+def test_cache_tail_past_the_keys_may_hold_nan(cuda, bs):
+    """The part of a cache past its keys is never read as data: filled with
+    NaN (as an unzeroed allocation may hold), it changes neither bsa_decode
+    nor bsa_decode_step."""
+    B, H, cap, D, k = 1, 2, 2048, 64, 8
+    kv_len = 1000                   # the last cached block is partly filled
+    Qn, Kn, Vn = (_rand((B, H, cap, D), s) for s in (21, 22, 23))
+    Q, K, V = to_gpu(Qn, Kn, Vn)
+    Kz, Vz = K.clone(), V.clone()
+    Kz[:, :, kv_len:] = 0
+    Vz[:, :, kv_len:] = 0
+    Kn_, Vn_ = K.clone(), V.clone()
+    Kn_[:, :, kv_len:] = float("nan")
+    Vn_[:, :, kv_len:] = float("nan")
+    outs = []
+    for Kc, Vc in ((Kz, Vz), (Kn_, Vn_)):
+        K_repr = torch.zeros(B, H, cap // bs, D, dtype=torch.float32, device=cuda)
+        bi.pool_k_blocks(Kc, K_repr, 0, -(-kv_len // bs), kv_len, bs)
+        q_pos = kv_len - 3
+        o = bi.decode(Q[:, :, q_pos:kv_len].contiguous(), q_pos, Kc, Vc, K_repr, True, bs, k)
+        # one step appending position kv_len - 1 again (the same key and value)
+        L = _lib.lib()
+        p = bi.problem(B, H, cap, D, True, bs, k)
+        o1 = torch.empty(B, H, 1, D, dtype=torch.bfloat16, device=cuda)
+        row = lambda x: x[:, :, kv_len - 1:kv_len].contiguous()   # noqa: E731
+        st = L.bsa_decode_step(ctypes.byref(p), bi._ptr(row(Q)), bi._ptr(row(K)), bi._ptr(row(V)),
+                               kv_len - 1, bi._ptr(Kc), bi._ptr(Vc), bi._ptr(K_repr), bi._ptr(o1),
+                               bi._stream(cuda))
+        assert st == _lib.BSA_OK, L.bsa_last_error()
+        outs.append((o, o1))
+    (a, a1), (b, b1) = outs
+    assert torch.isfinite(b.float()).all() and torch.isfinite(b1.float()).all()
+    assert torch.equal(a, b) and torch.equal(a1, b1)

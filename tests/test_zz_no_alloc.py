@@ -19,9 +19,6 @@ from flash_vs_sparse_attention_b200 import _lib, block_indexer_b200 as bi
 
 pytestmark = pytest.mark.gpu
 
-MAX_ABS = 2e-2
-MEAN_ABS = 2e-3
-
 
 def _inputs(B, H, N, D, seed):
     g = torch.Generator(device="cuda").manual_seed(seed)
@@ -46,21 +43,32 @@ def _forward_noalloc(L, p, Q, K, V):
     return O
 
 
-@pytest.mark.parametrize("shape", [(1, 2, 4096, 64, 64, 16, True), (1, 3, 2048, 128, 64, 32, True),
-                                   (2, 1, 1024, 32, 8, 4, False)])
+@pytest.mark.parametrize("shape", [
+    (1, 2, 4096, 64, 64, 16, True),
+    (1, 3, 2048, 128, 64, 32, True),
+    (2, 1, 1024, 32, 8, 4, False),
+    # One unit needs ~43 MiB of scratch here, so the 64 MiB array holds one
+    # unit per pass and the call runs four passes through the shared array.
+    (1, 4, 16384, 64, 64, 16, True),
+])
 def test_noalloc_matches_forward_two_calls(cuda, shape):
+    """Each unit's result does not depend on how many units share a pass, so
+    the no-allocation forward must equal bsa_forward bit for bit -- on two
+    calls in a row, the second reusing the first call's scratch contents."""
     B, H, N, D, bs, k, causal = shape
     L = _lib.lib()
     p = bi.problem(B, H, N, D, causal, bs, k)
-    for call, seed in enumerate((11, 12)):     # two calls in a row share the scratch
+    for call, seed in enumerate((11, 12)):
         Q, K, V = _inputs(B, H, N, D, seed)
-        want = _forward_with_workspace(L, p, Q, K, V).float()
-        got = _forward_noalloc(L, p, Q, K, V).float()
+        want = _forward_with_workspace(L, p, Q, K, V)
+        got = _forward_noalloc(L, p, Q, K, V)
         torch.cuda.synchronize()
-        err = (got - want).abs()
-        assert torch.isfinite(got).all(), f"call {call}: non-finite output"
-        assert err.max().item() <= MAX_ABS and err.mean().item() <= MEAN_ABS, (
-            f"call {call}: max-abs {err.max().item():.3e}, mean-abs {err.mean().item():.3e}")
+        assert torch.isfinite(got.float()).all(), f"call {call}: non-finite output"
+        assert torch.equal(got, want), (
+            f"call {call}: max-abs {(got.float() - want.float()).abs().max().item():.3e}")
+        bits = ctypes.c_uint32(0xffffffff)
+        assert L.bsa_noalloc_error(ctypes.byref(p), ctypes.byref(bits)) == _lib.BSA_OK
+        assert bits.value == 0, f"call {call}: error bits 0x{bits.value:x}"
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch(cuda):
