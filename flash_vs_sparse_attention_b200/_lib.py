@@ -24,6 +24,7 @@ BSA_ERR_CUDA = 5
 BSA_FLAG_SIMT_SELECT = 1
 BSA_FLAG_SIMT_FINE = 2
 BSA_FLAG_QBLOCK = 4
+BSA_FLAG_TEST_TIMEOUT = 8
 
 # Every function include/bsattn.h declares, with its ctypes signature.
 _c = ctypes
@@ -64,6 +65,7 @@ SIGNATURES = {
     "bsa_workspace_error": (_c.c_int, [_PP, _P, _c.c_size_t, _c.c_int, _c.POINTER(_c.c_uint32)]),
     "bsa_forward_noalloc": (_c.c_int, [_PP, _P, _P, _P, _P, _P]),
     "bsa_noalloc_error": (_c.c_int, [_PP, _c.POINTER(_c.c_uint32)]),
+    "bsa_workspace_error_offset": (_c.c_int, [_PP, _c.c_size_t, _c.c_int, _c.POINTER(_c.c_size_t)]),
     "bsa_host_workspace_bytes": (_c.c_size_t, [_PP, _c.c_int64]),
     "bsa_forward_host": (_c.c_int, [_PP, _P, _P, _P, _P, _c.c_int64, _P, _c.c_size_t, _P]),
     "bsa_pool_k_blocks": (_c.c_int, [_PP, _P, _P, _P, _c.c_int, _c.c_int, _c.c_int, _P]),

@@ -87,8 +87,57 @@ def _raise_on_kernel_error(L, p, ws, from_forward):
         raise RuntimeError(f"{VARIANT}: fine-stage kernel stopped early (error bits 0x{bits.value:x})")
 
 
+# Deferred error reports.  A pipeline wait of the tensor-core fine stage that
+# times out sets bits in the call's error word and makes that call's output
+# NaN.  Checking the word at once would synchronise every call, so by default
+# ``attention`` copies it into pinned host memory behind the forward (with an
+# event), and the next call on the device -- or ``raise_deferred_errors`` --
+# raises for any earlier call whose word has landed with bits set.
+_PENDING = {}          # device index -> [(event, pinned int32 tensor)]
+_MAX_PENDING = 64
+
+
+def _take_landed(device, wait):
+    lst = _PENDING.get(device.index, [])
+    keep, bits = [], 0
+    for ev, host in lst:
+        if wait:
+            ev.synchronize()
+        if ev.query():
+            bits |= int(host.item()) & 0xFFFFFFFF
+        else:
+            keep.append((ev, host))
+    _PENDING[device.index] = keep
+    if bits:
+        raise RuntimeError(f"{VARIANT}: an earlier call's fine-stage pipeline stopped early "
+                           f"(error bits 0x{bits:x}); that call's output is NaN")
+
+
+def raise_deferred_errors(device=None):
+    """Wait for the error words of this device's earlier ``attention`` calls
+    and raise ``RuntimeError`` if any of them reports a timed-out wait."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    _take_landed(dev, wait=True)
+
+
+def _defer_error_check(L, p, ws, device):
+    off = ctypes.c_size_t(0)
+    if L.bsa_workspace_error_offset(ctypes.byref(p), ctypes.c_size_t(ws.numel()), 1,
+                                    ctypes.byref(off)) != _lib.BSA_OK:
+        return                       # the CUDA-core fine stage keeps no error word
+    host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    host.copy_(ws[off.value:off.value + 4].view(torch.int32), non_blocking=True)
+    ev = torch.cuda.Event()
+    ev.record(torch.cuda.current_stream(device))
+    lst = _PENDING.setdefault(device.index, [])
+    lst.append((ev, host))
+    if len(lst) > _MAX_PENDING:      # bound the list: settle the oldest
+        lst[0][0].synchronize()
+        _take_landed(device, wait=False)
+
+
 def attention(Q, K, V, causal=False, block_size=64, top_k=16, *, flags=0,
-              workspace_cap=DEFAULT_WORKSPACE_CAP, check_errors=False):
+              workspace_cap=DEFAULT_WORKSPACE_CAP, check_errors=None):
     """
     Q, K, V: (batch, heads, seq_len, head_dim) bf16 CUDA tensors
     returns: (batch, heads, seq_len, head_dim) bf16
@@ -97,6 +146,12 @@ def attention(Q, K, V, causal=False, block_size=64, top_k=16, *, flags=0,
       Coarse: score each query against per-block mean-pooled keys; keep the
               top_k blocks per query token (ties to the lower block index).
       Fine:   exact softmax attention over the top_k * block_size keys kept.
+
+    check_errors: None (default) reports a timed-out pipeline wait without
+    synchronising -- this call's error word is copied behind the forward and
+    the next call (or ``raise_deferred_errors``) raises RuntimeError; True
+    synchronises and raises now; False does not look.  Such a call's output
+    is NaN either way.
     """
     L = _require_backend()
     B, H, N, D = Q.shape
@@ -107,6 +162,8 @@ def attention(Q, K, V, causal=False, block_size=64, top_k=16, *, flags=0,
     Qc, Kc, Vc = Q.contiguous(), K.contiguous(), V.contiguous()
     p = problem(B, H, N, D, causal, block_size, top_k, flags)
     with torch.cuda.device(Q.device):
+        if check_errors is None:
+            _take_landed(Q.device, wait=False)
         O = torch.empty_like(Qc)
         nbytes = workspace_bytes(p, workspace_cap)
         ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=Q.device)
@@ -115,11 +172,13 @@ def attention(Q, K, V, causal=False, block_size=64, top_k=16, *, flags=0,
         _lib.check(st, VARIANT)
         if check_errors:
             _raise_on_kernel_error(L, p, ws, True)
+        elif check_errors is None:
+            _defer_error_check(L, p, ws, Q.device)
     return O
 
 
 def attention_qblock(Q, K, V, causal=False, block_size=64, top_k=16, *, flags=0,
-                     workspace_cap=DEFAULT_WORKSPACE_CAP, check_errors=False):
+                     workspace_cap=DEFAULT_WORKSPACE_CAP, check_errors=None):
     """Per-query-block selection, a labelled variant (not the reference's
     per-token semantics): Q is mean-pooled per block like K; each query block
     of ``block_size`` rows takes the ``top_k`` key blocks of its pooled score

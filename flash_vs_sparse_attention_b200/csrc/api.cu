@@ -65,6 +65,7 @@ static Shape make_shape(const bsa_problem* p, int units) {
   s.Nq = s.N;
   s.q0 = 0;
   s.kv = s.N;
+  s.test_timeout = (p->flags & BSA_FLAG_TEST_TIMEOUT) ? 1 : 0;
   return s;
 }
 
@@ -512,13 +513,12 @@ int bsa_fine(const bsa_problem* p, const void* Q, const void* K, const void* V, 
   return e == cudaSuccess ? BSA_OK : cuda_fail(e, "fine launch");
 }
 
-int bsa_workspace_error(const bsa_problem* p, const void* workspace, size_t workspace_bytes,
-                        int from_forward, uint32_t* error_bits) {
+int bsa_workspace_error_offset(const bsa_problem* p, size_t workspace_bytes, int from_forward,
+                               size_t* offset) {
   g_last_error.clear();
   int st = check(p);
   if (st != BSA_OK) return st;
-  if (error_bits == nullptr) return fail(BSA_ERR_INVALID, "error_bits is NULL");
-  *error_bits = 0;
+  if (offset == nullptr) return fail(BSA_ERR_INVALID, "offset is NULL");
   int64_t units = total_units(p);
   size_t base = 0;
   if (from_forward) {
@@ -530,10 +530,29 @@ int bsa_workspace_error(const bsa_problem* p, const void* workspace, size_t work
     base = L.fine;
   }
   Shape s = make_shape(p, (int)units);
-  if (!fine_uses_tensor_cores(s, p->flags)) return BSA_OK;
-  size_t off = base + fine_kv_error_offset(s);
-  if (workspace == nullptr || off + 4 > workspace_bytes)
-    return fail(BSA_ERR_WORKSPACE, "workspace too small");
+  if (!fine_uses_tensor_cores(s, p->flags))
+    return fail(BSA_ERR_UNSUPPORTED, "this problem's fine stage keeps no error word");
+  const size_t off = base + fine_kv_error_offset(s);
+  if (off + 4 > workspace_bytes) return fail(BSA_ERR_WORKSPACE, "workspace too small");
+  *offset = off;
+  return BSA_OK;
+}
+
+int bsa_workspace_error(const bsa_problem* p, const void* workspace, size_t workspace_bytes,
+                        int from_forward, uint32_t* error_bits) {
+  g_last_error.clear();
+  int st = check(p);
+  if (st != BSA_OK) return st;
+  if (error_bits == nullptr) return fail(BSA_ERR_INVALID, "error_bits is NULL");
+  *error_bits = 0;
+  size_t off = 0;
+  st = bsa_workspace_error_offset(p, workspace_bytes, from_forward, &off);
+  if (st == BSA_ERR_UNSUPPORTED) {   // the CUDA-core fine stage never times out
+    g_last_error.clear();
+    return BSA_OK;
+  }
+  if (st != BSA_OK) return st;
+  if (workspace == nullptr) return fail(BSA_ERR_WORKSPACE, "workspace is NULL");
   cudaError_t e = cudaMemcpy(error_bits, (const unsigned char*)workspace + off, 4,
                              cudaMemcpyDeviceToHost);
   return e == cudaSuccess ? BSA_OK : cuda_fail(e, "reading the error word");

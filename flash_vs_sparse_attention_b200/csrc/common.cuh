@@ -85,6 +85,7 @@ struct Shape {
   int32_t Nq;          // query rows per unit (Q, O and idx unit stride)
   int32_t q0;          // position of query row 0
   int32_t kv;          // keys [0, kv) exist
+  int32_t test_timeout;  // BSA_FLAG_TEST_TIMEOUT: the fine kernel's test hook
 };
 
 }  // namespace bsa

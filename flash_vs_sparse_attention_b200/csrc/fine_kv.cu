@@ -66,7 +66,7 @@ constexpr int kRowBits = 14;   // staged entry: block << kRowBits | row in batch
 // Error codes ORed into the workspace error word.
 enum : uint32_t {
   kErrWaitQ = 1u, kErrWaitS = 2u, kErrWaitP = 4u, kErrWaitO = 8u, kErrWaitFree = 16u,
-  kErrWaitDrain = 32u, kErrWaitKV = 128u, kErrWaitEnt = 256u
+  kErrWaitDrain = 32u, kErrWaitKV = 128u, kErrWaitEnt = 256u, kErrTestTimeout = 512u
 };
 
 struct FineWs {
@@ -560,7 +560,7 @@ struct KvCfg {
   static_assert(kEntBytes % 16 == 0 && kMetaBytes % 16 == 0 && kRingOff % 16 == 0 &&
                     kEntOff % 16 == 0,
                 "alignment");
-  static_assert((2 * NQ + 2 * NKV + 5 * NWG + NG * kEntSlots) * 8 + 8 + 4 * (NWG + NKV) <= 512,
+  static_assert((2 * NQ + 2 * NKV + 5 * NWG + NG * kEntSlots + 1) * 8 + 8 + 4 * (NWG + NKV) <= 512,
                 "barrier area");
 };
 
@@ -598,7 +598,8 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
   uint64_t* o_full = p_full + NWG;              // [NWG] O in TMEM
   uint64_t* drain = o_full + NWG;               // [NWG] the group's MMAs are complete
   uint64_t* ent_full = drain + NWG;             // [NG * kEntSlots] a list slice landed
-  uint32_t* tmem_slot = (uint32_t*)(ent_full + C::NG * C::kEntSlots);
+  uint64_t* gate = ent_full + C::NG * C::kEntSlots;   // test hook: never completed
+  uint32_t* tmem_slot = (uint32_t*)(gate + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   int* o_done = (int*)(tmem_slot + 2);          // [NWG] last item whose O the group has seen
   int* run_last = o_done + NWG;                 // [NKV] last item of the slot's current run
@@ -629,6 +630,7 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
       o_done[g] = g - NWG;
     }
     for (int i = 0; i < C::NG * C::kEntSlots; ++i) mbar_init(&ent_full[i], 1);
+    mbar_init(gate, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -650,6 +652,17 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
   auto meta = [&](int st) { return (int32_t*)(smem + C::kMetaOff + st * C::kMetaBytes); };
   const float sc = s.scale * kLog2e;
 
+  // Test hook (BSA_FLAG_TEST_TIMEOUT): before any copy or MMA is issued, one
+  // bounded wait on a barrier that nothing completes.  It runs out after a
+  // few microseconds, reports kErrTestTimeout in the error word, and the CTA
+  // goes straight to its teardown -- the path a stuck pipeline takes, with
+  // nothing in flight.
+  if (s.test_timeout) {
+    if (threadIdx.x == 0 && !mbar_wait_ns(gate, 0, prm.err, kErrTestTimeout, 2000))
+      *abort_flag = 1;
+    __syncthreads();
+  }
+  if (*abort_flag == 0) {   // (the body runs unless the test hook stopped it)
   if (warp >= w_load) {
     // ------------------------------------------------------------ loaders
     // Each loader warp keeps its own ring of the work items, refilled half a
@@ -1072,6 +1085,7 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
       mbar_wait(&drain[wg], 0, prm.err, kErrWaitDrain);
     }
   }
+  }   // body
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

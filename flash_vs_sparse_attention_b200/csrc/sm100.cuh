@@ -78,6 +78,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   }
 }
 
+// mbar_wait with a given limit in nanoseconds (the test hook's short wait).
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                             uint32_t code, uint64_t limit_ns) {
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait(bar, parity, 1000u)) return true;
+    if (globaltimer() - t0 > limit_ns) {
+      if (err) atomicOr(err, code);
+      return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 // Tiled 2-D load of the tensor map's box at (x, y) into shared memory,
 // completing `bytes` on `bar`.  x is the innermost coordinate in elements.

@@ -16,7 +16,7 @@
  *
  * Tensors are dense, row-major (batch, heads, seq_len, head_dim) bf16 in
  * device memory (the reference's Triton path makes them contiguous too,
- * block_indexer_triton.py:116-117,199).  Every entry point enqueues work on
+ * block_indexer_triton.py:113,116-117,132).  Every entry point enqueues work on
  * the given stream and returns without synchronising; none allocates device
  * memory: scratch comes from the caller as a workspace of
  * bsa_workspace_bytes() bytes.  No entry point throws; each returns a
@@ -52,6 +52,11 @@ typedef enum bsa_status {
  * blocks j <= its own), and every query of the block attends to those
  * blocks' keys (token-level causal mask as usual). */
 #define BSA_FLAG_QBLOCK 4u
+/* Test only: the tensor-core fine stage makes one bounded wait on a barrier
+ * that nothing completes, before it issues any copy or MMA; the wait runs out
+ * after a few microseconds and the call ends with its error word set and a
+ * NaN output -- how a stuck pipeline is reported, exercised without one. */
+#define BSA_FLAG_TEST_TIMEOUT 8u
 
 typedef struct bsa_problem {
   int32_t batch;       /* B */
@@ -192,6 +197,14 @@ size_t bsa_fine_workspace_bytes(const bsa_problem* p);
  * rather than a bsa_fine one.  Synchronises with the device. */
 int bsa_workspace_error(const bsa_problem* p, const void* workspace, size_t workspace_bytes,
                         int from_forward, uint32_t* error_bits);
+
+/* Byte offset of that error word (a uint32) in such a workspace, so a caller
+ * can copy it asynchronously behind the forward instead of synchronising.
+ * BSA_ERR_UNSUPPORTED when the problem's fine stage keeps none (the
+ * CUDA-core path, which has no waits that can time out).  Host only.
+ * Companion of bsa_workspace_error; no counterpart in the reference. */
+int bsa_workspace_error_offset(const bsa_problem* p, size_t workspace_bytes, int from_forward,
+                               size_t* offset);
 
 /* bsa_forward without a workspace argument, for callers that cannot allocate
  * device memory where they run the attention (a memory pool they do not

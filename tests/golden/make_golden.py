@@ -4,9 +4,10 @@ Runs the reference's own ``attention/block_indexer.py`` (pure PyTorch, CPU,
 fp32) on seeded inputs and records its outputs plus, by wrapping
 ``torch.Tensor.topk`` for the duration of the call, the exact coarse scores it
 ranked and the indices it picked (block_indexer.py:53).  Needs the reference
-checkout, so it runs only where that exists:
+checkout, so it runs only where that exists; pass its path (or set
+BSA_REFERENCE_ROOT):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path to the reference checkout>
 
 Cases
   refshape_*  the reference test shape (test_correctness.py:6-14: seed 42,
@@ -168,7 +169,11 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    root = next((a for a in sys.argv[1:] if not a.startswith("--")), "/root/reference")
+    root = next((a for a in sys.argv[1:] if not a.startswith("--")),
+                os.environ.get("BSA_REFERENCE_ROOT", ""))
+    if not root or not os.path.isdir(os.path.join(root, "attention")):
+        sys.exit("usage: make_golden.py <reference checkout> [--flops-only] "
+                 "(or set BSA_REFERENCE_ROOT)")
     if "--flops-only" in sys.argv:
         flops_golden(root)
     else:

@@ -210,3 +210,27 @@ def test_tensor_core_path_is_deterministic(cuda, shape):
                                        V[:, u:u + 1].contiguous(), causal=True, block_size=bs,
                                        top_k=k) for u in range(Hd)], dim=1)
     assert torch.equal(per_unit, outs[0])
+
+
+def test_timed_out_wait_is_reported(cuda):
+    """A pipeline wait that runs out (forced by the test-only flag, before any
+    copy is issued) gives a NaN output and an error the default path raises:
+    at the next call, or at once with check_errors=True."""
+    gen = torch.Generator().manual_seed(5)
+    Q, K, V = (torch.randn(1, 2, 2048, 64, generator=gen).to(torch.bfloat16).cuda() for _ in range(3))
+    stuck = _lib.BSA_FLAG_TEST_TIMEOUT
+    bi.raise_deferred_errors(cuda)
+    out = bi.attention(Q, K, V, causal=True, flags=stuck)
+    assert torch.isnan(out.float()).all()
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="stopped early"):
+        bi.attention(Q, K, V, causal=True)          # the next call reports it
+    good = bi.attention(Q, K, V, causal=True)       # reported once; the device is fine
+    bi.raise_deferred_errors(cuda)
+    assert torch.isfinite(good.float()).all()
+    with pytest.raises(RuntimeError, match="stopped early"):
+        bi.attention(Q, K, V, causal=True, flags=stuck, check_errors=True)
+    bi.attention(Q, K, V, causal=True, flags=stuck)
+    with pytest.raises(RuntimeError, match="stopped early"):
+        bi.raise_deferred_errors(cuda)
+    assert torch.equal(bi.attention(Q, K, V, causal=True), good)

@@ -79,3 +79,24 @@ def test_noalloc_rejects_problems_beyond_its_scratch(cuda):
                                bi._stream(Q.device))
     assert st == _lib.BSA_ERR_WORKSPACE
     assert b"built-in scratch" in L.bsa_last_error()
+
+
+def test_noalloc_error_word_reports_a_timed_out_wait(cuda):
+    """bsa_noalloc_error reads the built-in scratch's error word: set after a
+    call whose pipeline wait ran out (the test-only flag forces one before any
+    copy is issued; that call's output is NaN), clear again after the next
+    regular call."""
+    L = _lib.lib()
+    B, H, N, D = 1, 2, 2048, 64
+    Q, K, V = _inputs(B, H, N, D, 21)
+    stuck = bi.problem(B, H, N, D, True, 64, 16, flags=_lib.BSA_FLAG_TEST_TIMEOUT)
+    out = _forward_noalloc(L, stuck, Q, K, V)
+    bits = ctypes.c_uint32(0)
+    assert L.bsa_noalloc_error(ctypes.byref(stuck), ctypes.byref(bits)) == _lib.BSA_OK
+    assert bits.value != 0
+    assert torch.isnan(out.float()).all()
+    p = bi.problem(B, H, N, D, True, 64, 16)
+    good = _forward_noalloc(L, p, Q, K, V)
+    assert L.bsa_noalloc_error(ctypes.byref(p), ctypes.byref(bits)) == _lib.BSA_OK
+    assert bits.value == 0
+    assert torch.equal(good, _forward_with_workspace(L, p, Q, K, V))
