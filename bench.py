@@ -209,7 +209,7 @@ def run_ours(args, cfg):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 
-    U = cfg["B"] * cfg["H"]
+    U = cfg["B"] * cfg["H"] if not args.units else args.units
     if args.scaling is None:
         args.scaling = "strong"   # one problem's (batch, head) units split over the ranks
     if args.scaling == "weak":
@@ -374,12 +374,16 @@ def run_ours(args, cfg):
                                      cfg["top_k"])
     achieved = fine_flops / (fine_ms * 1e-3) / 1e12 if fine_ms > 0 else None
     peak = float(peaks["bf16_tflops"])
+    # DRAM traffic of the fine kernel per (batch, head) unit, from a one-launch
+    # ncu capture of a smaller case (profiles/traffic.json), scaled by the
+    # units of this launch (the traffic grows in proportion to the units).
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
         try:
-            traffic = json.load(open(tpath)).get(f"config{args.config}", {}).get("fine")
-        except (OSError, ValueError):
+            per_unit = json.load(open(tpath)).get(f"config{args.config}", {}).get("fine_per_unit")
+            traffic = int(per_unit * pass_units) if per_unit else None
+        except (OSError, ValueError, TypeError):
             traffic = None
     stages = stage_model(cfg, pass_units, {k: statistics.mean(v) for k, v in stage_ms.items()},
                          peaks, peak_kind)
@@ -399,7 +403,8 @@ def run_ours(args, cfg):
                 "achieved": round(achieved, 2) if achieved else None, "peak": peak,
                 "unit": "TFLOP/s", "frac": round(achieved / peak, 4) if achieved else None,
                 "peak_source": f"{peak_kind} bf16_tflops (burst)",
-                "traffic": traffic, "traffic_unit": "bytes per launch (ncu, profiles/)",
+                "traffic": traffic,
+                "traffic_unit": "bytes per launch (ncu per-unit figure in profiles/traffic.json x units)",
                 "traffic_gbs": round(traffic / (fine_ms * 1e-3) / 1e9, 1) if traffic and fine_ms > 0 else None,
                 "flops_per_launch": fine_flops, "units_per_launch": pass_units,
                 "launch_ms": round(fine_ms, 4)}
@@ -412,7 +417,9 @@ def run_ours(args, cfg):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
             "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": workload_name(cfg), "units_per_gpu": my_units,
+            "config": {"workload": workload_name(cfg) + (
+                           f" (only {U} of {cfg['B'] * cfg['H']} units)" if args.units else ""),
+                       "units_per_gpu": my_units,
                        "total_units": total_units, "global_batch": cfg["B"] * (world if args.scaling == "weak" else 1),
                        "heads": cfg["H"], "seq_len": cfg["N"], "head_dim": cfg["D"],
                        "block_size": cfg["block_size"], "top_k": cfg["top_k"],
@@ -680,6 +687,9 @@ def main(argv=None):
     ap.add_argument("--cpu-rows", type=int, default=0,
                     help="query rows of unit 0 in the CPU timings (0: one whole unit for the "
                          "cpu_baseline key, the whole workload for --impl reference)")
+    ap.add_argument("--units", type=int, default=0,
+                    help="run only this many (batch, head) units of the workload (0: all); "
+                         "for small profiling captures, not for bench lines")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mode", default="forward", choices=["forward", "decode"],
