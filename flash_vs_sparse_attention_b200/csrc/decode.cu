@@ -13,12 +13,14 @@
 // order, -1 in slots left empty.
 //
 // Fine stage (block_size 32/64/128, head_dim 64/128; other shapes use the
-// general CUDA-core kernel): a CTA per new row, split over the selected
-// blocks.  Warp w takes slots w, w + 8, ...: lane l scores keys l, l + 32, ...
-// of the block (all K-row loads issued up front), exponentiates against the
-// block maximum, then accumulates P V for its own output columns with one
-// coalesced V-row load per key, all independent; the warp keeps a running
-// (m, l, O) over its blocks and the CTA merges the eight warps' states.
+// general CUDA-core kernel): a cluster of kDecCluster CTAs per new row.  The
+// row's selected blocks are cut into 32-key chunks spread over the cluster's
+// 64 warps; a warp loads its chunk's K rows and V rows together, scores,
+// exponentiates against the chunk maximum and accumulates P V, keeping a
+// running (m, l, O); each CTA merges its warps, then CTA 0 merges the CTAs
+// through distributed shared memory (fine_row_cluster).  The one-launch
+// decode step selects on the same cluster (cluster_pick: each CTA ranks a
+// part of the blocks, then the union of the parts' candidates).
 #include "common.cuh"
 #include "launchers.cuh"
 #include "rowops.cuh"
@@ -88,46 +90,127 @@ cudaError_t launch_qblock_select(const float* Q_repr, const float* K_repr, int32
 }
 
 // ---------------------------------------------------------------------------
+// A cluster of kDecCluster CTAs per new row (fine_row_cluster).
 template <int BS, int D>
-__global__ void __launch_bounds__(kDecFineWarps * 32)
+__global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(kDecFineWarps * 32)
 decode_fine_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restrict__ K,
                    const __nv_bfloat16* __restrict__ V, const int32_t* __restrict__ idx,
                    __nv_bfloat16* __restrict__ O, Shape s) {
-  const int64_t gr = blockIdx.x;
+  __shared__ float qs[D];
+  __shared__ int32_t row_idx[64], sel[64];   // top_k <= 64
+  __shared__ uint64_t state_bar;             // (CTA 0) the CTAs' partial states
+  const int tid = threadIdx.x;
+  const int64_t gr = blockIdx.x / kDecCluster;
   const int64_t unit = gr / s.Nq;
   const int pos = s.q0 + (int)(gr % s.Nq);
-  fine_row<BS, D, true>(Q + gr * D, K, V, idx + gr * s.k, O + gr * D, s, unit, pos);
+  if (tid == 0) {
+    sm100::mbar_init(&state_bar, 1);
+    if (cluster_rank() == 0) sm100::mbar_arrive_expect_tx(&state_bar, fine_state_bytes<D>());
+    sm100::fence_barrier_init();
+  }
+  for (int d = tid; d < D; d += blockDim.x) qs[d] = __bfloat162float(Q[gr * D + d]);
+  for (int t = tid; t < s.k; t += blockDim.x) row_idx[t] = idx[gr * s.k + t];
+  __syncthreads();
+  cluster_arrive();
+  // This CTA's part of the row's eligible blocks (as in the one-launch step)
+  // and the selected blocks in it, ascending.
+  const int nb_kv = (s.kv + BS - 1) / BS;
+  const int lim = s.causal ? min(nb_kv, pos / BS + 1) : nb_kv;
+  const int part = cluster_part(lim);
+  const int j0 = min(lim, (int)cluster_rank() * part), j1 = min(lim, j0 + part);
+  int n_sel = 0;
+  for (int t0 = 0; t0 < s.k; t0 += blockDim.x) {
+    const int t = t0 + tid;
+    const int j = t < s.k ? row_idx[t] : -1;
+    const bool mine = j >= j0 && j < j1;
+    if (mine) {
+      int slot = 0;
+      for (int u = 0; u < s.k; ++u) slot += (row_idx[u] >= j0 && row_idx[u] < j) ? 1 : 0;
+      sel[slot] = j;
+    }
+    n_sel += __syncthreads_count(mine);
+  }
+  fine_row_cluster<BS, D, true>(qs, K, V, sel, n_sel, O + gr * D, s, unit, pos, &state_bar,
+                                true, false, nullptr, nullptr, -1);
 }
 
-// One decode step in one launch, a CTA per unit: the new token's K and V rows
-// go into the cache at position s.q0, warp 0 re-pools the block they land in,
-// then the CTA selects the new row's blocks (into shared memory) and attends.
-// Every load of cache or block-mean data is an L2 load (NC = false): the CTA
-// itself wrote part of it a moment before.  Same arithmetic as
-// bsa_pool_k_blocks followed by bsa_decode.
+// One decode step in one launch, a cluster of kDecCluster CTAs per unit.
+// CTA r scores the eligible blocks [r * part, (r + 1) * part) (part =
+// cluster_part(eligible blocks)) against the new query row with the
+// sequential fp32 dot products of select_row.  The CTA whose part holds the
+// new token's block re-pools that block in its warp 0, reading the token's
+// key row from k_new (the same values and order as pooling the cache after
+// the append), scores it from the fresh mean, and writes the token's K and V
+// rows into the cache at position s.q0.  Every other load is issued at the
+// start, so the query row, the block means and the pooled block arrive in one
+// memory round trip.  Then cluster_pick (the exact top-k over the cluster)
+// and fine_row_cluster, which reads the token's own key and value from k_new
+// and v_new: no CTA reads what another wrote to global memory, so the CTAs
+// meet only through their shared-memory exchanges.  Same picks, block means
+// and output bits as bsa_pool_k_blocks followed by bsa_decode.
 template <int BS, int D>
-__global__ void __launch_bounds__(kDecSelThreads)
+__global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(kDecSelThreads)
 decode_step_kernel(const __nv_bfloat16* __restrict__ q_new, const __nv_bfloat16* __restrict__ k_new,
                    const __nv_bfloat16* __restrict__ v_new, __nv_bfloat16* __restrict__ K,
                    __nv_bfloat16* __restrict__ V, float* __restrict__ K_repr,
                    __nv_bfloat16* __restrict__ O, Shape s, int lanes_per_row) {
   static_assert(kDecSelThreads == kDecFineWarps * 32, "one CTA shape for all phases");
-  extern __shared__ __align__(16) float dsm[];   // selection: D + nb floats, 2 top_k ints
+  extern __shared__ __align__(16) float dsm[];   // PickSmem::bytes
+  __shared__ uint64_t bars[2];                   // candidates; (CTA 0) partial states
   const int tid = threadIdx.x;
-  const int64_t unit = blockIdx.x;
-  const int pos = s.q0;
-  const int64_t row = (unit * s.N + pos) * (int64_t)D;
-  for (int d = tid; d < D; d += kDecSelThreads) {
-    K[row + d] = k_new[unit * D + d];
-    V[row + d] = v_new[unit * D + d];
+  if (tid == 0) {
+    sm100::mbar_init(&bars[0], 1);
+    sm100::mbar_init(&bars[1], 1);
+    if (cluster_rank() == 0) sm100::mbar_arrive_expect_tx(&bars[1], fine_state_bytes<D>());
+    sm100::fence_barrier_init();
   }
-  __syncthreads();
-  if (tid < 32) pool_block_warp<false>(K, K_repr, nullptr, nullptr, s, lanes_per_row, unit,
-                                       pos / BS, tid);
-  __syncthreads();
-  int32_t* sel = reinterpret_cast<int32_t*>(dsm + D + s.nb) + s.k;   // after the picks
-  select_row<false, false>(q_new, K_repr, sel, s, unit, dsm);
-  fine_row<BS, D, false>(q_new + unit * D, K, V, sel, O + unit * D, s, unit, pos);
+  cluster_arrive();                              // waited for in cluster_pick
+  PickSmem sm;
+  sm.carve(dsm, D, s.nb, s.k);
+  const int64_t unit = blockIdx.x / kDecCluster;
+  const int pos = s.q0;
+  const int bp = pos / BS;                       // the new token's block
+  const int nb_kv = (s.kv + BS - 1) / BS;
+  const int lim = s.causal ? min(nb_kv, bp + 1) : nb_kv;   // eligible: [0, lim)
+  const int part = cluster_part(lim);
+  const int j0 = min(lim, (int)cluster_rank() * part), n_loc = min(lim, j0 + part) - j0;
+  const int own = (bp >= j0 && bp < j0 + n_loc) ? bp - j0 : -1;
+  const __nv_bfloat16* q = q_new + unit * D;
+  const __nv_bfloat16* kn = k_new + unit * D;
+  const __nv_bfloat16* vn = v_new + unit * D;
+  if (tid < D) sm.qf[tid] = __bfloat162float(q[tid]);
+  if (own >= 0 && tid < 32) {
+    // The token's rows are loaded with the pool's loads and stored after it.
+    const bool cp = tid < D / 8;
+    uint4 kc = make_uint4(0u, 0u, 0u, 0u), vc = kc;
+    if (cp) {
+      kc = __ldg(reinterpret_cast<const uint4*>(kn) + tid);
+      vc = __ldg(reinterpret_cast<const uint4*>(vn) + tid);
+    }
+    pool_block_warp<true>(K, K_repr, nullptr, nullptr, s, lanes_per_row, unit, bp, tid, kn,
+                          pos - bp * BS, sm.mean);
+    if (cp) {
+      const int64_t row = (unit * s.N + pos) * (int64_t)D;
+      reinterpret_cast<uint4*>(K + row)[tid] = kc;
+      reinterpret_cast<uint4*>(V + row)[tid] = vc;
+    }
+  }
+  // The only block mean written here is the new block's, which is not read.
+  const float* kr = K_repr + unit * s.nb * (int64_t)D;
+  if (tid >= 32) {
+    for (int i = tid - 32; i < n_loc; i += kDecSelThreads - 32)
+      if (i != own) sm.sc[i] = score_block<true>(q, kr + (int64_t)(j0 + i) * D, D, s.scale);
+  }
+  __syncthreads();                               // sm.qf and sm.mean complete
+  if (own >= 0 && tid == 32) {
+    float a = 0.f;
+    for (int d = 0; d < D; ++d) a = fmaf(sm.qf[d], sm.mean[d], a);
+    sm.sc[own] = a * s.scale;
+  }
+  const int n_own = cluster_pick(sm, n_loc, j0, s, &bars[0], K + unit * s.N * (int64_t)D,
+                                 V + unit * s.N * (int64_t)D, (uint32_t)(BS * D * 2));
+  fine_row_cluster<BS, D, true>(sm.qf, K, V, sm.sel, max(n_own, 0), O + unit * D, s, unit, pos,
+                                &bars[1], false, n_own < 0, kn, vn, pos);
 }
 
 bool decode_fine_supported(const Shape& s) {
@@ -141,7 +224,8 @@ cudaError_t launch_decode_step(const __nv_bfloat16* q_new, const __nv_bfloat16* 
   if (s.units == 0) return cudaSuccess;
   int lpr = 1;
   while (lpr < (s.D >> 3)) lpr <<= 1;
-  const size_t smem = sizeof(float) * ((size_t)s.D + s.nb) + 2 * sizeof(int32_t) * s.k;
+  const size_t smem = PickSmem::bytes(s.D, s.nb, s.k);
+  if ((int64_t)s.units * kDecCluster > 0x7fffffffLL) return cudaErrorInvalidValue;
 #define BSA_DECODE_STEP(BS_, D_)                                                         \
   if (s.bs == BS_ && s.D == D_) {                                                        \
     if (smem > 48 * 1024) {                                                              \
@@ -150,7 +234,8 @@ cudaError_t launch_decode_step(const __nv_bfloat16* q_new, const __nv_bfloat16* 
                                            (int)smem);                                   \
       if (e != cudaSuccess) return e;                                                    \
     }                                                                                    \
-    decode_step_kernel<BS_, D_><<<(unsigned)s.units, kDecSelThreads, smem, st>>>(        \
+    decode_step_kernel<BS_, D_><<<(unsigned)(s.units * kDecCluster), kDecSelThreads, smem, \
+                                  st>>>(                                                 \
         q_new, k_new, v_new, K, V, K_repr, O, s, lpr);                                   \
     return cudaGetLastError();                                                           \
   }
@@ -169,7 +254,8 @@ cudaError_t launch_decode_fine(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                                const Shape& s, cudaStream_t st) {
   const int64_t rows = (int64_t)s.units * s.Nq;
   if (rows == 0) return cudaSuccess;
-  const dim3 grid((unsigned)rows), block(kDecFineWarps * 32);
+  if (rows * kDecCluster > 0x7fffffffLL) return cudaErrorInvalidValue;
+  const dim3 grid((unsigned)(rows * kDecCluster)), block(kDecFineWarps * 32);
 #define BSA_DECODE_FINE(BS_, D_)                                                         \
   if (s.bs == BS_ && s.D == D_) {                                                        \
     decode_fine_kernel<BS_, D_><<<grid, block, 0, st>>>(Q, K, V, idx, O, s);             \
