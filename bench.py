@@ -636,6 +636,18 @@ def run_decode(args, cfg):
         torch.cuda.synchronize()
     ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
     ms_step = sum(ms) / len(ms)
+    # The floor of this timing pattern: the same flush and event pair around
+    # a one-element fill (one tiny kernel, no memory traffic to speak of).
+    tiny = torch.zeros(1, device=dev)
+    floor = []
+    for j in range(args.steps):
+        flush.zero_()
+        starts[j].record()
+        tiny.fill_(1.0)
+        ends[j].record()
+    torch.cuda.synchronize()
+    floor = sorted(a.elapsed_time(b) for a, b in zip(starts, ends))
+    floor_ms = floor[len(floor) // 2]
     # HBM bytes a step must move: the visible block means (fp32), the top_k
     # selected blocks' K and V, the new row's Q, K, V in and O out, and the
     # re-pooled block (its keys in, its mean out).
@@ -665,7 +677,11 @@ def run_decode(args, cfg):
                      "frac": round(achieved / float(peaks["hbm_gbs"]), 5),
                      "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
                      "bytes_per_step": step_bytes,
-                     "note": "one launch of 8 CTAs per step; at a few MB the step is launch-latency bound"},
+                     "note": "one launch per step, a cluster of 8 CTAs per unit; at a few MB the step is "
+                             "bound by dependent memory round trips and the launch",
+                     "event_floor_ms": round(floor_ms, 5),
+                     "event_floor_note": "median of the same flush + event pair around a one-element "
+                                         "fill: launch and event overhead, not step work"},
         "clocks": clk.summary(), "gpu_launches": args.steps,
         "cpu_baseline": {"value": round(cpu_ms, 3), "unit": "ms", "cores": 1, "kind": "port",
                          "sample": f"one decode step of all {U} units (the last position) through the "

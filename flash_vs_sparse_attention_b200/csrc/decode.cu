@@ -13,14 +13,17 @@
 // order, -1 in slots left empty.
 //
 // Fine stage (block_size 32/64/128, head_dim 64/128; other shapes use the
-// general CUDA-core kernel): a cluster of kDecCluster CTAs per new row.  The
-// row's selected blocks are cut into 32-key chunks spread over the cluster's
-// 64 warps; a warp loads its chunk's K rows and V rows together, scores,
-// exponentiates against the chunk maximum and accumulates P V, keeping a
-// running (m, l, O); each CTA merges its warps, then CTA 0 merges the CTAs
-// through distributed shared memory (fine_row_cluster).  The one-launch
-// decode step selects on the same cluster (cluster_pick: each CTA ranks a
-// part of the blocks, then the union of the parts' candidates).
+// general CUDA-core kernel): a cluster of kDecCluster CTAs per new row, CTA r
+// attending the selected blocks in part r of the row's eligible range
+// (cluster_part).  A CTA cuts its blocks into 32-key chunks over its warps; a
+// warp loads a chunk's K rows and V rows together, scores, exponentiates
+// against the chunk maximum and accumulates P V, keeping a running (m, l, O);
+// each CTA merges its warps and sends its state to CTA 0 through distributed
+// shared memory, which merges the CTAs in rank order (fine_row_cluster).  The
+// one-launch decode step selects on the same cluster (cluster_pick: each CTA
+// ranks its part, the parts' candidates are exchanged, and each CTA keeps the
+// global picks that fall in its part), so both paths attend the same blocks
+// with the same arithmetic.
 #include "common.cuh"
 #include "launchers.cuh"
 #include "rowops.cuh"

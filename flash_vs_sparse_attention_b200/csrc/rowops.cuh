@@ -109,7 +109,7 @@ __device__ __forceinline__ void pool_block_warp(const __nv_bfloat16* __restrict_
 }
 
 // ---------------------------------------------------------------------------
-constexpr int kDecSelThreads = 256;
+constexpr int kDecSelThreads = 512;
 
 // The whole CTA (kDecSelThreads threads): the top_k blocks of one query row
 // `gr` (of s.units * s.Nq) into out[0, top_k), ascending, -1 padded.  POOLED:
@@ -211,7 +211,7 @@ __device__ __forceinline__ void select_row(const void* __restrict__ Qv,
 // of the receiving CTA, which waits there (bounded): no cluster-wide barrier
 // and no ordering of global memory between the CTAs is needed.
 constexpr int kDecCluster = 8;
-constexpr int kDecFineWarps = 8;
+constexpr int kDecFineWarps = 16;
 // Candidates per CTA whose K and V blocks are prefetched into L2 while the
 // cluster's picks are exchanged.
 constexpr int kDecPrefetch = 4;
@@ -484,7 +484,8 @@ __host__ __device__ constexpr uint32_t fine_state_bytes() {
 // selected blocks of its own part of the eligible range (cluster_part), given
 // in `sel` (n_sel blocks, ascending).  Key `key_new` (when k_new is non-null)
 // is read from k_new / v_new instead of the cache.  Work item i is the 32-key
-// chunk i % (BS / 32) of sel[i / (BS / 32)]; warp w takes items w, w + 8, ...
+// chunk i % (BS / 32) of sel[i / (BS / 32)]; warp w takes items w, w + W, ...
+// (W = kDecFineWarps).
 // For an item, lane
 // l loads key row key0 + l and, at the same time, the V chunks of its P V
 // share (16-byte column chunk l % (D / 8) of the keys congruent to
