@@ -25,6 +25,8 @@ BSA_FLAG_SIMT_SELECT = 1
 BSA_FLAG_SIMT_FINE = 2
 BSA_FLAG_QBLOCK = 4
 BSA_FLAG_TEST_TIMEOUT = 8
+BSA_FLAG_FINE_KEY_STATIONARY = 16
+BSA_FLAG_FINE_QUERY_STATIONARY = 32
 
 # Every function include/bsattn.h declares, with its ctypes signature.
 _c = ctypes

@@ -30,7 +30,8 @@ cudaError_t launch_fine(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __
                         const Shape& s, uint32_t flags, cudaStream_t st, int* n_launches,
                         void* const* events, int n_events, bool pre_zeroed) {
   if (fine_uses_tensor_cores(s, flags) && ws_bytes >= fine_kv_workspace_bytes(s))
-    return launch_fine_kv(Q, K, V, idx, O, ws, s, st, n_launches, events, n_events, pre_zeroed);
+    return launch_fine_kv(Q, K, V, idx, O, ws, s, flags, st, n_launches, events, n_events,
+                          pre_zeroed);
   // The CUDA-core path has no bucket or combine kernel: it is all "fine".
   *n_launches = 1;
   if (events != nullptr && n_events > 2 && events[2] != nullptr)

@@ -71,7 +71,7 @@ enum : uint32_t {
 
 struct FineWs {
   uint32_t* err;       // [0] error bits (16 bytes)                  } zeroed before
-  uint32_t* ctr;       // [0] total work items (16 bytes)             } the stage (the
+  uint32_t* ctr;       // [0] total work items, [2] query tiles       } the stage (the
                        //                                                error word only
                        //                                                before the first
                        //                                                pass of a call)
@@ -81,6 +81,9 @@ struct FineWs {
   int32_t* offsets;    // units * nb: a block's first position in its unit's list
   int32_t* item_row;   // units * nb: 128 * (a block's first work item)
   int32_t* vexp;       // units * nb: the block's partial-output scale exponent
+  uint8_t* tile_mode;  // units * tiles: 1 = the 128-row tile is a query tile (fine_q.cu)
+  int4* qt_info;       // units * tiles: (unit, tile, union size) of query-tile slot i
+  uint32_t* qt_bits;   // units * tiles * nbw: the union bitmask of slot i
   int4* items;         // units * max_items_per_unit
   int32_t* lists;      // units * N * k: query rows grouped by block
   int32_t* inv;        // units * N * k: (query, slot) -> partial row
@@ -133,6 +136,12 @@ static FineWs fine_ws_layout(const Shape& s, unsigned char* base) {
   w.offsets = (int32_t*)take(4 * U * nb);
   w.item_row = (int32_t*)take(4 * U * nb);
   w.vexp = (int32_t*)take(4 * U * nb);
+  {
+    const size_t tiles = (size_t)(s.N + kTileRows - 1) / kTileRows, nbw = (nb + 31) / 32;
+    w.tile_mode = (uint8_t*)take(U * tiles);
+    w.qt_info = (int4*)take(16 * U * tiles);
+    w.qt_bits = (uint32_t*)take(4 * U * tiles * nbw);
+  }
   w.items = (int4*)take(16 * U * (size_t)max_items_per_unit(s));
   w.lists = (int32_t*)take(4 * (U * Nk + 256));   // slack for aligned list-slice copies
   w.inv = (int32_t*)take(4 * U * Nk);
@@ -173,22 +182,31 @@ __device__ __forceinline__ int batch_entry(int i) {
              : (int)threadIdx.x + kBucketThreads * i;
 }
 
+// Entries of rows in query tiles (tm[row / 128] != 0, tm indexed from the
+// unit's first tile; null: none) read as empty: those rows belong to the
+// query-stationary kernel.  Row of entry e of the batch: row0 + e / k, with
+// e / k from the float product (e < 2^14; see bucket_scatter_kernel).
 template <bool VEC>
 __device__ __forceinline__ void load_batch(const int32_t* __restrict__ src, int n,
-                                           int (&v)[kBucketPer]) {
+                                           int (&v)[kBucketPer], const uint8_t* tm, int row0,
+                                           float inv_k) {
+  auto in_q_tile = [&](int e) {
+    return tm != nullptr && tm[(row0 + __float2int_rz(((float)e + 0.5f) * inv_k)) / kTileRows] != 0;
+  };
   if constexpr (VEC) {
     const int4* s4 = reinterpret_cast<const int4*>(src);
 #pragma unroll
     for (int i = 0; i < kBucketPer / 4; ++i) {
       const int q = (int)threadIdx.x + kBucketThreads * i;
-      const int4 x = 4 * q < n ? __ldcg(s4 + q) : make_int4(-1, -1, -1, -1);
+      int4 x = 4 * q < n ? __ldcg(s4 + q) : make_int4(-1, -1, -1, -1);
+      if (4 * q < n && in_q_tile(4 * q)) x = make_int4(-1, -1, -1, -1);   // k % 4 == 0: one row
       v[4 * i] = x.x; v[4 * i + 1] = x.y; v[4 * i + 2] = x.z; v[4 * i + 3] = x.w;
     }
   } else {
 #pragma unroll
     for (int i = 0; i < kBucketPer; ++i) {
       const int e = batch_entry<false>(i);
-      v[i] = e < n ? __ldcg(src + e) : -1;
+      v[i] = (e < n && !in_q_tile(e)) ? __ldcg(src + e) : -1;
     }
   }
 }
@@ -279,13 +297,17 @@ bucket_count_kernel(const int32_t* __restrict__ idx, int32_t* __restrict__ curso
                     int32_t* __restrict__ chunk_rel, int32_t* __restrict__ done,
                     int32_t* __restrict__ offsets, int32_t* __restrict__ item_row,
                     int4* __restrict__ items, uint32_t* __restrict__ ctr,
-                    const __nv_bfloat16* __restrict__ V, int32_t* __restrict__ vexp, Shape s,
-                    BucketGeom g) {
+                    const __nv_bfloat16* __restrict__ V, int32_t* __restrict__ vexp,
+                    const uint8_t* __restrict__ tile_mode, Shape s, BucketGeom g, float inv_k) {
   extern __shared__ int32_t hist[];
   __shared__ int32_t wsum_c[kBucketThreads / 32], wsum_t[kBucketThreads / 32];
   __shared__ int32_t ticket, item_base;
   const int u = blockIdx.y, chunk = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint8_t* tm =
+      tile_mode == nullptr ? nullptr
+                           : tile_mode + (int64_t)u * ((s.N + kTileRows - 1) / kTileRows);
+
   {
     // Side job: the partial-output scale exponents of this chunk's share of
     // the unit's key blocks.
@@ -300,7 +322,7 @@ bucket_count_kernel(const int32_t* __restrict__ idx, int32_t* __restrict__ curso
   for (int row0 = chunk * g.chunk_rows; row0 < row_end; row0 += g.rows_batch) {
     const int n = min(g.rows_batch, row_end - row0) * s.k;
     int v[kBucketPer];
-    load_batch<VEC>(idx + ((int64_t)u * s.N + row0) * s.k, n, v);
+    load_batch<VEC>(idx + ((int64_t)u * s.N + row0) * s.k, n, v, tm, row0, inv_k);
 #pragma unroll
     for (int i = 0; i < kBucketPer; ++i)
       if (v[i] >= 0) atomicAdd(&hist[v[i]], 1);
@@ -377,8 +399,9 @@ template <bool VEC>
 __global__ void __launch_bounds__(kBucketThreads, 2)
 bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ chunk_rel,
                       const int32_t* __restrict__ offsets, const int32_t* __restrict__ item_row,
-                      int32_t* __restrict__ lists, int32_t* __restrict__ inv, Shape s,
-                      BucketGeom g, float inv_k) {
+                      int32_t* __restrict__ lists, int32_t* __restrict__ inv,
+                      const uint8_t* __restrict__ tile_mode, Shape s, BucketGeom g,
+                      float inv_k) {
   extern __shared__ int32_t smem_i[];
   int32_t* cnt = smem_i;                 // nb: batch counts -> local prefix -> local cursor
   int32_t* gap = smem_i + s.nb;          // nb: the block's cursor minus its local prefix
@@ -387,6 +410,9 @@ bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict
   const int u = blockIdx.y, chunk = blockIdx.x;
   const int t = threadIdx.x;
   const int per = (s.nb + kBucketThreads - 1) / kBucketThreads;
+  const uint8_t* tm =
+      tile_mode == nullptr ? nullptr
+                           : tile_mode + (int64_t)u * ((s.N + kTileRows - 1) / kTileRows);
   // Thread t owns blocks t + kBucketThreads m (the layout is in that order).
   const int32_t* start = chunk_rel + ((int64_t)u * g.chunks + chunk) * s.nb;
   for (int j = t; j < s.nb; j += kBucketThreads) { gap[j] = start[j]; cnt[j] = 0; }
@@ -399,7 +425,7 @@ bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict
     const int n = min(g.rows_batch, row_end - row0) * s.k;
     const int64_t e0 = ((int64_t)u * s.N + row0) * s.k;
     int v[kBucketPer];
-    load_batch<VEC>(idx + e0, n, v);
+    load_batch<VEC>(idx + e0, n, v, tm, row0, inv_k);
 #pragma unroll
     for (int i = 0; i < kBucketPer; ++i)
       if (v[i] >= 0) atomicAdd(&cnt[v[i]], 1);
@@ -1110,7 +1136,8 @@ template <int HD, int KMAX>
 __global__ void __launch_bounds__(256)
 combine_kernel(const int32_t* __restrict__ inv,
                const __half* __restrict__ part_o, const float2* __restrict__ part_ml,
-               const uint32_t* __restrict__ err, __nv_bfloat16* __restrict__ O, Shape s) {
+               const uint32_t* __restrict__ err, const uint8_t* __restrict__ tile_mode,
+               __nv_bfloat16* __restrict__ O, Shape s) {
   constexpr int CH = HD / 8;           // threads per row (8 or 16), a power of two <= 32
   constexpr int PER = (KMAX + CH - 1) / CH;   // slots whose metadata one thread loads
   const int64_t rows = (int64_t)s.units * s.N;
@@ -1118,6 +1145,12 @@ combine_kernel(const int32_t* __restrict__ inv,
   const int c = (int)(gid % CH);
   const bool live = gid / CH < rows;
   const int64_t R = live ? gid / CH : rows - 1;   // dead lanes mirror a real row
+  // Rows of query tiles are written by the query-stationary kernel.  A
+  // warp's 32 / CH rows are consecutive and aligned, so within one tile.
+  const int tiles = (s.N + kTileRows - 1) / kTileRows;
+  const bool q_row = tile_mode != nullptr &&
+                     tile_mode[(R / s.N) * tiles + (R % s.N) / kTileRows] != 0;
+  if (__all_sync(0xffffffffu, q_row)) return;
   const int lane = threadIdx.x & 31, base = lane & ~(CH - 1);
   const int32_t* prow = inv + R * s.k;   // -1: empty slot
   int32_t pr[PER];
@@ -1177,7 +1210,7 @@ combine_kernel(const int32_t* __restrict__ inv,
     acc[4] = fmaf(wt, x2.x, acc[4]); acc[5] = fmaf(wt, x2.y, acc[5]);
     acc[6] = fmaf(wt, x3.x, acc[6]); acc[7] = fmaf(wt, x3.y, acc[7]);
   }
-  if (!live) return;
+  if (!live || q_row) return;
   // 2^(A - B) / L in two factors, each well inside the float range.  If a
   // pipeline wait of this call timed out (error word set), the partials may
   // be stale: the output becomes NaN rather than plausible numbers.
@@ -1192,15 +1225,16 @@ combine_kernel(const int32_t* __restrict__ inv,
 }
 
 template <int HD>
-static void launch_combine(const FineWs& w, __nv_bfloat16* O, const Shape& s, cudaStream_t st) {
+static void launch_combine(const FineWs& w, const uint8_t* tm, __nv_bfloat16* O, const Shape& s,
+                           cudaStream_t st) {
   const int64_t threads = (int64_t)s.units * s.N * (HD / 8);
   const unsigned blocks = (unsigned)((threads + 255) / 256);
   if (s.k <= 16)
-    combine_kernel<HD, 16><<<blocks, 256, 0, st>>>(w.inv, w.part_o, w.part_ml, w.err, O, s);
+    combine_kernel<HD, 16><<<blocks, 256, 0, st>>>(w.inv, w.part_o, w.part_ml, w.err, tm, O, s);
   else if (s.k <= 32)
-    combine_kernel<HD, 32><<<blocks, 256, 0, st>>>(w.inv, w.part_o, w.part_ml, w.err, O, s);
+    combine_kernel<HD, 32><<<blocks, 256, 0, st>>>(w.inv, w.part_o, w.part_ml, w.err, tm, O, s);
   else
-    combine_kernel<HD, 64><<<blocks, 256, 0, st>>>(w.inv, w.part_o, w.part_ml, w.err, O, s);
+    combine_kernel<HD, 64><<<blocks, 256, 0, st>>>(w.inv, w.part_o, w.part_ml, w.err, tm, O, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -1275,8 +1309,8 @@ static cudaError_t launch_kv_kernel(const __nv_bfloat16* Q, const __nv_bfloat16*
 
 cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                            const __nv_bfloat16* V, const int32_t* idx, __nv_bfloat16* O,
-                           unsigned char* ws, const Shape& s, cudaStream_t st, int* n_launches,
-                           void* const* events, int n_events, bool pre_zeroed) {
+                           unsigned char* ws, const Shape& s, uint32_t flags, cudaStream_t st,
+                           int* n_launches, void* const* events, int n_events, bool pre_zeroed) {
   FineWs w = fine_ws_layout(s, ws);
   auto mark = [&](int i) {
     if (events != nullptr && i < n_events && events[i] != nullptr)
@@ -1284,6 +1318,14 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
   };
   cudaError_t e = cudaSuccess;
   if (!pre_zeroed && (e = cudaMemsetAsync(w.err, 0, w.zero_bytes, st)) != cudaSuccess) return e;
+  // Per-tile dispatch: query tiles (few distinct blocks between their rows)
+  // go to the query-stationary kernel, the rest through the buckets.
+  const int max_union = fine_q_supported(s) ? fine_q_max_union(s, flags) : 0;
+  const uint8_t* tm = max_union > 0 ? w.tile_mode : nullptr;
+  if (max_union > 0 &&
+      (e = launch_classify_tiles(idx, w.tile_mode, w.qt_bits, w.qt_info, w.ctr + 2, s, max_union,
+                                 st)) != cudaSuccess)
+    return e;
   const BucketGeom g = bucket_geom(s);
   const dim3 bgrid(g.chunks, s.units);
   const size_t count_smem = sizeof(int32_t) * s.nb;
@@ -1301,9 +1343,10 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
     return e;
   count_k<<<bgrid, kBucketThreads, count_smem, st>>>(idx, w.cursor, w.chunk_rel, w.done,
                                                      w.offsets, w.item_row, w.items, w.ctr, V,
-                                                     w.vexp, s, g);
+                                                     w.vexp, tm, s, g, 1.0f / (float)s.k);
   scatter_k<<<bgrid, kBucketThreads, scatter_smem, st>>>(idx, w.chunk_rel, w.offsets, w.item_row,
-                                                         w.lists, w.inv, s, g, 1.0f / (float)s.k);
+                                                         w.lists, w.inv, tm, s, g,
+                                                         1.0f / (float)s.k);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   mark(2);
   if (s.bs == 64 && s.D == 64) e = launch_kv_kernel<64, 64>(Q, K, V, w, s, st);
@@ -1311,12 +1354,16 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
   else if (s.bs == 128 && s.D == 64) e = launch_kv_kernel<128, 64>(Q, K, V, w, s, st);
   else e = cudaErrorNotSupported;
   if (e != cudaSuccess) return e;
+  if (max_union > 0 &&
+      (e = launch_fine_q(Q, K, V, idx, O, w.qt_bits, w.qt_info, w.ctr + 2, w.err, s, st)) !=
+          cudaSuccess)
+    return e;
   mark(3);
-  if (s.D == 64) launch_combine<64>(w, O, s, st);
-  else launch_combine<128>(w, O, s, st);
+  if (s.D == 64) launch_combine<64>(w, tm, O, s, st);
+  else launch_combine<128>(w, tm, O, s, st);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   mark(4);
-  *n_launches = 4;
+  *n_launches = max_union > 0 ? 6 : 4;
   return cudaSuccess;
 }
 

@@ -1,0 +1,604 @@
+// Stage 4, query-stationary (block_indexer_triton.py:12-83 mapped the way the
+// reference's Triton kernel maps it: a program per query tile walking key
+// blocks), on tcgen05 tensor cores, for the 128-row query tiles whose rows
+// between them select few distinct key blocks.
+//
+// Per-tile dispatch.  classify_tiles_kernel looks at every 128-row tile of
+// every unit: the union of the key blocks its rows selected (a bitmask) and
+// its size U.  A tile whose rows all list strictly increasing block indices
+// (no repeats: a repeated block must count twice, as the key-block-stationary
+// path counts it) and whose U is at most max_union becomes a query tile: it
+// gets a slot (its unit, tile and U, and the union bitmask), and tile_mode
+// marks it, so the bucket kernels treat its rows' entries as empty and the
+// combine leaves its rows alone.  Every other tile goes through the
+// key-block-stationary path (fine_kv.cu).  The default max_union is
+// 2.5 top_k: below it the tile's dense work over its union costs less than
+// the partial round trip of the key-stationary path.
+//
+// fine_q_kernel, persistent over the query-tile slots.  Per tile: TMA loads
+// the 128 query rows once (two buffers, so the next tile's rows load early);
+// for every block j of the union, in ascending order, TMA loads K_j and V_j
+// (plain tiled loads into a ring of stages), tcgen05 computes
+// S = Q K_j^T into TMEM (two S buffers), the softmax warpgroup (one thread
+// per row) masks the rows that did not select j and the keys past a row's
+// position (causal), and turns S into P (bf16, TMEM, two buffers) against a
+// running row maximum, and tcgen05 accumulates O += P V_j in TMEM.  The
+// running maximum is raised lazily: only when a block's maximum exceeds it by
+// more than 8 (a factor 2^8 in P) are the row's O and l rescaled, after the
+// previous block's PV has completed; P never exceeds 2^8.  At the end of the
+// tile each row's O / l is rounded to bf16 once and stored.
+//
+// Warps: 0-3 softmax (thread = row), 4 TMA producer, 5 MMA issuer (one
+// thread).  Every wait is bounded (an error bit and an abort, not a hang).
+// Barrier phases are tracked by per-role counters that advance identically:
+// every role visits the same tiles and the same union blocks in the same
+// order (g counts union blocks over the CTA's tiles, n counts tiles).
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "launchers.cuh"
+#include "sm100.cuh"
+
+namespace bsa {
+
+using namespace sm100;
+
+namespace {
+
+constexpr int kQRows = 128;          // query rows per tile (MMA M)
+constexpr int kQMaxUnion = 512;      // union blocks a query tile may have
+constexpr int kQUnionWords = kQMaxUnion / 32;
+constexpr int kQMaxNbWords = 512;    // block-bitmask words (nb <= 16384)
+constexpr int kQThreads = 192;
+
+// Error bits of this kernel's bounded waits (the fine stage's error word).
+constexpr uint32_t kErrQWaitQ = 1u << 12, kErrQWaitKV = 1u << 13, kErrQWaitS = 1u << 14,
+                   kErrQWaitP = 1u << 15, kErrQWaitO = 1u << 16, kErrQDrain = 1u << 17;
+
+template <int BS, int HD>
+struct QCfg {
+  static constexpr int kQBytes = kQRows * HD * 2;
+  static constexpr int kKBytes = BS * HD * 2;
+  static constexpr int kStageBytes = 2 * kKBytes;          // K_j and V_j
+  static constexpr int NS = (BS == 64 && HD == 64) ? 4 : 3;  // K/V stages
+  static constexpr int kCtasPerSm = (BS == 64 && HD == 64) ? 2 : 1;
+  static constexpr int kStageOff = 2 * kQBytes;
+  static constexpr int kRowBitsOff = kStageOff + NS * kStageBytes;
+  static constexpr int kRowBitsBytes = kQUnionWords * kQRows * 4;
+  static constexpr int kTileBitsOff = kRowBitsOff + kRowBitsBytes;
+  static constexpr int kTileBitsBytes = 2 * kQMaxNbWords * 4;   // bits, then prefix counts
+  static constexpr int kBarOff = kTileBitsOff + kTileBitsBytes;
+  static constexpr int kSmem = kBarOff + 256 + 1024 /*alignment*/;
+  // TMEM: S[2] (BS columns each), P[2] (bf16 pairs, BS / 2 each), O (HD).
+  static constexpr int kSCol = 0, kPCol = 2 * BS, kOCol = 3 * BS;
+  static constexpr int kCols = 3 * BS + HD;
+  static constexpr int kTmemCols = kCols <= 256 ? 256 : 512;
+  static_assert(kCols <= 512, "TMEM");
+  static_assert(kStageOff % 1024 == 0 && kStageBytes % 1024 == 0, "swizzled tiles");
+  static_assert(kSmem <= 227 * 1024, "shared memory");
+  static_assert(kCtasPerSm * (kSmem + 1024) <= 228 * 1024, "CTAs per SM");
+};
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// One CTA (128 threads) per (unit, tile); dynamic shared memory: nbw words.
+__global__ void __launch_bounds__(kQRows)
+classify_tiles_kernel(const int32_t* __restrict__ idx, uint8_t* __restrict__ tile_mode,
+                      uint32_t* __restrict__ qt_bits, int4* __restrict__ qt_info,
+                      uint32_t* __restrict__ n_qt, Shape s, int tiles, int max_union) {
+  extern __shared__ uint32_t bits[];
+  __shared__ int u_count, slot;
+  const int nbw = (s.nb + 31) / 32;
+  const int tid = threadIdx.x;
+  const int u = blockIdx.x / tiles, tile = blockIdx.x % tiles;
+  for (int w = tid; w < nbw; w += kQRows) bits[w] = 0u;
+  if (tid == 0) u_count = 0;
+  __syncthreads();
+  const int row = tile * kQRows + tid;
+  bool ok = true;
+  if (row < s.N) {
+    const int32_t* p = idx + ((int64_t)u * s.N + row) * s.k;
+    int prev = -1;
+    bool ended = false;
+    for (int t = 0; t < s.k; ++t) {
+      const int j = __ldg(p + t);
+      if (j < 0) { ended = true; continue; }
+      if (ended || j <= prev || j >= s.nb) { ok = false; break; }
+      atomicOr(&bits[j >> 5], 1u << (j & 31));
+      prev = j;
+    }
+  }
+  ok = __syncthreads_and(ok) != 0;
+  int c = 0;
+  for (int w = tid; w < nbw; w += kQRows) c += __popc(bits[w]);
+  if (c) atomicAdd(&u_count, c);
+  __syncthreads();
+  const int U = u_count;
+  const bool q = ok && U > 0 && U <= max_union;
+  if (tid == 0) {
+    tile_mode[(int64_t)u * tiles + tile] = q ? 1 : 0;
+    if (q) {
+      slot = (int)atomicAdd(n_qt, 1u);
+      qt_info[slot] = make_int4(u, tile, U, 0);
+    }
+  }
+  __syncthreads();
+  if (q)
+    for (int w = tid; w < nbw; w += kQRows) qt_bits[(int64_t)slot * nbw + w] = bits[w];
+}
+
+// ---------------------------------------------------------------------------
+struct FineQParams {
+  const int32_t* idx;        // (units, N, top_k) selections
+  const uint32_t* qt_bits;   // per query-tile slot: the union bitmask (nbw words)
+  const int4* qt_info;       // per slot: unit, tile, union size
+  const uint32_t* n_qt;      // number of slots
+  __nv_bfloat16* O;          // (units, N, HD)
+  uint32_t* err;             // the fine stage's error word
+  Shape s;
+};
+
+// Barrier 1 joins the softmax warps (0-3) only.  Every exit from their tile
+// loop goes through softmax_group_and, so all four warps leave together and
+// none is left waiting at a barrier the others never reach.
+__device__ __forceinline__ void softmax_group_sync() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+__device__ __forceinline__ bool softmax_group_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 128, p;\n"
+      " selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"(v ? 1u : 0u)
+      : "memory");
+  return r != 0u;
+}
+
+template <int BS, int HD>
+__global__ void __launch_bounds__(kQThreads, QCfg<BS, HD>::kCtasPerSm)
+fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+              const __grid_constant__ CUtensorMap tmap_v, FineQParams prm) {
+  using C = QCfg<BS, HD>;
+  constexpr int NS = C::NS;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  auto q_s = [&](int b) { return smem + b * C::kQBytes; };
+  auto k_s = [&](int st) { return smem + C::kStageOff + st * C::kStageBytes; };
+  auto v_s = [&](int st) { return k_s(st) + C::kKBytes; };
+  uint32_t* rowbits = reinterpret_cast<uint32_t*>(smem + C::kRowBitsOff);   // [word][row]
+  uint32_t* tb = reinterpret_cast<uint32_t*>(smem + C::kTileBitsOff);       // union bitmask
+  uint32_t* tpre = tb + kQMaxNbWords;                                        // its prefix counts
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* q_full = bars;          // [2]
+  uint64_t* q_empty = bars + 2;     // [2]
+  uint64_t* s_full = bars + 4;      // [2]
+  uint64_t* s_free = bars + 6;      // [2]
+  uint64_t* p_full = bars + 8;      // [2]
+  uint64_t* p_free = bars + 10;     // [2]
+  uint64_t* o_full = bars + 12;
+  uint64_t* o_empty = bars + 13;
+  uint64_t* drain = bars + 14;
+  uint64_t* kv_full = bars + 15;          // [NS]
+  uint64_t* kv_empty = bars + 15 + NS;    // [NS]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15 + 2 * NS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 16 + 2 * NS);
+  static_assert((17 + 2 * NS) * 8 <= 256, "barrier area");
+
+  const Shape s = prm.s;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = (int)*prm.n_qt;
+  if ((int)blockIdx.x >= n_tiles) return;   // the whole CTA, before any barrier
+  const int my_tiles = (n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  auto slot_of = [&](int n) { return (int)blockIdx.x + n * (int)gridDim.x; };
+  const int nbw = (s.nb + 31) / 32;
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&q_full[b], 1);
+      mbar_init(&q_empty[b], 1);
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_free[b], kQRows);
+      mbar_init(&p_full[b], kQRows);
+      mbar_init(&p_free[b], 1);
+    }
+    mbar_init(o_full, 1);
+    mbar_init(o_empty, kQRows);
+    mbar_init(drain, 1);
+    for (int st = 0; st < NS; ++st) {
+      mbar_init(&kv_full[st], 1);
+      mbar_init(&kv_empty[st], 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 4 && lane == 0) {
+    prefetch_tensormap(&tmap_q);
+    prefetch_tensormap(&tmap_k);
+    prefetch_tensormap(&tmap_v);
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int g = 0, qn = 0;   // K/V loads and Q loads issued
+      bool ok = true;
+      for (int n = 0; ok && n < my_tiles; ++n) {
+        const int4 info = __ldg(prm.qt_info + slot_of(n));
+        const int unit = info.x, tile = info.y;
+        const int qb = n & 1;
+        if (n >= 2) ok = mbar_wait(&q_empty[qb], ((n - 2) >> 1) & 1, prm.err, kErrQWaitQ);
+        if (!ok || *abort_flag) { ok = false; break; }
+        mbar_arrive_expect_tx(&q_full[qb], C::kQBytes);
+        ++qn;
+#pragma unroll
+        for (int p = 0; p < HD / 64; ++p)
+          tma_load_2d(q_s(qb) + p * (kQRows * 128), &tmap_q, &q_full[qb], p * 64,
+                      unit * s.N + tile * kQRows);
+        const uint32_t* bw = prm.qt_bits + (int64_t)slot_of(n) * nbw;
+        for (int w = 0; ok && w < nbw; ++w) {
+          uint32_t m = __ldg(bw + w);
+          while (m != 0u) {
+            const int j = w * 32 + __ffs(m) - 1;
+            m &= m - 1u;
+            const int st = g % NS;
+            if (g >= NS) ok = mbar_wait(&kv_empty[st], ((g - NS) / NS) & 1, prm.err, kErrQWaitKV);
+            if (!ok || *abort_flag) { ok = false; break; }
+            mbar_arrive_expect_tx(&kv_full[st], C::kStageBytes);
+            const int y = unit * s.N + j * BS;
+#pragma unroll
+            for (int p = 0; p < HD / 64; ++p) {
+              tma_load_2d(k_s(st) + p * (BS * 128), &tmap_k, &kv_full[st], p * 64, y);
+              tma_load_2d(v_s(st) + p * (BS * 128), &tmap_v, &kv_full[st], p * 64, y);
+            }
+            ++g;
+          }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        // Copies still in flight land before the CTA leaves: wait for the
+        // last load of every stage and Q buffer (bounded; those phases are
+        // the barriers' latest, so their parity is unambiguous).
+        for (int st = 0; st < NS; ++st) {
+          const int last = g - 1 - ((g - 1 - st) % NS + NS) % NS;
+          if (last >= 0) mbar_wait(&kv_full[st], (last / NS) & 1, prm.err, kErrQWaitKV);
+        }
+        for (int qb = 0; qb < 2; ++qb) {
+          const int last = qn - 1 - ((qn - 1 - qb) % 2 + 2) % 2;
+          if (last >= 0) mbar_wait(&q_full[qb], (last >> 1) & 1, prm.err, kErrQWaitQ);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_f32(kQRows, BS, false);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(kQRows, HD, true);
+      const uint64_t dq0 = smem_desc_sw128(smem_u32(q_s(0)), 16, 1024);
+      const uint64_t dk0 = smem_desc_sw128(smem_u32(k_s(0)), 16, 1024);
+      const uint64_t dv0 = smem_desc_sw128(smem_u32(v_s(0)), BS * 128, 1024);
+      // O += P(gp) V(gp); `first`: the tile's first PV, which overwrites O
+      // once the previous tile's epilogue has read it.
+      auto pv = [&](int gp, int n, bool first) -> bool {
+        const int bp = gp & 1, stp = gp % NS;
+        if (!mbar_wait(&p_full[bp], (gp >> 1) & 1, prm.err, kErrQWaitP)) return false;
+        if (first && n >= 1 && !mbar_wait(o_empty, (n - 1) & 1, prm.err, kErrQWaitO)) return false;
+        if (*abort_flag) return false;
+        tc_fence_after();
+        const uint64_t dv = dv0 + ((uint64_t)(stp * C::kStageBytes) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < BS / 16; ++kk)
+          mma_bf16_ts(tbase + C::kOCol, tbase + C::kPCol + bp * (BS / 2) + kk * 8,
+                      dv + ((kk * 16 * 128) >> 4), idesc_o, (!first || kk > 0) ? 1u : 0u);
+        mma_commit(&p_free[bp]);
+        mma_commit(&kv_empty[stp]);
+        return true;
+      };
+      int g = 0;
+      bool ok = true;
+      for (int n = 0; ok && n < my_tiles; ++n) {
+        const int U = __ldg(prm.qt_info + slot_of(n)).z;
+        const int qb = n & 1;
+        ok = mbar_wait(&q_full[qb], (n >> 1) & 1, prm.err, kErrQWaitQ);
+        const uint64_t dq = dq0 + ((uint64_t)(qb * C::kQBytes) >> 4);
+        for (int i = 0; ok && i < U; ++i, ++g) {
+          const int st = g % NS, b = g & 1;
+          ok = mbar_wait(&kv_full[st], (g / NS) & 1, prm.err, kErrQWaitKV);
+          if (ok && g >= 2) ok = mbar_wait(&s_free[b], ((g - 2) >> 1) & 1, prm.err, kErrQWaitS);
+          if (!ok || *abort_flag) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t dk = dk0 + ((uint64_t)(st * C::kStageBytes) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (kQRows * 128) + (kk & 3) * 32;
+            const uint32_t offk = (kk >> 2) * (BS * 128) + (kk & 3) * 32;
+            mma_bf16(tbase + C::kSCol + b * BS, dq + (off >> 4), dk + (offk >> 4), idesc_s,
+                     kk > 0 ? 1u : 0u);
+          }
+          mma_commit(&s_full[b]);
+          if (i == U - 1) mma_commit(&q_empty[qb]);
+          if (i >= 1) ok = pv(g - 1, n, i == 1);
+        }
+        if (ok) ok = pv(g - 1, n, U == 1);
+        if (ok) mma_commit(o_full);
+      }
+      if (!ok) *abort_flag = 1;
+      mma_commit(drain);
+      mbar_wait(drain, 0, prm.err, kErrQDrain);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int r = warp * 32 + lane;                    // row of the tile
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t o_addr = tbase + lane_off + C::kOCol;
+    const float sc = s.scale * kLog2e;                 // scores in the base-2 domain
+    int g = 0;
+    bool ok = true;
+    for (int n = 0; n < my_tiles; ++n) {
+      // All four warps agree to go on (and the last tile is done with the
+      // shared bitmask).
+      ok = softmax_group_and(ok && !*abort_flag);
+      if (!ok) break;
+      const int4 info = __ldg(prm.qt_info + slot_of(n));
+      const int unit = info.x, tile = info.y, U = info.z;
+      const int row = tile * kQRows + r;
+      const bool valid = row < s.N;
+      // The tile's union bitmask and, per word, the blocks before it.
+      const uint32_t* bw = prm.qt_bits + (int64_t)slot_of(n) * nbw;
+      for (int w = r; w < nbw; w += kQRows) tb[w] = __ldg(bw + w);
+      softmax_group_sync();
+      if (warp == 0) {
+        const int per = (nbw + 31) / 32;
+        int cnt = 0;
+        for (int q = 0; q < per; ++q) {
+          const int w = lane * per + q;
+          if (w < nbw) cnt += __popc(tb[w]);
+        }
+        int inc = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, inc, o);
+          if (lane >= o) inc += y;
+        }
+        int run = inc - cnt;
+        for (int q = 0; q < per; ++q) {
+          const int w = lane * per + q;
+          if (w < nbw) { tpre[w] = run; run += __popc(tb[w]); }
+        }
+      }
+      softmax_group_sync();
+      // This row's selected blocks as positions in the union.
+      const int UW = (U + 31) >> 5;
+      for (int w = 0; w < UW; ++w) rowbits[w * kQRows + r] = 0u;
+      if (valid) {
+        const int32_t* p = prm.idx + ((int64_t)unit * s.N + row) * s.k;
+        for (int t = 0; t < s.k; ++t) {
+          const int j = __ldg(p + t);
+          if (j < 0) continue;
+          const int pos = (int)tpre[j >> 5] + __popc(tb[j >> 5] & ((1u << (j & 31)) - 1u));
+          rowbits[(pos >> 5) * kQRows + r] |= 1u << (pos & 31);
+        }
+      }
+      float m_run = -INFINITY, l = 0.f;
+      uint32_t rw = 0u, cw = tb[0];
+      int wi = 0;
+      for (int i = 0; i < U; ++i, ++g) {
+        while (cw == 0u && wi + 1 < nbw) cw = tb[++wi];
+        const int j = wi * 32 + __ffs(cw) - 1;          // the union's i-th block
+        cw &= cw - 1u;
+        if ((i & 31) == 0) rw = rowbits[(i >> 5) * kQRows + r];
+        const bool sel = ((rw >> (i & 31)) & 1u) != 0u;
+        const int b = g & 1;
+        ok = mbar_wait(&s_full[b], (g >> 1) & 1, prm.err, kErrQWaitS);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok || *abort_flag) { ok = false; break; }
+        tc_fence_after();
+        float sv[BS];
+        if (__any_sync(0xffffffffu, sel)) {
+#pragma unroll
+          for (int c0 = 0; c0 < BS; c0 += 64) tmem_ld64(tbase + lane_off + C::kSCol + b * BS + c0, sv + c0);
+        }
+        tc_fence_before();
+        mbar_arrive(&s_free[b]);                        // S(g) is in registers
+        float mx = -INFINITY;
+        if (sel) {
+          // Token-level causal mask (block_indexer.py:73-81): key > query -> -inf.
+          const int key0 = j * BS;
+          if (s.causal && key0 + BS - 1 > row) {
+#pragma unroll
+            for (int c = 0; c < BS; ++c)
+              if (key0 + c > row) sv[c] = -INFINITY;
+          }
+#pragma unroll
+          for (int c = 0; c < BS; c += 2) mx = fmax3(mx, sv[c], sv[c + 1]);
+        }
+        const float msc = mx * sc;
+        bool resc = false;
+        if (sel && mx != -INFINITY) {
+          if (m_run == -INFINITY) m_run = msc;          // O and l are still zero
+          else if (msc > m_run + 8.f) resc = true;
+        }
+        if (__any_sync(0xffffffffu, resc)) {
+          // Raise the running maximum: O (complete through PV(g - 1), an
+          // earlier block of this tile) and l scale by 2^(old - new).
+          const int gp = g - 1;
+          ok = mbar_wait(&p_free[gp & 1], (gp >> 1) & 1, prm.err, kErrQWaitP);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+          const float alpha = resc ? fast_exp2(m_run - msc) : 1.f;
+          if (resc) { m_run = msc; l *= alpha; }
+#pragma unroll
+          for (int c0 = 0; c0 < HD; c0 += 32) {
+            float ov[32];
+            tmem_ld32(o_addr + c0, ov);
+#pragma unroll
+            for (int h = 0; h < 32; h += 16) {
+              uint32_t pk[16];
+#pragma unroll
+              for (int c = 0; c < 16; ++c) pk[c] = __float_as_uint(ov[h + c] * alpha);
+              tmem_st16(o_addr + c0 + h, pk);
+            }
+          }
+        }
+        if (g >= 2) {
+          // P buffer b is free once PV(g - 2) is done.
+          ok = mbar_wait(&p_free[b], ((g - 2) >> 1) & 1, prm.err, kErrQWaitP);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+        }
+        // p = 2^(s sc - m_run) (at most 2^8), 0 where masked or not selected.
+        const bool live = sel && m_run != -INFINITY;
+        float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+        for (int c0 = 0; c0 < BS; c0 += 32) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const float p0 = live ? fast_exp2(fmaf(sv[c0 + c], sc, -m_run)) : 0.f;
+            const float p1 = live ? fast_exp2(fmaf(sv[c0 + c + 1], sc, -m_run)) : 0.f;
+            l0 += p0;
+            l1 += p1;
+            pk[c >> 1] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16(tbase + lane_off + C::kPCol + b * (BS / 2) + (c0 >> 1), pk);
+        }
+        l += l0 + l1;
+        tc_fence_before();
+        mbar_arrive(&p_full[b]);
+      }
+      ok = softmax_group_and(ok);
+      if (!ok) break;
+      // Epilogue: O / l rounded to bf16 once.
+      ok = mbar_wait(o_full, n & 1, prm.err, kErrQWaitO);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) continue;                               // leaves at the next group vote
+      tc_fence_after();
+      const float inv = 1.f / l;
+      uint4* orow = reinterpret_cast<uint4*>(prm.O + ((int64_t)unit * s.N + row) * HD);
+#pragma unroll
+      for (int c0 = 0; c0 < HD; c0 += 32) {
+        float ov[32];
+        tmem_ld32(o_addr + c0, ov);
+        if (valid) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            orow[(c0 >> 3) + q] = make_uint4(
+                pack_bf16x2(ov[8 * q] * inv, ov[8 * q + 1] * inv),
+                pack_bf16x2(ov[8 * q + 2] * inv, ov[8 * q + 3] * inv),
+                pack_bf16x2(ov[8 * q + 4] * inv, ov[8 * q + 5] * inv),
+                pack_bf16x2(ov[8 * q + 6] * inv, ov[8 * q + 7] * inv));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(o_empty);
+    }
+    if (!ok) *abort_flag = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tbase, C::kTmemCols);
+}
+
+// ---------------------------------------------------------------------------
+// Host side.
+static bool q_make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols,
+                       uint32_t box_rows) {
+  static PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+  if (enc == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return false;
+    enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool fine_q_supported(const Shape& s) {
+  return ((s.bs == 64 && (s.D == 64 || s.D == 128)) || (s.bs == 128 && s.D == 64)) &&
+         (s.nb + 31) / 32 <= kQMaxNbWords && (int64_t)s.units * s.N < (1LL << 31);
+}
+
+int fine_q_max_union(const Shape& s, uint32_t flags) {
+  if (flags & BSA_FLAG_FINE_KEY_STATIONARY) return 0;
+  if (flags & BSA_FLAG_FINE_QUERY_STATIONARY) return kQMaxUnion;
+  return min(kQMaxUnion, (5 * s.k) / 2);
+}
+
+int fine_q_tiles(const Shape& s) { return (s.N + kQRows - 1) / kQRows; }
+
+cudaError_t launch_classify_tiles(const int32_t* idx, uint8_t* tile_mode, uint32_t* qt_bits,
+                                  int4* qt_info, uint32_t* n_qt, const Shape& s, int max_union,
+                                  cudaStream_t st) {
+  const int tiles = fine_q_tiles(s);
+  const int64_t grid = (int64_t)s.units * tiles;
+  if (grid == 0) return cudaSuccess;
+  const size_t smem = sizeof(uint32_t) * (size_t)((s.nb + 31) / 32);
+  classify_tiles_kernel<<<(unsigned)grid, kQRows, smem, st>>>(idx, tile_mode, qt_bits, qt_info,
+                                                              n_qt, s, tiles, max_union);
+  return cudaGetLastError();
+}
+
+template <int BS, int HD>
+static cudaError_t launch_q(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
+                            const FineQParams& prm, int64_t max_tiles, cudaStream_t st) {
+  using C = QCfg<BS, HD>;
+  const uint64_t rows = (uint64_t)prm.s.units * prm.s.N;
+  CUtensorMap mq, mk, mv;
+  if (!q_make_map(&mq, Q, rows, HD, kQRows) || !q_make_map(&mk, K, rows, HD, BS) ||
+      !q_make_map(&mv, V, rows, HD, BS))
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(fine_q_kernel<BS, HD>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (sms <= 0) sms = kNumSMs;
+  int64_t grid = (int64_t)sms * C::kCtasPerSm;
+  if (grid > max_tiles) grid = max_tiles;
+  if (grid <= 0) return cudaSuccess;
+  fine_q_kernel<BS, HD><<<(unsigned)grid, kQThreads, C::kSmem, st>>>(mq, mk, mv, prm);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fine_q(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
+                          const int32_t* idx, __nv_bfloat16* O, const uint32_t* qt_bits,
+                          const int4* qt_info, const uint32_t* n_qt, uint32_t* err,
+                          const Shape& s, cudaStream_t st) {
+  FineQParams prm;
+  prm.idx = idx;
+  prm.qt_bits = qt_bits;
+  prm.qt_info = qt_info;
+  prm.n_qt = n_qt;
+  prm.O = O;
+  prm.err = err;
+  prm.s = s;
+  const int64_t max_tiles = (int64_t)s.units * fine_q_tiles(s);
+  if (s.bs == 64 && s.D == 64) return launch_q<64, 64>(Q, K, V, prm, max_tiles, st);
+  if (s.bs == 64 && s.D == 128) return launch_q<64, 128>(Q, K, V, prm, max_tiles, st);
+  if (s.bs == 128 && s.D == 64) return launch_q<128, 64>(Q, K, V, prm, max_tiles, st);
+  return cudaErrorNotSupported;
+}
+
+}  // namespace bsa

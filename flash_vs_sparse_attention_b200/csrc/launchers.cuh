@@ -34,8 +34,21 @@ size_t fine_kv_counters_offset(const Shape& s);  // byte offset of the per-pass 
 size_t fine_kv_zero_bytes(const Shape& s);    // bytes to clear at the start of the region
 cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                            const __nv_bfloat16* V, const int32_t* idx, __nv_bfloat16* O,
-                           unsigned char* ws, const Shape& s, cudaStream_t st, int* n_launches,
-                           void* const* events, int n_events, bool pre_zeroed);
+                           unsigned char* ws, const Shape& s, uint32_t flags, cudaStream_t st,
+                           int* n_launches, void* const* events, int n_events, bool pre_zeroed);
+// Query-stationary fine kernel for query tiles (fine_q.cu): the shapes it
+// covers, the union limit for a tile under `flags` (0: none), tiles per
+// unit, the tile classifier and the kernel.
+bool fine_q_supported(const Shape& s);
+int fine_q_max_union(const Shape& s, uint32_t flags);
+int fine_q_tiles(const Shape& s);
+cudaError_t launch_classify_tiles(const int32_t* idx, uint8_t* tile_mode, uint32_t* qt_bits,
+                                  int4* qt_info, uint32_t* n_qt, const Shape& s, int max_union,
+                                  cudaStream_t st);
+cudaError_t launch_fine_q(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
+                          const int32_t* idx, __nv_bfloat16* O, const uint32_t* qt_bits,
+                          const int4* qt_info, const uint32_t* n_qt, uint32_t* err,
+                          const Shape& s, cudaStream_t st);
 
 // Decode (decode.cu): per new query row, the top-k cached blocks (a warp per
 // row; exact top-k, lowest index on ties, ascending order, -1 padded).

@@ -57,6 +57,16 @@ typedef enum bsa_status {
  * after a few microseconds and the call ends with its error word set and a
  * NaN output -- how a stuck pipeline is reported, exercised without one. */
 #define BSA_FLAG_TEST_TIMEOUT 8u
+/* The tensor-core fine stage picks, per 128-row query tile, between a
+ * key-block-stationary kernel (every selected block with the queries that
+ * picked it, partial results merged per query) and a query-stationary one
+ * (the tile's rows over the union of their selected blocks, the output
+ * written once), by the size of that union: at most 2.5 top_k blocks ->
+ * query-stationary.  These force one side (tests compare them):
+ * KEY_STATIONARY sends every tile to the first, QUERY_STATIONARY every tile
+ * whose union is at most 512 blocks to the second. */
+#define BSA_FLAG_FINE_KEY_STATIONARY 16u
+#define BSA_FLAG_FINE_QUERY_STATIONARY 32u
 
 typedef struct bsa_problem {
   int32_t batch;       /* B */

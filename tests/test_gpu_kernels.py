@@ -69,7 +69,11 @@ def test_select_blocks_index_parity(cuda, shape, flags):
                 assert np.all(np.diff(v) > 0) and np.all(row[len(v):] == -1), row
 
 
-@pytest.mark.parametrize("flags", [0, SIMT])
+KEY_ONLY = _lib.BSA_FLAG_FINE_KEY_STATIONARY
+QUERY_ONLY = _lib.BSA_FLAG_FINE_QUERY_STATIONARY
+
+
+@pytest.mark.parametrize("flags", [0, SIMT, KEY_ONLY, QUERY_ONLY])
 @pytest.mark.parametrize("shape", SHAPES)
 def test_fine_stage_given_indices(cuda, shape, flags):
     """Fine stage fed the GPU's own selection vs the oracle's fine stage."""
@@ -84,3 +88,46 @@ def test_fine_stage_given_indices(cuda, shape, flags):
         for h in range(H):
             want = oracle_fine(Q[b, h], K[b, h], V[b, h], idx[b, h], rows, bs, causal)
             assert_close_out(O[b, h], want, f"unit ({b},{h})")
+
+
+def recent_blocks_selection(N, bs, k, causal, rows):
+    """Per row of `rows`: the k most recent eligible blocks (ascending), -1
+    padded -- a structured selection whose 128-row tiles share few blocks."""
+    out = np.full((len(rows), k), -1, dtype=np.int32)
+    nb = N // bs
+    for i, r in enumerate(rows):
+        last = r // bs if causal else nb - 1
+        sel = np.arange(max(0, last - k + 1), last + 1)
+        out[i, :len(sel)] = sel
+    return out
+
+
+@pytest.mark.parametrize("shape", [(1, 2, 4096, 64, 64, 16, True), (1, 1, 4096, 128, 64, 32, False),
+                                   (1, 1, 8192, 64, 128, 16, True)])
+def test_fine_stage_mixed_tile_dispatch(cuda, shape):
+    """Even 128-row tiles get a selection with a small union (query-stationary
+    kernel), odd tiles the GPU's own selection (key-block-stationary): the
+    default dispatch mixes both in one call and matches the oracle, and the
+    forced key-stationary path agrees with it."""
+    B, H, N, D, bs, k, causal = shape
+    Q, K, V = rand_inputs(B, H, N, D, seed=5)
+    Qg, Kg, Vg = to_gpu(Q, K, V)
+    idx = bi.select_blocks(Qg, Kg, causal=causal, block_size=bs, top_k=k).cpu().numpy()
+    rows = np.arange(N)
+    even = (rows // 128) % 2 == 0
+    for b in range(B):
+        for h in range(H):
+            idx[b, h, even] = recent_blocks_selection(N, bs, k, causal, rows[even])
+    idx_g = torch.from_numpy(idx).to(cuda)
+    O = bi.fine(Qg, Kg, Vg, idx_g, causal=causal, block_size=bs).float().cpu().numpy()
+    O_kv = bi.fine(Qg, Kg, Vg, idx_g, causal=causal, block_size=bs,
+                   flags=KEY_ONLY).float().cpu().numpy()
+    for b in range(B):
+        for h in range(H):
+            want = oracle_fine(Q[b, h], K[b, h], V[b, h], idx[b, h], rows, bs, causal)
+            assert_close_out(O[b, h], want, f"unit ({b},{h}) mixed")
+            assert_close_out(O_kv[b, h], want, f"unit ({b},{h}) key-stationary")
+    # The two kernels round differently (one bf16 rounding against fp16
+    # partials merged), so the even tiles' bits show which kernel ran.
+    assert not np.array_equal(O[:, :, even], O_kv[:, :, even]), "query tiles not dispatched"
+    assert np.array_equal(O[:, :, ~even], O_kv[:, :, ~even])
