@@ -96,6 +96,20 @@ struct FineWs {
 
 static size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
 
+// The query tiles as the bucket kernels and the combine see them: the tile
+// marks count only when the query tiles are at least min_count of the tiles
+// (device word *count from the classifier); otherwise every tile takes the
+// key-block-stationary path.
+struct QTiles {
+  const uint8_t* mode;     // units * tiles, or null: no query tiles
+  const uint32_t* count;
+  int min_count;
+};
+
+__device__ __forceinline__ const uint8_t* active_tile_mode(const QTiles& q) {
+  return (q.mode != nullptr && *q.count >= (uint32_t)q.min_count) ? q.mode : nullptr;
+}
+
 // How the bucket kernels cut a unit's rows: batches of rows_batch rows
 // (rows_batch * k <= kBucketBatch entries), chunks of whole batches.
 struct BucketGeom {
@@ -298,8 +312,9 @@ bucket_count_kernel(const int32_t* __restrict__ idx, int32_t* __restrict__ curso
                     int32_t* __restrict__ offsets, int32_t* __restrict__ item_row,
                     int4* __restrict__ items, uint32_t* __restrict__ ctr,
                     const __nv_bfloat16* __restrict__ V, int32_t* __restrict__ vexp,
-                    const uint8_t* __restrict__ tile_mode, Shape s, BucketGeom g, float inv_k) {
+                    QTiles qtiles, Shape s, BucketGeom g, float inv_k) {
   extern __shared__ int32_t hist[];
+  const uint8_t* tile_mode = active_tile_mode(qtiles);
   __shared__ int32_t wsum_c[kBucketThreads / 32], wsum_t[kBucketThreads / 32];
   __shared__ int32_t ticket, item_base;
   const int u = blockIdx.y, chunk = blockIdx.x;
@@ -400,8 +415,8 @@ __global__ void __launch_bounds__(kBucketThreads, 2)
 bucket_scatter_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ chunk_rel,
                       const int32_t* __restrict__ offsets, const int32_t* __restrict__ item_row,
                       int32_t* __restrict__ lists, int32_t* __restrict__ inv,
-                      const uint8_t* __restrict__ tile_mode, Shape s, BucketGeom g,
-                      float inv_k) {
+                      QTiles qtiles, Shape s, BucketGeom g, float inv_k) {
+  const uint8_t* tile_mode = active_tile_mode(qtiles);
   extern __shared__ int32_t smem_i[];
   int32_t* cnt = smem_i;                 // nb: batch counts -> local prefix -> local cursor
   int32_t* gap = smem_i + s.nb;          // nb: the block's cursor minus its local prefix
@@ -1136,8 +1151,9 @@ template <int HD, int KMAX>
 __global__ void __launch_bounds__(256)
 combine_kernel(const int32_t* __restrict__ inv,
                const __half* __restrict__ part_o, const float2* __restrict__ part_ml,
-               const uint32_t* __restrict__ err, const uint8_t* __restrict__ tile_mode,
-               __nv_bfloat16* __restrict__ O, Shape s) {
+               const uint32_t* __restrict__ err, QTiles qtiles, __nv_bfloat16* __restrict__ O,
+               Shape s) {
+  const uint8_t* tile_mode = active_tile_mode(qtiles);
   constexpr int CH = HD / 8;           // threads per row (8 or 16), a power of two <= 32
   constexpr int PER = (KMAX + CH - 1) / CH;   // slots whose metadata one thread loads
   const int64_t rows = (int64_t)s.units * s.N;
@@ -1225,7 +1241,7 @@ combine_kernel(const int32_t* __restrict__ inv,
 }
 
 template <int HD>
-static void launch_combine(const FineWs& w, const uint8_t* tm, __nv_bfloat16* O, const Shape& s,
+static void launch_combine(const FineWs& w, QTiles tm, __nv_bfloat16* O, const Shape& s,
                            cudaStream_t st) {
   const int64_t threads = (int64_t)s.units * s.N * (HD / 8);
   const unsigned blocks = (unsigned)((threads + 255) / 256);
@@ -1321,7 +1337,13 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
   // Per-tile dispatch: query tiles (few distinct blocks between their rows)
   // go to the query-stationary kernel, the rest through the buckets.
   const int max_union = fine_q_supported(s) ? fine_q_max_union(s, flags) : 0;
-  const uint8_t* tm = max_union > 0 ? w.tile_mode : nullptr;
+  // Unless forced, the query-stationary kernel takes the query tiles only
+  // when they are at least half of all tiles: a few long query tiles (early
+  // causal tiles see few blocks) would run after the key-stationary kernel
+  // and lengthen the stage instead of shortening it.
+  const int tiles_total = s.units * fine_q_tiles(s);
+  const int min_q = (flags & BSA_FLAG_FINE_QUERY_STATIONARY) ? 1 : (tiles_total + 1) / 2;
+  const QTiles tm{max_union > 0 ? w.tile_mode : nullptr, w.ctr + 2, min_q};
   if (max_union > 0 &&
       (e = launch_classify_tiles(idx, w.tile_mode, w.qt_bits, w.qt_info, w.ctr + 2, s, max_union,
                                  st)) != cudaSuccess)
@@ -1355,8 +1377,8 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
   else e = cudaErrorNotSupported;
   if (e != cudaSuccess) return e;
   if (max_union > 0 &&
-      (e = launch_fine_q(Q, K, V, idx, O, w.qt_bits, w.qt_info, w.ctr + 2, w.err, s, st)) !=
-          cudaSuccess)
+      (e = launch_fine_q(Q, K, V, idx, O, w.qt_bits, w.qt_info, w.ctr + 2, min_q, w.err, s,
+                         st)) != cudaSuccess)
     return e;
   mark(3);
   if (s.D == 64) launch_combine<64>(w, tm, O, s, st);

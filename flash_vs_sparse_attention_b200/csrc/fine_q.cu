@@ -52,6 +52,8 @@ constexpr int kQMaxNbWords = 512;    // block-bitmask words (nb <= 16384)
 constexpr int kQThreads = 192;
 
 // Error bits of this kernel's bounded waits (the fine stage's error word).
+// kErrQTestTimeout is the key-stationary kernel's test-hook bit (same meaning).
+constexpr uint32_t kErrQTestTimeout = 512u;
 constexpr uint32_t kErrQWaitQ = 1u << 12, kErrQWaitKV = 1u << 13, kErrQWaitS = 1u << 14,
                    kErrQWaitP = 1u << 15, kErrQWaitO = 1u << 16, kErrQDrain = 1u << 17;
 
@@ -82,36 +84,88 @@ struct QCfg {
 }  // namespace
 
 // ---------------------------------------------------------------------------
-// One CTA (128 threads) per (unit, tile); dynamic shared memory: nbw words.
+// One CTA (128 threads) per (unit, tile).  Dynamic shared memory: a byte per
+// block (nb rounded up to 16) marking the blocks the tile's rows selected --
+// plain stores of 1, no atomics, so rows picking the same blocks do not
+// serialise -- then packed into nbw bitmask words.
+template <int KMAX>
 __global__ void __launch_bounds__(kQRows)
 classify_tiles_kernel(const int32_t* __restrict__ idx, uint8_t* __restrict__ tile_mode,
                       uint32_t* __restrict__ qt_bits, int4* __restrict__ qt_info,
                       uint32_t* __restrict__ n_qt, Shape s, int tiles, int max_union) {
-  extern __shared__ uint32_t bits[];
+  extern __shared__ __align__(16) uint8_t present[];
   __shared__ int u_count, slot;
   const int nbw = (s.nb + 31) / 32;
+  const int nb16 = (s.nb + 15) / 16;
   const int tid = threadIdx.x;
   const int u = blockIdx.x / tiles, tile = blockIdx.x % tiles;
-  for (int w = tid; w < nbw; w += kQRows) bits[w] = 0u;
+  for (int w = tid; w < nb16; w += kQRows)
+    reinterpret_cast<uint4*>(present)[w] = make_uint4(0u, 0u, 0u, 0u);
   if (tid == 0) u_count = 0;
   __syncthreads();
   const int row = tile * kQRows + tid;
   bool ok = true;
   if (row < s.N) {
+    // The row's entries, all loads in flight before the scan (top_k <=
+    // KMAX; 16-byte loads when a row starts on a 16-byte boundary).
     const int32_t* p = idx + ((int64_t)u * s.N + row) * s.k;
+    int v[KMAX];
+    if ((s.k & 3) == 0 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+      for (int t = 0; t < KMAX; t += 4) {
+        if (t < s.k) {
+          const int4 x = __ldg(reinterpret_cast<const int4*>(p + t));
+          v[t] = x.x; v[t + 1] = x.y; v[t + 2] = x.z; v[t + 3] = x.w;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < KMAX; ++t)
+        if (t < s.k) v[t] = __ldg(p + t);
+    }
     int prev = -1;
     bool ended = false;
-    for (int t = 0; t < s.k; ++t) {
-      const int j = __ldg(p + t);
-      if (j < 0) { ended = true; continue; }
-      if (ended || j <= prev || j >= s.nb) { ok = false; break; }
-      atomicOr(&bits[j >> 5], 1u << (j & 31));
-      prev = j;
+#pragma unroll
+    for (int t = 0; t < KMAX; ++t) {
+      if (t < s.k && ok) {
+        const int j = v[t];
+        if (j < 0) {
+          ended = true;
+        } else if (ended || j <= prev || j >= s.nb) {
+          ok = false;
+        } else {
+          present[j] = 1;
+          prev = j;
+        }
+      }
     }
   }
   ok = __syncthreads_and(ok) != 0;
+  // Pack 32 bytes into a word; count the union.
+  uint32_t my_words[kQMaxNbWords / kQRows];
   int c = 0;
-  for (int w = tid; w < nbw; w += kQRows) c += __popc(bits[w]);
+#pragma unroll
+  for (int q = 0; q < kQMaxNbWords / kQRows; ++q) {
+    const int w = tid + q * kQRows;
+    uint32_t m = 0u;
+    if (w < nbw) {
+      const uint4* b4 = reinterpret_cast<const uint4*>(present + 32 * w);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (32 * w + 16 * h < 16 * nb16) {
+          const uint4 x = b4[h];
+          const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+#pragma unroll
+            for (int bb = 0; bb < 4; ++bb)
+              m |= ((xs[e] >> (8 * bb)) & 1u) << (16 * h + 4 * e + bb);
+        }
+      }
+    }
+    my_words[q] = m;
+    c += __popc(m);
+  }
   if (c) atomicAdd(&u_count, c);
   __syncthreads();
   const int U = u_count;
@@ -124,8 +178,13 @@ classify_tiles_kernel(const int32_t* __restrict__ idx, uint8_t* __restrict__ til
     }
   }
   __syncthreads();
-  if (q)
-    for (int w = tid; w < nbw; w += kQRows) qt_bits[(int64_t)slot * nbw + w] = bits[w];
+  if (q) {
+#pragma unroll
+    for (int qq = 0; qq < kQMaxNbWords / kQRows; ++qq) {
+      const int w = tid + qq * kQRows;
+      if (w < nbw) qt_bits[(int64_t)slot * nbw + w] = my_words[qq];
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -134,6 +193,7 @@ struct FineQParams {
   const uint32_t* qt_bits;   // per query-tile slot: the union bitmask (nbw words)
   const int4* qt_info;       // per slot: unit, tile, union size
   const uint32_t* n_qt;      // number of slots
+  int min_q_tiles;           // fewer slots than this: the key-stationary path took them
   __nv_bfloat16* O;          // (units, N, HD)
   uint32_t* err;             // the fine stage's error word
   Shape s;
@@ -184,12 +244,13 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
   uint64_t* kv_empty = bars + 15 + NS;    // [NS]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15 + 2 * NS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 16 + 2 * NS);
-  static_assert((17 + 2 * NS) * 8 <= 256, "barrier area");
+  uint64_t* gate = bars + 17 + 2 * NS;    // test hook: nothing completes it
+  static_assert((18 + 2 * NS) * 8 <= 256, "barrier area");
 
   const Shape s = prm.s;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = (int)*prm.n_qt;
-  if ((int)blockIdx.x >= n_tiles) return;   // the whole CTA, before any barrier
+  if (n_tiles < prm.min_q_tiles || (int)blockIdx.x >= n_tiles) return;   // whole CTA, no barrier yet
   const int my_tiles = (n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
   auto slot_of = [&](int n) { return (int)blockIdx.x + n * (int)gridDim.x; };
   const int nbw = (s.nb + 31) / 32;
@@ -206,6 +267,7 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
     mbar_init(o_full, 1);
     mbar_init(o_empty, kQRows);
     mbar_init(drain, 1);
+    mbar_init(gate, 1);
     for (int st = 0; st < NS; ++st) {
       mbar_init(&kv_full[st], 1);
       mbar_init(&kv_empty[st], 1);
@@ -224,7 +286,25 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
-  if (warp == 4) {
+  if (s.test_timeout) {
+    // Test hook (BSA_FLAG_TEST_TIMEOUT): one bounded wait of a few
+    // microseconds on a barrier nothing completes, before any copy or MMA;
+    // it records its bit in the error word, and the CTA's rows come out NaN.
+    if (threadIdx.x == 0) mbar_wait_ns(gate, 0, prm.err, kErrQTestTimeout, 2000);
+    __syncthreads();
+    if (warp < 4) {
+      const int r = warp * 32 + lane;
+      const uint32_t nan2 = 0x7fc07fc0u;   // two bf16 NaNs
+      for (int n = 0; n < my_tiles; ++n) {
+        const int4 info = __ldg(prm.qt_info + slot_of(n));
+        const int row = info.y * kQRows + r;
+        if (row >= s.N) continue;
+        uint4* orow = reinterpret_cast<uint4*>(prm.O + ((int64_t)info.x * s.N + row) * HD);
+#pragma unroll
+        for (int q = 0; q < HD / 8; ++q) orow[q] = make_uint4(nan2, nan2, nan2, nan2);
+      }
+    }
+  } else if (warp == 4) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       int g = 0, qn = 0;   // K/V loads and Q loads issued
@@ -458,22 +538,33 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
           tc_fence_after();
         }
         // p = 2^(s sc - m_run) (at most 2^8), 0 where masked or not selected.
+        // A warp none of whose rows selected the block stores zeros.
         const bool live = sel && m_run != -INFINITY;
-        float l0 = 0.f, l1 = 0.f;
+        const uint32_t p_addr = tbase + lane_off + C::kPCol + b * (BS / 2);
+        if (__any_sync(0xffffffffu, live)) {
+          const float shift = live ? m_run : INFINITY;   // not live: every p = 0
+          float l0 = 0.f, l1 = 0.f;
 #pragma unroll
-        for (int c0 = 0; c0 < BS; c0 += 32) {
+          for (int c0 = 0; c0 < BS; c0 += 32) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int c = 0; c < 32; c += 2) {
+              const float p0 = fast_exp2(fmaf(sv[c0 + c], sc, -shift));
+              const float p1 = fast_exp2(fmaf(sv[c0 + c + 1], sc, -shift));
+              l0 += p0;
+              l1 += p1;
+              pk[c >> 1] = pack_bf16x2(p0, p1);
+            }
+            tmem_st16(p_addr + (c0 >> 1), pk);
+          }
+          if (live) l += l0 + l1;
+        } else {
           uint32_t pk[16];
 #pragma unroll
-          for (int c = 0; c < 32; c += 2) {
-            const float p0 = live ? fast_exp2(fmaf(sv[c0 + c], sc, -m_run)) : 0.f;
-            const float p1 = live ? fast_exp2(fmaf(sv[c0 + c + 1], sc, -m_run)) : 0.f;
-            l0 += p0;
-            l1 += p1;
-            pk[c >> 1] = pack_bf16x2(p0, p1);
-          }
-          tmem_st16(tbase + lane_off + C::kPCol + b * (BS / 2) + (c0 >> 1), pk);
+          for (int c = 0; c < 16; ++c) pk[c] = 0u;
+#pragma unroll
+          for (int c0 = 0; c0 < BS; c0 += 32) tmem_st16(p_addr + (c0 >> 1), pk);
         }
-        l += l0 + l1;
         tc_fence_before();
         mbar_arrive(&p_full[b]);
       }
@@ -484,7 +575,11 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) continue;                               // leaves at the next group vote
       tc_fence_after();
-      const float inv = 1.f / l;
+      // A timed-out wait anywhere in the fine stage (this kernel or the
+      // key-stationary one before it) leaves its bit in the error word:
+      // the rows then come out NaN, as the combine writes them.
+      const float inv = *reinterpret_cast<volatile uint32_t*>(prm.err) != 0u
+                            ? __int_as_float(0x7fc00000) : 1.f / l;
       uint4* orow = reinterpret_cast<uint4*>(prm.O + ((int64_t)unit * s.N + row) * HD);
 #pragma unroll
       for (int c0 = 0; c0 < HD; c0 += 32) {
@@ -553,9 +648,11 @@ cudaError_t launch_classify_tiles(const int32_t* idx, uint8_t* tile_mode, uint32
   const int tiles = fine_q_tiles(s);
   const int64_t grid = (int64_t)s.units * tiles;
   if (grid == 0) return cudaSuccess;
-  const size_t smem = sizeof(uint32_t) * (size_t)((s.nb + 31) / 32);
-  classify_tiles_kernel<<<(unsigned)grid, kQRows, smem, st>>>(idx, tile_mode, qt_bits, qt_info,
-                                                              n_qt, s, tiles, max_union);
+  const size_t smem = 32 * (size_t)((s.nb + 31) / 32);   // whole words of bytes
+  auto kern = s.k <= 16 ? classify_tiles_kernel<16>
+             : (s.k <= 32 ? classify_tiles_kernel<32> : classify_tiles_kernel<64>);
+  kern<<<(unsigned)grid, kQRows, smem, st>>>(idx, tile_mode, qt_bits, qt_info, n_qt, s, tiles,
+                                             max_union);
   return cudaGetLastError();
 }
 
@@ -584,13 +681,14 @@ static cudaError_t launch_q(const __nv_bfloat16* Q, const __nv_bfloat16* K, cons
 
 cudaError_t launch_fine_q(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
                           const int32_t* idx, __nv_bfloat16* O, const uint32_t* qt_bits,
-                          const int4* qt_info, const uint32_t* n_qt, uint32_t* err,
-                          const Shape& s, cudaStream_t st) {
+                          const int4* qt_info, const uint32_t* n_qt, int min_q_tiles,
+                          uint32_t* err, const Shape& s, cudaStream_t st) {
   FineQParams prm;
   prm.idx = idx;
   prm.qt_bits = qt_bits;
   prm.qt_info = qt_info;
   prm.n_qt = n_qt;
+  prm.min_q_tiles = min_q_tiles;
   prm.O = O;
   prm.err = err;
   prm.s = s;

@@ -47,8 +47,8 @@ cudaError_t launch_classify_tiles(const int32_t* idx, uint8_t* tile_mode, uint32
                                   cudaStream_t st);
 cudaError_t launch_fine_q(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
                           const int32_t* idx, __nv_bfloat16* O, const uint32_t* qt_bits,
-                          const int4* qt_info, const uint32_t* n_qt, uint32_t* err,
-                          const Shape& s, cudaStream_t st);
+                          const int4* qt_info, const uint32_t* n_qt, int min_q_tiles,
+                          uint32_t* err, const Shape& s, cudaStream_t st);
 
 // Decode (decode.cu): per new query row, the top-k cached blocks (a warp per
 // row; exact top-k, lowest index on ties, ascending order, -1 padded).

@@ -127,7 +127,18 @@ def test_fine_stage_mixed_tile_dispatch(cuda, shape):
             want = oracle_fine(Q[b, h], K[b, h], V[b, h], idx[b, h], rows, bs, causal)
             assert_close_out(O[b, h], want, f"unit ({b},{h}) mixed")
             assert_close_out(O_kv[b, h], want, f"unit ({b},{h}) key-stationary")
-    # The two kernels round differently (one bf16 rounding against fp16
-    # partials merged), so the even tiles' bits show which kernel ran.
-    assert not np.array_equal(O[:, :, even], O_kv[:, :, even]), "query tiles not dispatched"
-    assert np.array_equal(O[:, :, ~even], O_kv[:, :, ~even])
+    # Which tiles the dispatch should send where: a tile's union of selected
+    # blocks at most 2.5 top_k -> query-stationary.  The two kernels round
+    # differently (one bf16 rounding against fp16 partials merged), so the
+    # bits show which kernel ran: key-stationary tiles equal the forced run.
+    n_q = 0
+    for b in range(B):
+        for h in range(H):
+            for t0 in range(0, N, 128):
+                sel = idx[b, h, t0:t0 + 128]
+                q_tile = len(np.unique(sel[sel >= 0])) <= (5 * k) // 2
+                n_q += q_tile
+                if not q_tile:
+                    assert np.array_equal(O[b, h, t0:t0 + 128], O_kv[b, h, t0:t0 + 128])
+    assert n_q >= (N // 256) * B * H        # at least the even tiles
+    assert not np.array_equal(O, O_kv), "query tiles not dispatched"
