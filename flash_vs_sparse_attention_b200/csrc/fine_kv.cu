@@ -1042,8 +1042,10 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
         tc_fence_after();
         if (storer) publish_o_done(tp);
       }
-      // p = 2^(s sc - m sc), summed per row in (even, odd) column halves.
-      float l0 = 0.f, l1 = 0.f;
+      // p = 2^(s sc - m sc), summed per row in (even, odd) column halves
+      // (packed pairs: one fma and one add per two columns).
+      float2 l2 = make_float2(0.f, 0.f);
+      const float2 sc2 = make_float2(sc, sc), sh2 = make_float2(-msh, -msh);
 #pragma unroll
       for (int c0 = 0; c0 < BS; c0 += 64) {
 #pragma unroll
@@ -1051,16 +1053,24 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
           uint32_t pk[16];
 #pragma unroll
           for (int c = 0; c < 32; c += 2) {
-            const float p0 = fast_exp2(fmaf(sv[c0 + h + c], sc, -msh));
-            const float p1 = fast_exp2(fmaf(sv[c0 + h + c + 1], sc, -msh));
-            l0 += p0;
-            l1 += p1;
+            float p0, p1;
+            if constexpr (BS == 64) {
+              const float2 x = ffma2(make_float2(sv[c0 + h + c], sv[c0 + h + c + 1]), sc2, sh2);
+              p0 = fast_exp2(x.x);
+              p1 = fast_exp2(x.y);
+              l2 = fadd2(l2, make_float2(p0, p1));
+            } else {   // the 128-key block has no registers to spare for pairs
+              p0 = fast_exp2(fmaf(sv[c0 + h + c], sc, -msh));
+              p1 = fast_exp2(fmaf(sv[c0 + h + c + 1], sc, -msh));
+              l2.x += p0;
+              l2.y += p1;
+            }
             pk[c >> 1] = pack_bf16x2(p0, p1);
           }
           tmem_st16(p_addr + ((c0 + h) >> 1), pk);
         }
       }
-      const float l = l0 + l1;
+      const float l = l2.x + l2.y;
       bool issued_next = false;
       if (s_issuer && t + NWG < T) {
         // Every row of S(t) has been read: S(t + NWG) may go into its columns

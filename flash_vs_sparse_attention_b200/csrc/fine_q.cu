@@ -543,21 +543,30 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
         const uint32_t p_addr = tbase + lane_off + C::kPCol + b * (BS / 2);
         if (__any_sync(0xffffffffu, live)) {
           const float shift = live ? m_run : INFINITY;   // not live: every p = 0
-          float l0 = 0.f, l1 = 0.f;
+          float2 l2 = make_float2(0.f, 0.f);
+          const float2 sc2 = make_float2(sc, sc), sh2 = make_float2(-shift, -shift);
 #pragma unroll
           for (int c0 = 0; c0 < BS; c0 += 32) {
             uint32_t pk[16];
 #pragma unroll
             for (int c = 0; c < 32; c += 2) {
-              const float p0 = fast_exp2(fmaf(sv[c0 + c], sc, -shift));
-              const float p1 = fast_exp2(fmaf(sv[c0 + c + 1], sc, -shift));
-              l0 += p0;
-              l1 += p1;
+              float p0, p1;
+              if constexpr (BS == 64) {   // packed pairs: one fma and one add per two keys
+                const float2 x = ffma2(make_float2(sv[c0 + c], sv[c0 + c + 1]), sc2, sh2);
+                p0 = fast_exp2(x.x);
+                p1 = fast_exp2(x.y);
+                l2 = fadd2(l2, make_float2(p0, p1));
+              } else {
+                p0 = fast_exp2(fmaf(sv[c0 + c], sc, -shift));
+                p1 = fast_exp2(fmaf(sv[c0 + c + 1], sc, -shift));
+                l2.x += p0;
+                l2.y += p1;
+              }
               pk[c >> 1] = pack_bf16x2(p0, p1);
             }
             tmem_st16(p_addr + (c0 >> 1), pk);
           }
-          if (live) l += l0 + l1;
+          if (live) l += l2.x + l2.y;
         } else {
           uint32_t pk[16];
 #pragma unroll
