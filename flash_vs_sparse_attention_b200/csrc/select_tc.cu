@@ -227,9 +227,16 @@ select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
       const int lim = !valid ? 0 : (s.causal ? min(s.nb, row / s.bs + 1) : s.nb);
       RowTopK<KCAP> sel;
       sel.init(cbuf + r, kSelRows, C::kCap, s.k);
-      float gm[32];
+      // Group maxima: 32 strided groups (column % 32) for top_k <= 16; for
+      // larger top_k 64 groups (column % 64: the two halves gm / gm2, by the
+      // parity of the 32-column chunk), whose k-th largest maximum is a much
+      // tighter floor than the smallest of 32 when k is 32 or more.
+      constexpr bool kG64 = KCAP > 16;
+      float gm[32], gm2[kG64 ? 32 : 1];
 #pragma unroll
       for (int i = 0; i < 32; ++i) gm[i] = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < (kG64 ? 32 : 1); ++i) gm2[i] = -INFINITY;
       for (int ww = 0; ww < 2 * nw; ++ww, ++kw) {
         const int pass = ww >= nw;
         const int w = ww - pass * nw;
@@ -261,7 +268,11 @@ select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
             if (need_mask || !valid) {
 #pragma unroll
               for (int i = 0; i < 32; ++i)
-                gm[i] = fmaxf(gm[i], ((vm >> i) & 1u) ? x[i] : -INFINITY);
+                if (((vm >> i) & 1u) == 0u) x[i] = -INFINITY;
+            }
+            if (kG64 && ((j0 >> 5) & 1)) {   // the same for the whole warp
+#pragma unroll
+              for (int i = 0; i < (kG64 ? 32 : 1); ++i) gm2[i] = fmaxf(gm2[i], x[i]);
             } else {
 #pragma unroll
               for (int i = 0; i < 32; ++i) gm[i] = fmaxf(gm[i], x[i]);
@@ -284,8 +295,12 @@ select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
           tc_fence_before();
           mbar_arrive(&s_free[b]);
         }
-        if (pass == 0 && w == nw - 1 && s.k <= 32)
-          sel.raise_floor(kth_of_32(gm, s.k));   // -inf if fewer than k groups are non-empty
+        // The floor: the k-th largest group maximum (-inf if fewer than k
+        // groups are non-empty).
+        if (pass == 0 && w == nw - 1) {
+          if constexpr (kG64) sel.raise_floor(kth_of_64(gm, gm2, s.k));
+          else if (s.k <= 32) sel.raise_floor(kth_of_32(gm, s.k));
+        }
       }
       if (!ok) break;
       if (valid) sel.emit(prm.idx + ((int64_t)unit * s.N + row) * s.k);

@@ -201,4 +201,32 @@ __device__ __forceinline__ float kth_of_32(float (&v)[32], int k) {
   return T;
 }
 
+// k-th largest of the 64 values lo[0..32) and hi[0..32) (1 <= k <= 64):
+// bitonic sort of the 64 values, descending, in registers (lo then hi); the
+// min of the first k.
+__device__ __forceinline__ float kth_of_64(float (&lo)[32], float (&hi)[32], int k) {
+  float v[64];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) { v[i] = lo[i]; v[32 + i] = hi[i]; }
+#pragma unroll
+  for (int k2 = 2; k2 <= 64; k2 <<= 1) {
+#pragma unroll
+    for (int j = k2 >> 1; j > 0; j >>= 1) {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const int l = i ^ j;
+        if (l > i) {
+          const float a = v[i], b = v[l];
+          const float hv = fmaxf(a, b), lv = fminf(a, b);
+          if ((i & k2) == 0) { v[i] = hv; v[l] = lv; } else { v[i] = lv; v[l] = hv; }
+        }
+      }
+    }
+  }
+  float T = INFINITY;
+#pragma unroll
+  for (int p = 0; p < 64; ++p) T = fminf(T, p < k ? v[p] : INFINITY);
+  return T;
+}
+
 }  // namespace bsa
