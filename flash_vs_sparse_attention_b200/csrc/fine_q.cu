@@ -16,10 +16,11 @@
 // the partial round trip of the key-stationary path.
 //
 // fine_q_kernel, persistent over the query-tile slots.  Per tile: TMA loads
-// the 128 query rows once (two buffers, so the next tile's rows load early);
+// the 128 query rows once (two buffers where room allows, so the next tile's
+// rows load early);
 // for every block j of the union, in ascending order, TMA loads K_j and V_j
 // (plain tiled loads into a ring of stages), tcgen05 computes
-// S = Q K_j^T into TMEM (two S buffers), the softmax warpgroup (one thread
+// S = Q K_j^T into TMEM (one or two S buffers), the softmax warpgroup (one thread
 // per row) masks the rows that did not select j and the keys past a row's
 // position (causal), and turns S into P (bf16, TMEM, two buffers) against a
 // running row maximum, and tcgen05 accumulates O += P V_j in TMEM.  The
@@ -62,23 +63,29 @@ struct QCfg {
   static constexpr int kQBytes = kQRows * HD * 2;
   static constexpr int kKBytes = BS * HD * 2;
   static constexpr int kStageBytes = 2 * kKBytes;          // K_j and V_j
-  static constexpr int NS = (BS == 64 && HD == 64) ? 4 : 3;  // K/V stages
-  static constexpr int kCtasPerSm = (BS == 64 && HD == 64) ? 2 : 1;
-  static constexpr int kStageOff = 2 * kQBytes;
+  // Two CTAs per SM where TMEM (256 columns each) and shared memory allow:
+  // head_dim 128 then keeps one Q buffer, one S buffer and two K/V stages
+  // (the other CTA fills the gaps these leave); block 128 runs one CTA.
+  static constexpr int kCtasPerSm = (BS == 64) ? 2 : 1;
+  static constexpr int kQBufs = (BS == 64 && HD == 128) ? 1 : 2;
+  static constexpr int kSBufs = (BS == 64 && HD == 128) ? 1 : 2;
+  static constexpr int NS = (BS == 64 && HD == 64) ? 4 : ((BS == 64) ? 2 : 3);   // K/V stages
+  static constexpr int kStageOff = kQBufs * kQBytes;
   static constexpr int kRowBitsOff = kStageOff + NS * kStageBytes;
   static constexpr int kRowBitsBytes = kQUnionWords * kQRows * 4;
   static constexpr int kTileBitsOff = kRowBitsOff + kRowBitsBytes;
   static constexpr int kTileBitsBytes = 2 * kQMaxNbWords * 4;   // bits, then prefix counts
   static constexpr int kBarOff = kTileBitsOff + kTileBitsBytes;
   static constexpr int kSmem = kBarOff + 256 + 1024 /*alignment*/;
-  // TMEM: S[2] (BS columns each), P[2] (bf16 pairs, BS / 2 each), O (HD).
-  static constexpr int kSCol = 0, kPCol = 2 * BS, kOCol = 3 * BS;
-  static constexpr int kCols = 3 * BS + HD;
+  // TMEM: S[kSBufs] (BS columns each), P[2] (bf16 pairs, BS / 2 each), O (HD).
+  static constexpr int kSCol = 0, kPCol = kSBufs * BS, kOCol = kSBufs * BS + BS;
+  static constexpr int kCols = kSBufs * BS + BS + HD;
   static constexpr int kTmemCols = kCols <= 256 ? 256 : 512;
   static_assert(kCols <= 512, "TMEM");
   static_assert(kStageOff % 1024 == 0 && kStageBytes % 1024 == 0, "swizzled tiles");
   static_assert(kSmem <= 227 * 1024, "shared memory");
   static_assert(kCtasPerSm * (kSmem + 1024) <= 228 * 1024, "CTAs per SM");
+  static_assert(kCtasPerSm * kTmemCols <= 512, "TMEM per SM");
 };
 
 }  // namespace
@@ -312,8 +319,9 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
       for (int n = 0; ok && n < my_tiles; ++n) {
         const int4 info = __ldg(prm.qt_info + slot_of(n));
         const int unit = info.x, tile = info.y;
-        const int qb = n & 1;
-        if (n >= 2) ok = mbar_wait(&q_empty[qb], ((n - 2) >> 1) & 1, prm.err, kErrQWaitQ);
+        const int qb = n % C::kQBufs;
+        if (n >= C::kQBufs)
+          ok = mbar_wait(&q_empty[qb], ((n - C::kQBufs) / C::kQBufs) & 1, prm.err, kErrQWaitQ);
         if (!ok || *abort_flag) { ok = false; break; }
         mbar_arrive_expect_tx(&q_full[qb], C::kQBytes);
         ++qn;
@@ -350,9 +358,9 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
           const int last = g - 1 - ((g - 1 - st) % NS + NS) % NS;
           if (last >= 0) mbar_wait(&kv_full[st], (last / NS) & 1, prm.err, kErrQWaitKV);
         }
-        for (int qb = 0; qb < 2; ++qb) {
-          const int last = qn - 1 - ((qn - 1 - qb) % 2 + 2) % 2;
-          if (last >= 0) mbar_wait(&q_full[qb], (last >> 1) & 1, prm.err, kErrQWaitQ);
+        for (int qb = 0; qb < C::kQBufs; ++qb) {
+          const int last = qn - 1 - ((qn - 1 - qb) % C::kQBufs + C::kQBufs) % C::kQBufs;
+          if (last >= 0) mbar_wait(&q_full[qb], (last / C::kQBufs) & 1, prm.err, kErrQWaitQ);
         }
       }
     }
@@ -386,13 +394,14 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
       bool ok = true;
       for (int n = 0; ok && n < my_tiles; ++n) {
         const int U = __ldg(prm.qt_info + slot_of(n)).z;
-        const int qb = n & 1;
-        ok = mbar_wait(&q_full[qb], (n >> 1) & 1, prm.err, kErrQWaitQ);
+        const int qb = n % C::kQBufs;
+        ok = mbar_wait(&q_full[qb], (n / C::kQBufs) & 1, prm.err, kErrQWaitQ);
         const uint64_t dq = dq0 + ((uint64_t)(qb * C::kQBytes) >> 4);
         for (int i = 0; ok && i < U; ++i, ++g) {
-          const int st = g % NS, b = g & 1;
+          const int st = g % NS, sb = g % C::kSBufs;
           ok = mbar_wait(&kv_full[st], (g / NS) & 1, prm.err, kErrQWaitKV);
-          if (ok && g >= 2) ok = mbar_wait(&s_free[b], ((g - 2) >> 1) & 1, prm.err, kErrQWaitS);
+          if (ok && g >= C::kSBufs)
+            ok = mbar_wait(&s_free[sb], ((g - C::kSBufs) / C::kSBufs) & 1, prm.err, kErrQWaitS);
           if (!ok || *abort_flag) { ok = false; break; }
           tc_fence_after();
           const uint64_t dk = dk0 + ((uint64_t)(st * C::kStageBytes) >> 4);
@@ -400,10 +409,10 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
           for (int kk = 0; kk < HD / 16; ++kk) {
             const uint32_t off = (kk >> 2) * (kQRows * 128) + (kk & 3) * 32;
             const uint32_t offk = (kk >> 2) * (BS * 128) + (kk & 3) * 32;
-            mma_bf16(tbase + C::kSCol + b * BS, dq + (off >> 4), dk + (offk >> 4), idesc_s,
+            mma_bf16(tbase + C::kSCol + sb * BS, dq + (off >> 4), dk + (offk >> 4), idesc_s,
                      kk > 0 ? 1u : 0u);
           }
-          mma_commit(&s_full[b]);
+          mma_commit(&s_full[sb]);
           if (i == U - 1) mma_commit(&q_empty[qb]);
           if (i >= 1) ok = pv(g - 1, n, i == 1);
         }
@@ -477,18 +486,20 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
         cw &= cw - 1u;
         if ((i & 31) == 0) rw = rowbits[(i >> 5) * kQRows + r];
         const bool sel = ((rw >> (i & 31)) & 1u) != 0u;
-        const int b = g & 1;
-        ok = mbar_wait(&s_full[b], (g >> 1) & 1, prm.err, kErrQWaitS);
+        const int b = g & 1;                            // P buffer
+        const int sb = g % C::kSBufs;                   // S buffer
+        ok = mbar_wait(&s_full[sb], (g / C::kSBufs) & 1, prm.err, kErrQWaitS);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok || *abort_flag) { ok = false; break; }
         tc_fence_after();
         float sv[BS];
         if (__any_sync(0xffffffffu, sel)) {
 #pragma unroll
-          for (int c0 = 0; c0 < BS; c0 += 64) tmem_ld64(tbase + lane_off + C::kSCol + b * BS + c0, sv + c0);
+          for (int c0 = 0; c0 < BS; c0 += 64)
+            tmem_ld64(tbase + lane_off + C::kSCol + sb * BS + c0, sv + c0);
         }
         tc_fence_before();
-        mbar_arrive(&s_free[b]);                        // S(g) is in registers
+        mbar_arrive(&s_free[sb]);                       // S(g) is in registers
         float mx = -INFINITY;
         if (sel) {
           // Token-level causal mask (block_indexer.py:73-81): key > query -> -inf.
