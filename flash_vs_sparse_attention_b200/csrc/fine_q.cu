@@ -12,8 +12,10 @@
 // marks it, so the bucket kernels treat its rows' entries as empty and the
 // combine leaves its rows alone.  Every other tile goes through the
 // key-block-stationary path (fine_kv.cu).  The default max_union is
-// 2.5 top_k: below it the tile's dense work over its union costs less than
-// the partial round trip of the key-stationary path.
+// 3 top_k: up to there the tile's dense work over its union costs less than
+// the partial round trip of the key-stationary path (on clustered content,
+// B2 H32 N32768 D128 k32: 14.08 ms per step at 2.5 top_k, 12.39 at 3, 12.42
+// at 4).
 //
 // fine_q_kernel, persistent over the query-tile slots.  Per tile: TMA loads
 // the 128 query rows once (two buffers where room allows, so the next tile's
@@ -657,7 +659,7 @@ bool fine_q_supported(const Shape& s) {
 int fine_q_max_union(const Shape& s, uint32_t flags) {
   if (flags & BSA_FLAG_FINE_KEY_STATIONARY) return 0;
   if (flags & BSA_FLAG_FINE_QUERY_STATIONARY) return kQMaxUnion;
-  return min(kQMaxUnion, (5 * s.k) / 2);
+  return min(kQMaxUnion, 3 * s.k);
 }
 
 int fine_q_tiles(const Shape& s) { return (s.N + kQRows - 1) / kQRows; }

@@ -61,8 +61,8 @@ typedef enum bsa_status {
  * key-block-stationary kernel (every selected block with the queries that
  * picked it, partial results merged per query) and a query-stationary one
  * (the tile's rows over the union of their selected blocks, the output
- * written once), by the size of that union: at most 2.5 top_k blocks ->
- * query-stationary.  These force one side (tests compare them):
+ * written once), by the size of that union: at most 3 top_k blocks ->
+ * query-stationary, when such tiles are at least half of all tiles.  These force one side (tests compare them):
  * KEY_STATIONARY sends every tile to the first, QUERY_STATIONARY every tile
  * whose union is at most 512 blocks to the second. */
 #define BSA_FLAG_FINE_KEY_STATIONARY 16u
