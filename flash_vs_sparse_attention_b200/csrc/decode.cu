@@ -77,13 +77,116 @@ expand_block_selection_kernel(const int32_t* __restrict__ bidx, int32_t* __restr
   }
 }
 
+// Per-query-block selection, kQbRows pooled rows per CTA: every block-mean
+// row is loaded once and scored against all of the CTA's rows (the same
+// sequential fp32 dot products as select_row, so the same picks); then warp
+// r runs row r's top_k rounds of a warp arg-max (score descending, block
+// ascending) over its eligible blocks, as select_row does, and writes the
+// picks in ascending block order, -1 padded.  Dynamic shared memory:
+// rows * (D + nb) floats.
+constexpr int kQbRows = 8;
+
+__global__ void __launch_bounds__(kQbRows * 32)
+qblock_select_kernel(const float* __restrict__ Q_repr, const float* __restrict__ K_repr,
+                     int32_t* __restrict__ bidx, Shape s, int rows_per_cta) {
+  extern __shared__ __align__(16) float qsm[];
+  __shared__ int32_t picks[kQbRows][64];
+  const int R = rows_per_cta;
+  const int cpu = (s.nb + R - 1) / R;            // CTAs per unit
+  const int64_t unit = blockIdx.x / cpu;
+  const int i0 = (int)(blockIdx.x % cpu) * R;    // this CTA's first query block
+  const int nr = min(R, s.nb - i0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* qs = qsm;                               // R x D pooled rows
+  float* sc = qsm + (size_t)R * s.D;             // R x nb scores
+  for (int e = tid; e < nr * s.D; e += kQbRows * 32)
+    qs[e] = __ldg(Q_repr + (unit * s.nb + i0) * (int64_t)s.D + e);
+  __syncthreads();
+  const int lim_max = s.causal ? min(s.nb, i0 + nr) : s.nb;
+  const float* kr = K_repr + unit * s.nb * (int64_t)s.D;
+  const int d4n = s.D >> 2;
+  for (int j = tid; j < lim_max; j += kQbRows * 32) {
+    const float4* kj = reinterpret_cast<const float4*>(kr + (int64_t)j * s.D);
+    float a[kQbRows];
+#pragma unroll
+    for (int r = 0; r < kQbRows; ++r) a[r] = 0.f;
+    for (int d0 = 0; d0 < d4n; d0 += 16) {   // 16 row loads in flight, then their FMAs
+      float4 k4[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u)
+        k4[u] = d0 + u < d4n ? __ldg(kj + d0 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        if (d0 + u < d4n) {
+#pragma unroll
+          for (int r = 0; r < kQbRows; ++r) {
+            if (r < nr) {
+              const float* qd = qs + r * s.D + 4 * (d0 + u);
+              a[r] = fmaf(qd[0], k4[u].x, a[r]);
+              a[r] = fmaf(qd[1], k4[u].y, a[r]);
+              a[r] = fmaf(qd[2], k4[u].z, a[r]);
+              a[r] = fmaf(qd[3], k4[u].w, a[r]);
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kQbRows; ++r)
+      if (r < nr) sc[(size_t)r * s.nb + j] = a[r] * s.scale;
+  }
+  __syncthreads();
+  if (warp >= nr) return;
+  const int i = i0 + warp;                       // this warp's query block
+  const int lim = s.causal ? i + 1 : s.nb;       // eligible: [0, lim)
+  float* row = sc + (size_t)warp * s.nb;
+  int n = 0;
+  for (; n < s.k; ++n) {
+    float bv = -INFINITY;
+    int bj = 0x7fffffff;
+    for (int j = lane; j < lim; j += 32) {       // blocks ascend within a lane
+      const float v = row[j];
+      if (v > bv) { bv = v; bj = j; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oj = __shfl_xor_sync(0xffffffffu, bj, o);
+      if (ov > bv || (ov == bv && oj < bj)) { bv = ov; bj = oj; }
+    }
+    if (bv == -INFINITY) break;                  // no eligible block left
+    if (lane == 0) picks[warp][n] = bj;
+    if ((bj & 31) == lane) row[bj] = -INFINITY;  // the owning lane retires the pick
+    __syncwarp();
+  }
+  int32_t* out = bidx + (unit * s.nb + i) * (int64_t)s.k;
+  for (int t = lane; t < s.k; t += 32) {
+    if (t < n) {
+      const int v = picks[warp][t];
+      int rank = 0;
+      for (int u = 0; u < n; ++u) rank += picks[warp][u] < v ? 1 : 0;
+      out[rank] = v;
+    } else {
+      out[t] = -1;
+    }
+  }
+}
+
 cudaError_t launch_qblock_select(const float* Q_repr, const float* K_repr, int32_t* bidx,
                                  int32_t* idx, const Shape& s, cudaStream_t st) {
-  Shape sb = s;
-  sb.Nq = s.nb;     // one pooled row per query block
-  sb.q0 = 0;
-  sb.kv = s.N;
-  cudaError_t e = launch_select_rows<true>(Q_repr, K_repr, bidx, sb, st);
+  int R = kQbRows;
+  while (R > 1 && sizeof(float) * (size_t)R * (s.D + s.nb) > 200 * 1024) R >>= 1;
+  const size_t smem = sizeof(float) * (size_t)R * (s.D + s.nb);
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(qblock_select_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  const int64_t grid = (int64_t)s.units * ((s.nb + R - 1) / R);
+  if (grid > 0) qblock_select_kernel<<<(unsigned)grid, kQbRows * 32, smem, st>>>(Q_repr, K_repr,
+                                                                                 bidx, s, R);
+  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int64_t total = (int64_t)s.units * s.N * s.k;
   const int64_t blocks = (total + 255) / 256;
