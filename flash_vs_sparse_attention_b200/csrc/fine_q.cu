@@ -471,12 +471,30 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
       const int UW = (U + 31) >> 5;
       for (int w = 0; w < UW; ++w) rowbits[w * kQRows + r] = 0u;
       if (valid) {
+        // The row's indices, 16 per batch with every load of the batch in
+        // flight before the first is used (16-byte loads when aligned).
         const int32_t* p = prm.idx + ((int64_t)unit * s.N + row) * s.k;
-        for (int t = 0; t < s.k; ++t) {
-          const int j = __ldg(p + t);
-          if (j < 0) continue;
-          const int pos = (int)tpre[j >> 5] + __popc(tb[j >> 5] & ((1u << (j & 31)) - 1u));
-          rowbits[(pos >> 5) * kQRows + r] |= 1u << (pos & 31);
+        const bool vec = (s.k & 3) == 0 && (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+        for (int t0 = 0; t0 < s.k; t0 += 16) {
+          int v[16];
+          if (vec) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int4 x = t0 + 4 * q < s.k ? __ldg(reinterpret_cast<const int4*>(p + t0) + q)
+                                              : make_int4(-1, -1, -1, -1);
+              v[4 * q] = x.x; v[4 * q + 1] = x.y; v[4 * q + 2] = x.z; v[4 * q + 3] = x.w;
+            }
+          } else {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) v[q] = t0 + q < s.k ? __ldg(p + t0 + q) : -1;
+          }
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const int j = v[q];
+            if (j < 0) continue;
+            const int pos = (int)tpre[j >> 5] + __popc(tb[j >> 5] & ((1u << (j & 31)) - 1u));
+            rowbits[(pos >> 5) * kQRows + r] |= 1u << (pos & 31);
+          }
         }
       }
       float m_run = -INFINITY, l = 0.f;
