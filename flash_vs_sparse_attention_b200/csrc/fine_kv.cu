@@ -1067,9 +1067,10 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
             }
             pk[c >> 1] = pack_bf16x2(p0, p1);
           }
-          tmem_st16(p_addr + ((c0 + h) >> 1), pk);
+          tmem_st16_async(p_addr + ((c0 + h) >> 1), pk);
         }
       }
+      tmem_wait_st();   // every P store of the item has landed
       const float l = l2.x + l2.y;
       bool issued_next = false;
       if (s_issuer && t + NWG < T) {

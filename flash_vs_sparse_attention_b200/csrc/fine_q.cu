@@ -595,7 +595,7 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
               }
               pk[c >> 1] = pack_bf16x2(p0, p1);
             }
-            tmem_st16(p_addr + (c0 >> 1), pk);
+            tmem_st16_async(p_addr + (c0 >> 1), pk);
           }
           if (live) l += l2.x + l2.y;
         } else {
@@ -603,8 +603,9 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
 #pragma unroll
           for (int c = 0; c < 16; ++c) pk[c] = 0u;
 #pragma unroll
-          for (int c0 = 0; c0 < BS; c0 += 32) tmem_st16(p_addr + (c0 >> 1), pk);
+          for (int c0 = 0; c0 < BS; c0 += 32) tmem_st16_async(p_addr + (c0 >> 1), pk);
         }
+        tmem_wait_st();                                 // P(g) is in TMEM
         tc_fence_before();
         mbar_arrive(&p_full[b]);
       }
