@@ -11,7 +11,10 @@ are quoted on).  Rank 0 prints one JSON line.
 * ``value``: effective TFLOP/s (FLOPs of the reference's benchmark/flops.py
   model, summed over every unit all ranks processed, divided by the max over
   ranks of the CUDA-event time of K steps), inputs resident in HBM, L2
-  flushed before every step.  With N GPUs the workload's (batch, head) units
+  flushed before every step.  Each timed step replays a CUDA graph of one
+  whole forward (captured once after the warm-up: every kernel and memset
+  of the step runs every step; ``--no-graph`` launches them directly).
+  With N GPUs the workload's (batch, head) units
   are split over the ranks (``--scaling strong``, the default; ``weak`` runs
   the whole workload on every rank); ``with_gather`` then times the forward
   plus the NCCL all-gather that assembles the whole output on every rank.
@@ -233,7 +236,7 @@ def run_ours(args, cfg):
     n_launch = ctypes.c_int(0)
     ev_arr = (ctypes.c_void_p * len(STAGES))()
 
-    def forward(stage_events=None):
+    def forward(stage_events=None, stream_handle=None):
         if stage_events is not None:
             for i, e in enumerate(stage_events):
                 ev_arr[i] = ctypes.c_void_p(e.cuda_event)
@@ -243,14 +246,35 @@ def run_ours(args, cfg):
         st = L.bsa_forward_ex(ctypes.byref(p), ctypes.c_void_p(Q.data_ptr()),
                               ctypes.c_void_p(K.data_ptr()), ctypes.c_void_p(V.data_ptr()),
                               ctypes.c_void_p(O.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
-                              ctypes.c_size_t(ws_bytes), sp, evp, len(STAGES) if evp else 0,
-                              ctypes.byref(n_launch))
+                              ctypes.c_size_t(ws_bytes), stream_handle or sp, evp,
+                              len(STAGES) if evp else 0, ctypes.byref(n_launch))
         _lib.check(st, "bsa_forward_ex")
 
     for _ in range(args.warmup):
         flush.zero_()
         forward()
     torch.cuda.synchronize()
+
+    # The timed steps replay a CUDA graph of one forward (every kernel and
+    # memset of the step, captured once with the same buffers), which removes
+    # the per-launch gaps the host call leaves between kernels; the stage
+    # times come from a second, directly launched pass with stage events.
+    graph = None
+    if not args.no_graph:
+        gs = torch.cuda.Stream(dev)
+        gs.wait_stream(stream)
+        with torch.cuda.stream(gs):
+            forward(stream_handle=ctypes.c_void_p(gs.cuda_stream))
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=gs):
+            forward(stream_handle=ctypes.c_void_p(gs.cuda_stream))
+        torch.cuda.synchronize()
+        graph_launches = n_launch.value
+        for _ in range(2):
+            flush.zero_()
+            graph.replay()
+        torch.cuda.synchronize()
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -269,16 +293,29 @@ def run_ours(args, cfg):
         for i in range(args.steps):
             flush.zero_()
             starts[i].record(stream)
-            forward(stage_ev[i])
+            if graph is not None:
+                graph.replay()
+                launches += graph_launches
+            else:
+                forward(stage_ev[i])
+                launches += n_launch.value
             ends[i].record(stream)
-            launches += n_launch.value
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    stage_starts = starts
+    if graph is not None:
+        # Stage times: the same steps launched directly with stage events.
+        stage_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        for i in range(args.steps):
+            flush.zero_()
+            stage_starts[i].record(stream)
+            forward(stage_ev[i])
+        torch.cuda.synchronize()
     stage_ms = {name: [] for name in STAGES}
     for i in range(args.steps):
-        prev = starts[i]
+        prev = stage_starts[i]
         for name, e in zip(STAGES, stage_ev[i]):
             stage_ms[name].append(prev.elapsed_time(e))
             prev = e
@@ -424,7 +461,10 @@ def run_ours(args, cfg):
                        "heads": cfg["H"], "seq_len": cfg["N"], "head_dim": cfg["D"],
                        "block_size": cfg["block_size"], "top_k": cfg["top_k"],
                        "causal": cfg["causal"], "parallelism": f"head-sharded x{world}",
-                       "l2": f"flushed before every step ({L2_FLUSH_BYTES >> 20} MiB write, outside the events)"},
+                       "l2": f"flushed before every step ({L2_FLUSH_BYTES >> 20} MiB write, outside the events)",
+                       "launch": ("one CUDA graph of a whole forward (all its kernels and memsets), "
+                                  "captured once and replayed every step; stage times from a "
+                                  "direct pass") if graph is not None else "direct launches"},
             "hbm_gbs": round(hbm_bytes * args.steps / (total_ms * 1e-3) / 1e9, 2),
             "hbm_gbs_note": "compulsory bytes (read Q,K,V + write O) / step time",
             "stages_ms": {k: round(statistics.mean(v), 4) for k, v in stage_ms.items()},
@@ -707,6 +747,8 @@ def main(argv=None):
                     help="run only this many (batch, head) units of the workload (0: all); "
                          "for small profiling captures, not for bench lines")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch the timed steps directly instead of replaying a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mode", default="forward", choices=["forward", "decode"],
                     help="decode: one-token decode steps over a KV cache (its own JSON line)")
