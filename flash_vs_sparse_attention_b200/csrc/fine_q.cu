@@ -19,13 +19,13 @@
 //
 // fine_q_kernel, persistent over the query-tile slots.  Per tile: TMA loads
 // the 128 query rows once (two buffers where room allows, so the next tile's
-// rows load early);
-// for every block j of the union, in ascending order, TMA loads K_j and V_j
-// (plain tiled loads into a ring of stages), tcgen05 computes
-// S = Q K_j^T into TMEM (one or two S buffers), the softmax warpgroup (one thread
-// per row) masks the rows that did not select j and the keys past a row's
-// position (causal), and turns S into P (bf16, TMEM, two buffers) against a
-// running row maximum, and tcgen05 accumulates O += P V_j in TMEM.  The
+// rows load early); for every block j of the union, in ascending order, TMA
+// loads K_j and V_j (plain tiled loads into a ring of stages, the blocks a
+// few ahead prefetched into L2 first), tcgen05 computes S = Q K_j^T into
+// TMEM (one or two S buffers), the softmax warpgroup (one thread per row)
+// masks the rows that did not select j and the keys past a row's position
+// (causal), and turns S into P (bf16, TMEM, two buffers) against a running
+// row maximum, and tcgen05 accumulates O += P V_j in TMEM.  The
 // running maximum is raised lazily: only when a block's maximum exceeds it by
 // more than 8 (a factor 2^8 in P) are the row's O and l rescaled, after the
 // previous block's PV has completed; P never exceeds 2^8.  At the end of the
@@ -53,6 +53,7 @@ constexpr int kQMaxUnion = 512;      // union blocks a query tile may have
 constexpr int kQUnionWords = kQMaxUnion / 32;
 constexpr int kQMaxNbWords = 512;    // block-bitmask words (nb <= 16384)
 constexpr int kQThreads = 192;
+constexpr int kQPrefetch = 4;        // union blocks whose K/V go to L2 ahead of their loads
 
 // Error bits of this kernel's bounded waits (the fine stage's error word).
 // kErrQTestTimeout is the key-stationary kernel's test-hook bit (same meaning).
@@ -198,6 +199,8 @@ classify_tiles_kernel(const int32_t* __restrict__ idx, uint8_t* __restrict__ til
 
 // ---------------------------------------------------------------------------
 struct FineQParams {
+  const __nv_bfloat16* K;    // (units, N, HD): for the L2 prefetches
+  const __nv_bfloat16* V;
   const int32_t* idx;        // (units, N, top_k) selections
   const uint32_t* qt_bits;   // per query-tile slot: the union bitmask (nbw words)
   const int4* qt_info;       // per slot: unit, tile, union size
@@ -332,6 +335,21 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
           tma_load_2d(q_s(qb) + p * (kQRows * 128), &tmap_q, &q_full[qb], p * 64,
                       unit * s.N + tile * kQRows);
         const uint32_t* bw = prm.qt_bits + (int64_t)slot_of(n) * nbw;
+        // The K/V blocks kQPrefetch ahead of the loads go to L2 first, so a
+        // stage's TMA load (which waits for the PV two blocks back) finds
+        // them there.
+        int pw = 0;
+        uint32_t pm = __ldg(bw);
+        auto prefetch_next = [&]() {
+          while (pm == 0u && pw + 1 < nbw) pm = __ldg(bw + ++pw);
+          if (pm == 0u) return;
+          const int jp = pw * 32 + __ffs(pm) - 1;
+          pm &= pm - 1u;
+          const int64_t off = ((int64_t)unit * s.N + (int64_t)jp * BS) * HD;
+          bulk_prefetch_l2(prm.K + off, (uint32_t)C::kKBytes);
+          bulk_prefetch_l2(prm.V + off, (uint32_t)C::kKBytes);
+        };
+        for (int q = 0; q < kQPrefetch; ++q) prefetch_next();
         for (int w = 0; ok && w < nbw; ++w) {
           uint32_t m = __ldg(bw + w);
           while (m != 0u) {
@@ -347,6 +365,7 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
               tma_load_2d(k_s(st) + p * (BS * 128), &tmap_k, &kv_full[st], p * 64, y);
               tma_load_2d(v_s(st) + p * (BS * 128), &tmap_v, &kv_full[st], p * 64, y);
             }
+            prefetch_next();
             ++g;
           }
         }
@@ -725,6 +744,8 @@ cudaError_t launch_fine_q(const __nv_bfloat16* Q, const __nv_bfloat16* K, const 
                           const int4* qt_info, const uint32_t* n_qt, int min_q_tiles,
                           uint32_t* err, const Shape& s, cudaStream_t st) {
   FineQParams prm;
+  prm.K = K;
+  prm.V = V;
   prm.idx = idx;
   prm.qt_bits = qt_bits;
   prm.qt_info = qt_info;

@@ -340,6 +340,11 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
 
 // Store 16 consecutive 32-bit columns of this warp's 32 TMEM lanes, then wait
 // until the stores are complete.
+// Prefetch `bytes` (a multiple of 16, 16-byte aligned) at `p` into L2.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // tmem_st16 without the wait: several stores in flight, then one
 // tmem_wait_st() before anything that needs them in TMEM (an MMA).
 __device__ __forceinline__ void tmem_st16_async(uint32_t taddr, const uint32_t* r) {
