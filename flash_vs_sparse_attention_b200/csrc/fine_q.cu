@@ -64,28 +64,31 @@ constexpr uint32_t kErrQWaitQ = 1u << 12, kErrQWaitKV = 1u << 13, kErrQWaitS = 1
 template <int BS, int HD>
 struct QCfg {
   static constexpr int kQBytes = kQRows * HD * 2;
-  static constexpr int kKBytes = BS * HD * 2;
-  static constexpr int kStageBytes = 2 * kKBytes;          // K_j and V_j
+  static constexpr int kKBytes = BS * HD * 2;               // one block of K (or V)
   // Two CTAs per SM where TMEM (256 columns each) and shared memory allow:
-  // head_dim 128 then keeps one Q buffer, one S buffer and two K/V stages
-  // (the other CTA fills the gaps these leave); block 128 runs one CTA.
+  // head_dim 128 then keeps one Q buffer, one S buffer and two K and two V
+  // stages (the other CTA fills the gaps these leave); block 128 runs one CTA.
+  // K and V have rings of their own: K_j's stage is free once S(j) is done,
+  // V_j's once PV(j) is, so K loads run ahead of V loads.
   static constexpr int kCtasPerSm = (BS == 64) ? 2 : 1;
   static constexpr int kQBufs = (BS == 64 && HD == 128) ? 1 : 2;
   static constexpr int kSBufs = (BS == 64 && HD == 128) ? 1 : 2;
-  static constexpr int NS = (BS == 64 && HD == 64) ? 4 : ((BS == 64) ? 2 : 3);   // K/V stages
-  static constexpr int kStageOff = kQBufs * kQBytes;
-  static constexpr int kRowBitsOff = kStageOff + NS * kStageBytes;
+  static constexpr int NK = (BS == 64 && HD == 64) ? 4 : ((BS == 64) ? 2 : 3);   // K stages
+  static constexpr int NV = NK;                                                  // V stages
+  static constexpr int kKRingOff = kQBufs * kQBytes;
+  static constexpr int kVRingOff = kKRingOff + NK * kKBytes;
+  static constexpr int kRowBitsOff = kVRingOff + NV * kKBytes;
   static constexpr int kRowBitsBytes = kQUnionWords * kQRows * 4;
   static constexpr int kTileBitsOff = kRowBitsOff + kRowBitsBytes;
   static constexpr int kTileBitsBytes = 2 * kQMaxNbWords * 4;   // bits, then prefix counts
   static constexpr int kBarOff = kTileBitsOff + kTileBitsBytes;
-  static constexpr int kSmem = kBarOff + 256 + 1024 /*alignment*/;
+  static constexpr int kSmem = kBarOff + 512 + 1024 /*alignment*/;
   // TMEM: S[kSBufs] (BS columns each), P[2] (bf16 pairs, BS / 2 each), O (HD).
   static constexpr int kSCol = 0, kPCol = kSBufs * BS, kOCol = kSBufs * BS + BS;
   static constexpr int kCols = kSBufs * BS + BS + HD;
   static constexpr int kTmemCols = kCols <= 256 ? 256 : 512;
   static_assert(kCols <= 512, "TMEM");
-  static_assert(kStageOff % 1024 == 0 && kStageBytes % 1024 == 0, "swizzled tiles");
+  static_assert(kKRingOff % 1024 == 0 && kKBytes % 1024 == 0, "swizzled tiles");
   static_assert(kSmem <= 227 * 1024, "shared memory");
   static_assert(kCtasPerSm * (kSmem + 1024) <= 228 * 1024, "CTAs per SM");
   static_assert(kCtasPerSm * kTmemCols <= 512, "TMEM per SM");
@@ -233,12 +236,12 @@ __global__ void __launch_bounds__(kQThreads, QCfg<BS, HD>::kCtasPerSm)
 fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
               const __grid_constant__ CUtensorMap tmap_v, FineQParams prm) {
   using C = QCfg<BS, HD>;
-  constexpr int NS = C::NS;
+  constexpr int NK = C::NK, NV = C::NV;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   auto q_s = [&](int b) { return smem + b * C::kQBytes; };
-  auto k_s = [&](int st) { return smem + C::kStageOff + st * C::kStageBytes; };
-  auto v_s = [&](int st) { return k_s(st) + C::kKBytes; };
+  auto k_s = [&](int st) { return smem + C::kKRingOff + st * C::kKBytes; };
+  auto v_s = [&](int st) { return smem + C::kVRingOff + st * C::kKBytes; };
   uint32_t* rowbits = reinterpret_cast<uint32_t*>(smem + C::kRowBitsOff);   // [word][row]
   uint32_t* tb = reinterpret_cast<uint32_t*>(smem + C::kTileBitsOff);       // union bitmask
   uint32_t* tpre = tb + kQMaxNbWords;                                        // its prefix counts
@@ -252,12 +255,14 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
   uint64_t* o_full = bars + 12;
   uint64_t* o_empty = bars + 13;
   uint64_t* drain = bars + 14;
-  uint64_t* kv_full = bars + 15;          // [NS]
-  uint64_t* kv_empty = bars + 15 + NS;    // [NS]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15 + 2 * NS);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 16 + 2 * NS);
-  uint64_t* gate = bars + 17 + 2 * NS;    // test hook: nothing completes it
-  static_assert((18 + 2 * NS) * 8 <= 256, "barrier area");
+  uint64_t* k_full = bars + 15;                    // [NK]
+  uint64_t* k_empty = k_full + NK;                 // [NK]
+  uint64_t* v_full = k_empty + NK;                 // [NV]
+  uint64_t* v_empty = v_full + NV;                 // [NV]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(v_empty + NV);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(v_empty + NV + 1);
+  uint64_t* gate = v_empty + NV + 2;               // test hook: nothing completes it
+  static_assert((18 + 2 * NK + 2 * NV) * 8 <= 512, "barrier area");
 
   const Shape s = prm.s;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -280,9 +285,13 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
     mbar_init(o_empty, kQRows);
     mbar_init(drain, 1);
     mbar_init(gate, 1);
-    for (int st = 0; st < NS; ++st) {
-      mbar_init(&kv_full[st], 1);
-      mbar_init(&kv_empty[st], 1);
+    for (int st = 0; st < NK; ++st) {
+      mbar_init(&k_full[st], 1);
+      mbar_init(&k_empty[st], 1);
+    }
+    for (int st = 0; st < NV; ++st) {
+      mbar_init(&v_full[st], 1);
+      mbar_init(&v_empty[st], 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -317,26 +326,36 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
       }
     }
   } else if (warp == 4) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      int g = 0, qn = 0;   // K/V loads and Q loads issued
+    // ------------------------------------------------------------ TMA producers
+    // Lane 0: Q of every tile, K of every union block, and the L2 prefetch
+    // of the K/V blocks kQPrefetch ahead.  Lane 1: V of every union block.
+    // Each walks the same tiles and union bitmasks in the same order.
+    if (lane < 2) {
+      const bool kq = lane == 0;
+      const int NR = kq ? NK : NV;                 // this lane's ring
+      uint64_t* full = kq ? k_full : v_full;
+      uint64_t* empty = kq ? k_empty : v_empty;
+      const CUtensorMap* tm = kq ? &tmap_k : &tmap_v;
+      int g = 0, qn = 0;   // ring loads and Q loads issued
       bool ok = true;
       for (int n = 0; ok && n < my_tiles; ++n) {
         const int4 info = __ldg(prm.qt_info + slot_of(n));
         const int unit = info.x, tile = info.y;
-        const int qb = n % C::kQBufs;
-        if (n >= C::kQBufs)
-          ok = mbar_wait(&q_empty[qb], ((n - C::kQBufs) / C::kQBufs) & 1, prm.err, kErrQWaitQ);
-        if (!ok || *abort_flag) { ok = false; break; }
-        mbar_arrive_expect_tx(&q_full[qb], C::kQBytes);
-        ++qn;
+        if (kq) {
+          const int qb = n % C::kQBufs;
+          if (n >= C::kQBufs)
+            ok = mbar_wait(&q_empty[qb], ((n - C::kQBufs) / C::kQBufs) & 1, prm.err, kErrQWaitQ);
+          if (!ok || *abort_flag) { ok = false; break; }
+          mbar_arrive_expect_tx(&q_full[qb], C::kQBytes);
+          ++qn;
 #pragma unroll
-        for (int p = 0; p < HD / 64; ++p)
-          tma_load_2d(q_s(qb) + p * (kQRows * 128), &tmap_q, &q_full[qb], p * 64,
-                      unit * s.N + tile * kQRows);
+          for (int p = 0; p < HD / 64; ++p)
+            tma_load_2d(q_s(qb) + p * (kQRows * 128), &tmap_q, &q_full[qb], p * 64,
+                        unit * s.N + tile * kQRows);
+        }
         const uint32_t* bw = prm.qt_bits + (int64_t)slot_of(n) * nbw;
         // The K/V blocks kQPrefetch ahead of the loads go to L2 first, so a
-        // stage's TMA load (which waits for the PV two blocks back) finds
+        // stage's TMA load (which waits for the MMA that frees it) finds
         // them there.
         int pw = 0;
         uint32_t pm = __ldg(bw);
@@ -349,23 +368,23 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
           bulk_prefetch_l2(prm.K + off, (uint32_t)C::kKBytes);
           bulk_prefetch_l2(prm.V + off, (uint32_t)C::kKBytes);
         };
-        for (int q = 0; q < kQPrefetch; ++q) prefetch_next();
+        if (kq)
+          for (int q = 0; q < kQPrefetch; ++q) prefetch_next();
         for (int w = 0; ok && w < nbw; ++w) {
           uint32_t m = __ldg(bw + w);
           while (m != 0u) {
             const int j = w * 32 + __ffs(m) - 1;
             m &= m - 1u;
-            const int st = g % NS;
-            if (g >= NS) ok = mbar_wait(&kv_empty[st], ((g - NS) / NS) & 1, prm.err, kErrQWaitKV);
+            const int st = g % NR;
+            if (g >= NR) ok = mbar_wait(&empty[st], ((g - NR) / NR) & 1, prm.err, kErrQWaitKV);
             if (!ok || *abort_flag) { ok = false; break; }
-            mbar_arrive_expect_tx(&kv_full[st], C::kStageBytes);
+            mbar_arrive_expect_tx(&full[st], C::kKBytes);
+            unsigned char* dst = kq ? k_s(st) : v_s(st);
             const int y = unit * s.N + j * BS;
 #pragma unroll
-            for (int p = 0; p < HD / 64; ++p) {
-              tma_load_2d(k_s(st) + p * (BS * 128), &tmap_k, &kv_full[st], p * 64, y);
-              tma_load_2d(v_s(st) + p * (BS * 128), &tmap_v, &kv_full[st], p * 64, y);
-            }
-            prefetch_next();
+            for (int p = 0; p < HD / 64; ++p)
+              tma_load_2d(dst + p * (BS * 128), tm, &full[st], p * 64, y);
+            if (kq) prefetch_next();
             ++g;
           }
         }
@@ -373,15 +392,18 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
       if (!ok) {
         *abort_flag = 1;
         // Copies still in flight land before the CTA leaves: wait for the
-        // last load of every stage and Q buffer (bounded; those phases are
-        // the barriers' latest, so their parity is unambiguous).
-        for (int st = 0; st < NS; ++st) {
-          const int last = g - 1 - ((g - 1 - st) % NS + NS) % NS;
-          if (last >= 0) mbar_wait(&kv_full[st], (last / NS) & 1, prm.err, kErrQWaitKV);
+        // last load of every stage of this lane's ring (and Q buffer),
+        // bounded; those phases are the barriers' latest, so their parity is
+        // unambiguous.
+        for (int st = 0; st < NR; ++st) {
+          const int last = g - 1 - ((g - 1 - st) % NR + NR) % NR;
+          if (last >= 0) mbar_wait(&full[st], (last / NR) & 1, prm.err, kErrQWaitKV);
         }
-        for (int qb = 0; qb < C::kQBufs; ++qb) {
-          const int last = qn - 1 - ((qn - 1 - qb) % C::kQBufs + C::kQBufs) % C::kQBufs;
-          if (last >= 0) mbar_wait(&q_full[qb], (last / C::kQBufs) & 1, prm.err, kErrQWaitQ);
+        if (kq) {
+          for (int qb = 0; qb < C::kQBufs; ++qb) {
+            const int last = qn - 1 - ((qn - 1 - qb) % C::kQBufs + C::kQBufs) % C::kQBufs;
+            if (last >= 0) mbar_wait(&q_full[qb], (last / C::kQBufs) & 1, prm.err, kErrQWaitQ);
+          }
         }
       }
     }
@@ -397,18 +419,19 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
       // O += P(gp) V(gp); `first`: the tile's first PV, which overwrites O
       // once the previous tile's epilogue has read it.
       auto pv = [&](int gp, int n, bool first) -> bool {
-        const int bp = gp & 1, stp = gp % NS;
+        const int bp = gp & 1, stp = gp % NV;
         if (!mbar_wait(&p_full[bp], (gp >> 1) & 1, prm.err, kErrQWaitP)) return false;
+        if (!mbar_wait(&v_full[stp], (gp / NV) & 1, prm.err, kErrQWaitKV)) return false;
         if (first && n >= 1 && !mbar_wait(o_empty, (n - 1) & 1, prm.err, kErrQWaitO)) return false;
         if (*abort_flag) return false;
         tc_fence_after();
-        const uint64_t dv = dv0 + ((uint64_t)(stp * C::kStageBytes) >> 4);
+        const uint64_t dv = dv0 + ((uint64_t)(stp * C::kKBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < BS / 16; ++kk)
           mma_bf16_ts(tbase + C::kOCol, tbase + C::kPCol + bp * (BS / 2) + kk * 8,
                       dv + ((kk * 16 * 128) >> 4), idesc_o, (!first || kk > 0) ? 1u : 0u);
         mma_commit(&p_free[bp]);
-        mma_commit(&kv_empty[stp]);
+        mma_commit(&v_empty[stp]);
         return true;
       };
       int g = 0;
@@ -419,13 +442,13 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
         ok = mbar_wait(&q_full[qb], (n / C::kQBufs) & 1, prm.err, kErrQWaitQ);
         const uint64_t dq = dq0 + ((uint64_t)(qb * C::kQBytes) >> 4);
         for (int i = 0; ok && i < U; ++i, ++g) {
-          const int st = g % NS, sb = g % C::kSBufs;
-          ok = mbar_wait(&kv_full[st], (g / NS) & 1, prm.err, kErrQWaitKV);
+          const int st = g % NK, sb = g % C::kSBufs;
+          ok = mbar_wait(&k_full[st], (g / NK) & 1, prm.err, kErrQWaitKV);
           if (ok && g >= C::kSBufs)
             ok = mbar_wait(&s_free[sb], ((g - C::kSBufs) / C::kSBufs) & 1, prm.err, kErrQWaitS);
           if (!ok || *abort_flag) { ok = false; break; }
           tc_fence_after();
-          const uint64_t dk = dk0 + ((uint64_t)(st * C::kStageBytes) >> 4);
+          const uint64_t dk = dk0 + ((uint64_t)(st * C::kKBytes) >> 4);
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
             const uint32_t off = (kk >> 2) * (kQRows * 128) + (kk & 3) * 32;
@@ -434,6 +457,7 @@ fine_q_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant_
                      kk > 0 ? 1u : 0u);
           }
           mma_commit(&s_full[sb]);
+          mma_commit(&k_empty[st]);                 // K_j's stage, once S(j) is done
           if (i == U - 1) mma_commit(&q_empty[qb]);
           if (i >= 1) ok = pv(g - 1, n, i == 1);
         }
