@@ -93,21 +93,47 @@ def _raise_on_kernel_error(L, p, ws, from_forward):
 # ``attention`` copies it into pinned host memory behind the forward (with an
 # event), and the next call on the device -- or ``raise_deferred_errors`` --
 # raises for any earlier call whose word has landed with bits set.
-_PENDING = {}          # device index -> [(event, pinned int32 tensor)]
-_MAX_PENDING = 64
+class _ErrorRing:
+    """Per device: the error words of recent calls, copied behind each call's
+    forward into a ring of pinned slots.  A slot holds -1 (a value no error
+    word takes) until its copy lands, so the host reads it without any CUDA
+    call; a call costs one 4-byte copy."""
+
+    SLOTS = 64
+    PENDING = -1
+
+    def __init__(self, device):
+        self.device = device
+        self.words = torch.full((self.SLOTS,), self.PENDING, dtype=torch.int32, pin_memory=True)
+        self.live = [False] * self.SLOTS      # a copy was issued into the slot
+        self.next = 0
+
+    def settle(self, slot, wait):
+        """The slot's word once its copy has landed (waiting for it if asked), else None."""
+        if not self.live[slot]:
+            return 0
+        v = int(self.words[slot].item())
+        if v == self.PENDING:
+            if not wait:
+                return None
+            torch.cuda.synchronize(self.device)
+            v = int(self.words[slot].item())
+        self.live[slot] = False
+        return v & 0xFFFFFFFF
 
 
-def _take_landed(device, wait):
-    lst = _PENDING.get(device.index, [])
-    keep, bits = [], 0
-    for ev, host in lst:
-        if wait:
-            ev.synchronize()
-        if ev.query():
-            bits |= int(host.item()) & 0xFFFFFFFF
-        else:
-            keep.append((ev, host))
-    _PENDING[device.index] = keep
+_RINGS = {}
+_ERR_OFFSETS = {}      # (problem fields, workspace bytes) -> error word offset, or None
+
+
+def _ring(device):
+    r = _RINGS.get(device.index)
+    if r is None:
+        r = _RINGS[device.index] = _ErrorRing(device)
+    return r
+
+
+def _raise_bits(bits):
     if bits:
         raise RuntimeError(f"{VARIANT}: an earlier call's fine-stage pipeline stopped early "
                            f"(error bits 0x{bits:x}); that call's output is NaN")
@@ -117,23 +143,40 @@ def raise_deferred_errors(device=None):
     """Wait for the error words of this device's earlier ``attention`` calls
     and raise ``RuntimeError`` if any of them reports a timed-out wait."""
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-    _take_landed(dev, wait=True)
+    r = _ring(dev)
+    bits = 0
+    for slot in range(r.SLOTS):
+        bits |= r.settle(slot, wait=True) or 0
+    _raise_bits(bits)
+
+
+def _error_offset(L, p, ws_bytes):
+    key = (p.batch, p.heads, p.seq_len, p.head_dim, p.block_size, p.top_k, p.causal, p.flags,
+           ws_bytes)
+    if key not in _ERR_OFFSETS:
+        off = ctypes.c_size_t(0)
+        ok = L.bsa_workspace_error_offset(ctypes.byref(p), ctypes.c_size_t(ws_bytes), 1,
+                                          ctypes.byref(off)) == _lib.BSA_OK
+        _ERR_OFFSETS[key] = off.value if ok else None   # None: the CUDA-core fine stage
+    return _ERR_OFFSETS[key]
 
 
 def _defer_error_check(L, p, ws, device):
-    off = ctypes.c_size_t(0)
-    if L.bsa_workspace_error_offset(ctypes.byref(p), ctypes.c_size_t(ws.numel()), 1,
-                                    ctypes.byref(off)) != _lib.BSA_OK:
+    """Copy this call's error word behind its forward; report the previous
+    call's word if it has landed (a slot still in flight is settled when the
+    ring comes back to it, or by raise_deferred_errors)."""
+    off = _error_offset(L, p, ws.numel())
+    if off is None:
         return                       # the CUDA-core fine stage keeps no error word
-    host = torch.empty(1, dtype=torch.int32, pin_memory=True)
-    host.copy_(ws[off.value:off.value + 4].view(torch.int32), non_blocking=True)
-    ev = torch.cuda.Event()
-    ev.record(torch.cuda.current_stream(device))
-    lst = _PENDING.setdefault(device.index, [])
-    lst.append((ev, host))
-    if len(lst) > _MAX_PENDING:      # bound the list: settle the oldest
-        lst[0][0].synchronize()
-        _take_landed(device, wait=False)
+    r = _ring(device)
+    slot = r.next
+    r.next = (slot + 1) % r.SLOTS
+    bits = r.settle((slot - 1) % r.SLOTS, wait=False) or 0
+    bits |= r.settle(slot, wait=True) or 0          # the slot is about to be reused
+    r.words[slot] = r.PENDING
+    r.words[slot:slot + 1].copy_(ws[off:off + 4].view(torch.int32), non_blocking=True)
+    r.live[slot] = True
+    _raise_bits(bits)
 
 
 def attention(Q, K, V, causal=False, block_size=64, top_k=16, *, flags=0,
@@ -162,8 +205,6 @@ def attention(Q, K, V, causal=False, block_size=64, top_k=16, *, flags=0,
     Qc, Kc, Vc = Q.contiguous(), K.contiguous(), V.contiguous()
     p = problem(B, H, N, D, causal, block_size, top_k, flags)
     with torch.cuda.device(Q.device):
-        if check_errors is None:
-            _take_landed(Q.device, wait=False)
         O = torch.empty_like(Qc)
         nbytes = workspace_bytes(p, workspace_cap)
         ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=Q.device)

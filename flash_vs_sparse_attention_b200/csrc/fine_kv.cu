@@ -1346,14 +1346,16 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
   cudaError_t e = cudaSuccess;
   if (!pre_zeroed && (e = cudaMemsetAsync(w.err, 0, w.zero_bytes, st)) != cudaSuccess) return e;
   // Per-tile dispatch: query tiles (few distinct blocks between their rows)
-  // go to the query-stationary kernel, the rest through the buckets.
-  const int max_union = fine_q_supported(s) ? fine_q_max_union(s, flags) : 0;
-  // Unless forced, the query-stationary kernel takes the query tiles only
-  // when they are at least half of all tiles: a few long query tiles (early
+  // go to the query-stationary kernel, the rest through the buckets.  Unless
+  // forced, the query-stationary kernel takes the query tiles only when there
+  // are enough of them (fine_q_min_tiles): a few long query tiles (early
   // causal tiles see few blocks) would run after the key-stationary kernel
-  // and lengthen the stage instead of shortening it.
-  const int tiles_total = s.units * fine_q_tiles(s);
-  const int min_q = (flags & BSA_FLAG_FINE_QUERY_STATIONARY) ? 1 : (tiles_total + 1) / 2;
+  // and lengthen the stage instead of shortening it.  A problem with fewer
+  // tiles in all than that minimum skips the classifier and the query kernel.
+  const int min_q = fine_q_min_tiles(s, flags);
+  const bool q_possible =
+      fine_q_supported(s) && (int64_t)s.units * fine_q_tiles(s) >= (int64_t)min_q;
+  const int max_union = q_possible ? fine_q_max_union(s, flags) : 0;
   const QTiles tm{max_union > 0 ? w.tile_mode : nullptr, w.ctr + 2, min_q};
   if (max_union > 0 &&
       (e = launch_classify_tiles(idx, w.tile_mode, w.qt_bits, w.qt_info, w.ctr + 2, s, max_union,

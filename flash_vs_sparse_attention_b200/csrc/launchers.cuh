@@ -42,6 +42,7 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
 bool fine_q_supported(const Shape& s);
 int fine_q_max_union(const Shape& s, uint32_t flags);
 int fine_q_tiles(const Shape& s);
+int fine_q_min_tiles(const Shape& s, uint32_t flags);
 cudaError_t launch_classify_tiles(const int32_t* idx, uint8_t* tile_mode, uint32_t* qt_bits,
                                   int4* qt_info, uint32_t* n_qt, const Shape& s, int max_union,
                                   cudaStream_t st);

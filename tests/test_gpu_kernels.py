@@ -102,13 +102,14 @@ def recent_blocks_selection(N, bs, k, causal, rows):
     return out
 
 
-@pytest.mark.parametrize("shape", [(1, 2, 4096, 64, 64, 16, True), (1, 1, 4096, 128, 64, 32, False),
-                                   (1, 1, 8192, 64, 128, 16, True)])
+@pytest.mark.parametrize("shape", [(1, 24, 8192, 64, 64, 16, True), (1, 24, 8192, 128, 64, 32, False),
+                                   (1, 24, 8192, 64, 128, 16, True)])
 def test_fine_stage_mixed_tile_dispatch(cuda, shape):
     """Even 128-row tiles get a selection with a small union (query-stationary
     kernel), odd tiles the GPU's own selection (key-block-stationary): the
-    default dispatch mixes both in one call and matches the oracle, and the
-    forced key-stationary path agrees with it."""
+    default dispatch mixes both in one call and matches the oracle (checked
+    on two units), and every tile the dispatch leaves to the key-stationary
+    kernel equals the forced key-stationary run bit for bit."""
     B, H, N, D, bs, k, causal = shape
     Q, K, V = rand_inputs(B, H, N, D, seed=5)
     Qg, Kg, Vg = to_gpu(Q, K, V)
@@ -122,23 +123,27 @@ def test_fine_stage_mixed_tile_dispatch(cuda, shape):
     O = bi.fine(Qg, Kg, Vg, idx_g, causal=causal, block_size=bs).float().cpu().numpy()
     O_kv = bi.fine(Qg, Kg, Vg, idx_g, causal=causal, block_size=bs,
                    flags=KEY_ONLY).float().cpu().numpy()
-    for b in range(B):
-        for h in range(H):
-            want = oracle_fine(Q[b, h], K[b, h], V[b, h], idx[b, h], rows, bs, causal)
-            assert_close_out(O[b, h], want, f"unit ({b},{h}) mixed")
-            assert_close_out(O_kv[b, h], want, f"unit ({b},{h}) key-stationary")
+    for h in range(2):
+        want = oracle_fine(Q[0, h], K[0, h], V[0, h], idx[0, h], rows, bs, causal)
+        assert_close_out(O[0, h], want, f"unit (0,{h}) mixed")
+        assert_close_out(O_kv[0, h], want, f"unit (0,{h}) key-stationary")
     # Which tiles the dispatch should send where: a tile's union of selected
-    # blocks at most 3 top_k -> query-stationary.  The two kernels round
-    # differently (one bf16 rounding against fp16 partials merged), so the
-    # bits show which kernel ran: key-stationary tiles equal the forced run.
-    n_q = 0
+    # blocks at most 3 top_k -> query-stationary, when such tiles are at least
+    # half of all tiles and twice the query kernel's resident CTAs.  The two
+    # kernels round differently (one bf16 rounding against fp16 partials
+    # merged), so the bits show which kernel ran.
+    n_q, q_tiles = 0, []
     for b in range(B):
         for h in range(H):
             for t0 in range(0, N, 128):
                 sel = idx[b, h, t0:t0 + 128]
-                q_tile = len(np.unique(sel[sel >= 0])) <= 3 * k
-                n_q += q_tile
-                if not q_tile:
-                    assert np.array_equal(O[b, h, t0:t0 + 128], O_kv[b, h, t0:t0 + 128])
-    assert n_q >= (N // 256) * B * H        # at least the even tiles
+                q = len(np.unique(sel[sel >= 0])) <= 3 * k
+                n_q += q
+                q_tiles.append((b, h, t0, q))
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    tiles = B * H * (N // 128)
+    assert n_q >= max((tiles + 1) // 2, 2 * sms * (2 if bs == 64 else 1)), "shape too small"
+    for b, h, t0, q in q_tiles:
+        if not q:
+            assert np.array_equal(O[b, h, t0:t0 + 128], O_kv[b, h, t0:t0 + 128])
     assert not np.array_equal(O, O_kv), "query tiles not dispatched"

@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 import torch
 
-from flash_vs_sparse_attention_b200 import block_indexer_b200 as bi, flops
+from flash_vs_sparse_attention_b200 import _lib, block_indexer_b200 as bi, flops
 from oracle import attention_unit, qblock_attention_unit, qblock_scores, round_to_bf16
 from parity import assert_close_out, to_gpu
 
@@ -49,17 +49,20 @@ def test_flop_model_of_the_variant():
 
 # ---------------------------------------------------------------- GPU
 @pytest.mark.gpu
+@pytest.mark.parametrize("fine_flags", [0, _lib.BSA_FLAG_FINE_QUERY_STATIONARY])
 @pytest.mark.parametrize("shape", [
     (1, 2, 4096, 64, 64, 16, True),      # tensor-core fine stage
     (1, 2, 2048, 64, 64, 8, False),
     (1, 2, 4096, 128, 64, 16, True),     # head_dim 128
     (1, 2, 1024, 32, 16, 4, True),       # CUDA-core fine stage
 ])
-def test_qblock_matches_its_restatement(cuda, shape):
+def test_qblock_matches_its_restatement(cuda, shape, fine_flags):
+    """Both fine kernels (the query-stationary one forced, and the default
+    dispatch, which sends these small problems to the key-stationary one)."""
     B, H, N, D, bs, k, causal = shape
     Qn, Kn, Vn = (_rand((B, H, N, D), s) for s in (7, 8, 9))
     Q, K, V = to_gpu(Qn, Kn, Vn)
-    got = bi.attention_qblock(Q, K, V, causal=causal, block_size=bs, top_k=k,
+    got = bi.attention_qblock(Q, K, V, causal=causal, block_size=bs, top_k=k, flags=fine_flags,
                               check_errors=True).float().cpu().numpy()
     for u in range(H):
         s = qblock_scores(Qn[0, u], Kn[0, u], bs, causal)
