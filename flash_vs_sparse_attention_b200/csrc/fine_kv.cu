@@ -934,27 +934,26 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
     // chunk c at the 128-byte swizzled place the TMA store expects), (m, l)
     // per row, and the warp's own TMA store of its rows.  Each warp only
     // waits for its own previous store to have read its rows.
-    auto epilogue = [&](int tp, int np, float mp, float lp, int e2) {
+    auto epilogue_begin = [&](int np) {   // the staging tile is free again
       if (np >= 1 && lane == 0) bulk_wait_group_read0();
       __syncwarp();
-      const float f2 = exp2i(e2);
+    };
+    // 64 columns of O, in registers, into the staging tile as fp16.
+    auto stage_cols = [&](int c0, float (&ov)[64], int e2, float f2) {
+      if (e2 != 0) {
 #pragma unroll
-      for (int c0 = 0; c0 < HD; c0 += 64) {
-        float ov[64];
-        tmem_ld64(o_addr + c0, ov);
-        if (e2 != 0) {
-#pragma unroll
-          for (int c = 0; c < 64; ++c) ov[c] *= f2;
-        }
-#pragma unroll
-        for (int c = 0; c < 64; c += 8) {
-          const int ch = c >> 3;
-          *reinterpret_cast<uint4*>(out + (c0 >> 6) * (kTileRows * 128) + r * 128 +
-                                    ((ch ^ (r & 7)) << 4)) =
-              make_uint4(pack_f16x2(ov[c], ov[c + 1]), pack_f16x2(ov[c + 2], ov[c + 3]),
-                         pack_f16x2(ov[c + 4], ov[c + 5]), pack_f16x2(ov[c + 6], ov[c + 7]));
-        }
+        for (int c = 0; c < 64; ++c) ov[c] *= f2;
       }
+#pragma unroll
+      for (int c = 0; c < 64; c += 8) {
+        const int ch = c >> 3;
+        *reinterpret_cast<uint4*>(out + (c0 >> 6) * (kTileRows * 128) + r * 128 +
+                                  ((ch ^ (r & 7)) << 4)) =
+            make_uint4(pack_f16x2(ov[c], ov[c + 1]), pack_f16x2(ov[c + 2], ov[c + 3]),
+                       pack_f16x2(ov[c + 4], ov[c + 5]), pack_f16x2(ov[c + 6], ov[c + 7]));
+      }
+    };
+    auto epilogue_end = [&](int tp, float mp, float lp, float f2) {
       // Work item gi owns partial rows [128 gi, 128 gi + 128); rows past the
       // item's count hold values that are never read.
       const int gi = (int)t_begin + tp;
@@ -968,6 +967,24 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
                             gi * kTileRows + quad * 32, pol_o);
         bulk_commit_group();
       }
+    };
+    // With `hand_off`: once O is read out of TMEM (the first 64 columns at
+    // head_dim 64, all of it at 128), P(t) of the current item is handed to
+    // the PV issuer before the staging.
+    auto epilogue = [&](int tp, int np, float mp, float lp, int e2, bool hand_off) {
+      const float f2 = exp2i(e2);
+#pragma unroll
+      for (int c0 = 0; c0 < HD; c0 += 64) {
+        float ov[64];
+        tmem_ld64(o_addr + c0, ov);
+        if (hand_off && c0 + 64 == HD) {
+          tc_fence_before();   // P(t) stored, O(t - NWG) read out
+          mbar_arrive(&p_full[wg]);
+        }
+        if (c0 == 0) epilogue_begin(np);
+        stage_cols(c0, ov, e2, f2);
+      }
+      epilogue_end(tp, mp, lp, f2);
     };
     // O(t) complete means every MMA this group issued before it (S(t),
     // PV(t) and all earlier items') is done reading its K/V slot.
@@ -1083,9 +1100,15 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
         if (!ok) { *abort_flag = 1; break; }
         issued_next = try_issue_s(t + NWG);
       }
-      if (n >= 1) epilogue(tp, n - 1, mp, lp, ep);
-      tc_fence_before();   // P(t) stored, O(t - NWG) read out
-      mbar_arrive(&p_full[wg]);
+      // The previous item's O comes out of TMEM into registers before P(t)
+      // is handed to the PV issuer; the staging and store follow the
+      // handoff, so PV(t) need not wait for the whole epilogue.
+      if (n >= 1) {
+        epilogue(tp, n - 1, mp, lp, ep, true);
+      } else {
+        tc_fence_before();   // P(t) stored
+        mbar_arrive(&p_full[wg]);
+      }
       if (issuer) {
         ok = mbar_wait(&p_full[wg], n & 1, prm.err, kErrWaitP);
         ok = __all_sync(0xffffffffu, ok);
@@ -1125,7 +1148,7 @@ fine_kv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant
       if (ok) {
         tc_fence_after();
         if (storer) publish_o_done(tp);
-        epilogue(tp, n - 1, mp, lp, ep);
+        epilogue(tp, n - 1, mp, lp, ep, false);
       }
       if (!ok) *abort_flag = 1;
     }
