@@ -62,6 +62,8 @@ SIGNATURES = {
                                   _c.POINTER(_P), _c.c_int, _c.POINTER(_c.c_int)]),
     "bsa_pool_k": (_c.c_int, [_PP, _P, _P, _P, _P]),
     "bsa_select_blocks": (_c.c_int, [_PP, _P, _P, _P, _P, _P]),
+    "bsa_forward_heads": (_c.c_int, [_PP, _P, _P, _P, _P, _P, _P, _c.c_size_t, _P]),
+    "bsa_select_blocks_heads": (_c.c_int, [_PP, _P, _P, _P, _P, _P, _P]),
     "bsa_fine": (_c.c_int, [_PP, _P, _P, _P, _P, _P, _P, _c.c_size_t, _P]),
     "bsa_fine_workspace_bytes": (_c.c_size_t, [_PP]),
     "bsa_workspace_error": (_c.c_int, [_PP, _P, _c.c_size_t, _c.c_int, _c.POINTER(_c.c_uint32)]),

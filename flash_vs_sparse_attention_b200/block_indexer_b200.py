@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import ctypes
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -179,6 +180,25 @@ def _defer_error_check(L, p, ws, device):
     _raise_bits(bits)
 
 
+def _head_budgets(top_k, H, num_blocks, device):
+    """top_k as given to ``attention`` / ``select_blocks``: an int (every head
+    keeps that many blocks) or a sequence of H per-head budgets.  Returns the
+    slot count per row and the budgets as a device int32 tensor (None for an
+    int)."""
+    if isinstance(top_k, (int, np.integer)):
+        k = int(top_k)
+        assert k <= num_blocks, f"top_k {k} exceeds num_blocks {num_blocks}"
+        return k, None
+    ks = [int(x) for x in (top_k.tolist() if hasattr(top_k, "tolist") else top_k)]
+    if len(ks) != H:
+        raise ValueError(f"{VARIANT}: per-head top_k needs {H} values (got {len(ks)})")
+    if min(ks) < 1:
+        raise ValueError(f"{VARIANT}: per-head top_k values must be >= 1 (got {min(ks)})")
+    k = max(ks)
+    assert k <= num_blocks, f"top_k {k} exceeds num_blocks {num_blocks}"
+    return k, torch.tensor(ks, dtype=torch.int32, device=device)
+
+
 def attention(Q, K, V, causal=False, block_size=64, top_k=16, *, flags=0,
               workspace_cap=DEFAULT_WORKSPACE_CAP, check_errors=None):
     """
@@ -190,6 +210,10 @@ def attention(Q, K, V, causal=False, block_size=64, top_k=16, *, flags=0,
               top_k blocks per query token (ties to the lower block index).
       Fine:   exact softmax attention over the top_k * block_size keys kept.
 
+    top_k: an int, or a sequence of one budget per head (per-head sparsity,
+    the reference's stated next step, blog.md:135): head h keeps top_k[h]
+    blocks per row.
+
     check_errors: None (default) reports a timed-out pipeline wait without
     synchronising -- this call's error word is copied behind the forward and
     the next call (or ``raise_deferred_errors``) raises RuntimeError; True
@@ -200,16 +224,21 @@ def attention(Q, K, V, causal=False, block_size=64, top_k=16, *, flags=0,
     B, H, N, D = Q.shape
     assert N % block_size == 0, f"seq_len {N} must be divisible by block_size {block_size}"
     num_blocks = N // block_size
-    assert top_k <= num_blocks, f"top_k {top_k} exceeds num_blocks {num_blocks}"
     _check_inputs(Q, K, V)
+    slots, budgets = _head_budgets(top_k, H, num_blocks, Q.device)
     Qc, Kc, Vc = Q.contiguous(), K.contiguous(), V.contiguous()
-    p = problem(B, H, N, D, causal, block_size, top_k, flags)
+    p = problem(B, H, N, D, causal, block_size, slots, flags)
     with torch.cuda.device(Q.device):
         O = torch.empty_like(Qc)
         nbytes = workspace_bytes(p, workspace_cap)
         ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=Q.device)
-        st = L.bsa_forward(ctypes.byref(p), _ptr(Qc), _ptr(Kc), _ptr(Vc), _ptr(O), _ptr(ws),
-                           ctypes.c_size_t(ws.numel()), _stream(Q.device))
+        if budgets is None:
+            st = L.bsa_forward(ctypes.byref(p), _ptr(Qc), _ptr(Kc), _ptr(Vc), _ptr(O), _ptr(ws),
+                               ctypes.c_size_t(ws.numel()), _stream(Q.device))
+        else:
+            st = L.bsa_forward_heads(ctypes.byref(p), _ptr(budgets), _ptr(Qc), _ptr(Kc), _ptr(Vc),
+                                     _ptr(O), _ptr(ws), ctypes.c_size_t(ws.numel()),
+                                     _stream(Q.device))
         _lib.check(st, VARIANT)
         if check_errors:
             _raise_on_kernel_error(L, p, ws, True)
@@ -298,18 +327,25 @@ def pool_k(K, block_size=64):
 def select_blocks(Q, K, causal=False, block_size=64, top_k=16, *, flags=0):
     """Stages 1-3: the selected blocks of every query row, (B, H, N, top_k)
     int32 in ascending block order (ties in the coarse score go to the lower
-    block index), -1 in slots left empty (fewer than top_k eligible blocks)."""
+    block index), -1 in slots left empty (fewer than top_k eligible blocks).
+    top_k may be a sequence of per-head budgets (see ``attention``): the last
+    dimension is then their maximum and a head's slots past its budget hold -1."""
     L = _require_backend()
     B, H, N, D = Q.shape
     assert N % block_size == 0, f"seq_len {N} must be divisible by block_size {block_size}"
-    assert top_k <= N // block_size, f"top_k {top_k} exceeds num_blocks {N // block_size}"
+    slots, budgets = _head_budgets(top_k, H, N // block_size, Q.device)
     K_repr, K_split = pool_k(K, block_size)
     Qc = Q.contiguous()
-    p = problem(B, H, N, D, causal, block_size, top_k, flags)
+    p = problem(B, H, N, D, causal, block_size, slots, flags)
     with torch.cuda.device(Q.device):
-        idx = torch.empty(B, H, N, top_k, dtype=torch.int32, device=Q.device)
-        _lib.check(L.bsa_select_blocks(ctypes.byref(p), _ptr(Qc), _ptr(K_repr), _ptr(K_split),
-                                       _ptr(idx), _stream(Q.device)), VARIANT)
+        idx = torch.empty(B, H, N, slots, dtype=torch.int32, device=Q.device)
+        if budgets is None:
+            st = L.bsa_select_blocks(ctypes.byref(p), _ptr(Qc), _ptr(K_repr), _ptr(K_split),
+                                     _ptr(idx), _stream(Q.device))
+        else:
+            st = L.bsa_select_blocks_heads(ctypes.byref(p), _ptr(budgets), _ptr(Qc), _ptr(K_repr),
+                                           _ptr(K_split), _ptr(idx), _stream(Q.device))
+        _lib.check(st, VARIANT)
     return idx
 
 

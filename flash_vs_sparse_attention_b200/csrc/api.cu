@@ -66,6 +66,9 @@ static Shape make_shape(const bsa_problem* p, int units) {
   s.q0 = 0;
   s.kv = s.N;
   s.test_timeout = (p->flags & BSA_FLAG_TEST_TIMEOUT) ? 1 : 0;
+  s.head_k = nullptr;
+  s.heads = p->heads;
+  s.unit0 = 0;
   return s;
 }
 
@@ -204,12 +207,15 @@ size_t bsa_fine_workspace_bytes(const bsa_problem* p) {
   return fine_workspace_bytes(make_shape(p, (int)total_units(p)), p->flags);
 }
 
-int bsa_forward_ex(const bsa_problem* p, const void* Q, const void* K, const void* V, void* O,
-                   void* workspace, size_t workspace_bytes, void* stream, void* const* events,
-                   int n_events, int* n_launches) {
+// The forward over passes; head_k: per-head budgets (device) or null.
+static int forward_impl(const bsa_problem* p, const int32_t* head_k, const void* Q, const void* K,
+                        const void* V, void* O, void* workspace, size_t workspace_bytes,
+                        void* stream, void* const* events, int n_events, int* n_launches) {
   g_last_error.clear();
   int st = check(p);
   if (st != BSA_OK) return st;
+  if (head_k != nullptr && (p->flags & BSA_FLAG_QBLOCK))
+    return fail(BSA_ERR_UNSUPPORTED, "per-head top_k is not available with per-query-block selection");
   if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O) || !aligned16(workspace))
     return fail(BSA_ERR_ALIGNMENT, "Q, K, V, O and workspace must be 16-byte aligned");
   const int64_t U = total_units(p);
@@ -227,6 +233,8 @@ int bsa_forward_ex(const bsa_problem* p, const void* Q, const void* K, const voi
   for (int64_t u0 = 0; u0 < U; u0 += g) {
     const int units = (int)((U - u0) < g ? (U - u0) : g);
     Shape s = make_shape(p, units);
+    s.head_k = head_k;
+    s.unit0 = (int32_t)(u0 % p->heads);
     const __nv_bfloat16* q = (const __nv_bfloat16*)Q + u0 * elems;
     const __nv_bfloat16* k = (const __nv_bfloat16*)K + u0 * elems;
     const __nv_bfloat16* v = (const __nv_bfloat16*)V + u0 * elems;
@@ -281,9 +289,28 @@ int bsa_forward_ex(const bsa_problem* p, const void* Q, const void* K, const voi
   return BSA_OK;
 }
 
+int bsa_forward_ex(const bsa_problem* p, const void* Q, const void* K, const void* V, void* O,
+                   void* workspace, size_t workspace_bytes, void* stream, void* const* events,
+                   int n_events, int* n_launches) {
+  return forward_impl(p, nullptr, Q, K, V, O, workspace, workspace_bytes, stream, events,
+                      n_events, n_launches);
+}
+
 int bsa_forward(const bsa_problem* p, const void* Q, const void* K, const void* V, void* O,
                 void* workspace, size_t workspace_bytes, void* stream) {
-  return bsa_forward_ex(p, Q, K, V, O, workspace, workspace_bytes, stream, nullptr, 0, nullptr);
+  return forward_impl(p, nullptr, Q, K, V, O, workspace, workspace_bytes, stream, nullptr, 0,
+                      nullptr);
+}
+
+int bsa_forward_heads(const bsa_problem* p, const int32_t* head_top_k, const void* Q,
+                      const void* K, const void* V, void* O, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  if (head_top_k == nullptr) {
+    g_last_error.clear();
+    return fail(BSA_ERR_INVALID, "head_top_k is NULL");
+  }
+  return forward_impl(p, head_top_k, Q, K, V, O, workspace, workspace_bytes, stream, nullptr, 0,
+                      nullptr);
 }
 
 size_t bsa_host_workspace_bytes(const bsa_problem* p, int64_t units_per_chunk) {
@@ -471,8 +498,8 @@ int bsa_decode_step(const bsa_problem* p, const void* q_new, const void* k_new,
   return e == cudaSuccess ? BSA_OK : cuda_fail(e, "decode step launch");
 }
 
-int bsa_select_blocks(const bsa_problem* p, const void* Q, const float* K_repr,
-                      const void* K_split, int32_t* idx, void* stream) {
+static int select_impl(const bsa_problem* p, const int32_t* head_k, const void* Q,
+                       const float* K_repr, const void* K_split, int32_t* idx, void* stream) {
   g_last_error.clear();
   int st = check(p);
   if (st != BSA_OK) return st;
@@ -481,6 +508,7 @@ int bsa_select_blocks(const bsa_problem* p, const void* Q, const float* K_repr,
   if (p->flags & BSA_FLAG_QBLOCK)
     return fail(BSA_ERR_UNSUPPORTED, "per-query-block selection runs inside bsa_forward");
   Shape s = make_shape(p, (int)total_units(p));
+  s.head_k = head_k;
   const __nv_bfloat16* hi = (const __nv_bfloat16*)K_split;
   const __nv_bfloat16* lo = hi ? hi + (size_t)s.units * s.nb * s.D : nullptr;
   uint32_t flags = p->flags;
@@ -490,6 +518,21 @@ int bsa_select_blocks(const bsa_problem* p, const void* Q, const float* K_repr,
   cudaError_t e = launch_select((const __nv_bfloat16*)Q, K_repr, hi, lo, idx, nullptr, s, flags,
                                 (cudaStream_t)stream, &nl);
   return e == cudaSuccess ? BSA_OK : cuda_fail(e, "select launch");
+}
+
+int bsa_select_blocks(const bsa_problem* p, const void* Q, const float* K_repr,
+                      const void* K_split, int32_t* idx, void* stream) {
+  return select_impl(p, nullptr, Q, K_repr, K_split, idx, stream);
+}
+
+int bsa_select_blocks_heads(const bsa_problem* p, const int32_t* head_top_k, const void* Q,
+                            const float* K_repr, const void* K_split, int32_t* idx,
+                            void* stream) {
+  if (head_top_k == nullptr) {
+    g_last_error.clear();
+    return fail(BSA_ERR_INVALID, "head_top_k is NULL");
+  }
+  return select_impl(p, head_top_k, Q, K_repr, K_split, idx, stream);
 }
 
 int bsa_fine(const bsa_problem* p, const void* Q, const void* K, const void* V, const int32_t* idx,

@@ -106,6 +106,19 @@ struct Shape {
   int32_t q0;          // position of query row 0
   int32_t kv;          // keys [0, kv) exist
   int32_t test_timeout;  // BSA_FLAG_TEST_TIMEOUT: the fine kernel's test hook
+  // Per-head top_k (a per-head sparsity budget): device array of `heads`
+  // budgets, or null (every row keeps k blocks).  Unit u of a launch is
+  // head (unit0 + u) % heads; k is then the slot count of a row of idx.
+  const int32_t* head_k;
+  int32_t heads;
+  int32_t unit0;
 };
+
+// Blocks a row of unit u keeps: its head's budget clamped to [1, k], or k.
+__device__ __forceinline__ int unit_top_k(const Shape& s, int u) {
+  if (s.head_k == nullptr) return s.k;
+  const int kh = __ldg(s.head_k + (s.unit0 + u) % s.heads);
+  return kh < 1 ? 1 : (kh > s.k ? s.k : kh);
+}
 
 }  // namespace bsa

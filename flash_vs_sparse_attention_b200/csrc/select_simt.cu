@@ -40,7 +40,7 @@ select_simt_kernel(const __nv_bfloat16* __restrict__ Q, const float* __restrict_
   }
 
   RowTopK<KCAP> sel;
-  sel.init(bbuf + t, kSimtRows, cap, s.k);
+  sel.init(bbuf + t, kSimtRows, cap, unit_top_k(s, unit));   // this head's budget
 
   int last_row = min(row0 + kSimtRows, s.N) - 1;
   int nb_visit = s.causal ? min(s.nb, last_row / s.bs + 1) : s.nb;
@@ -73,7 +73,7 @@ select_simt_kernel(const __nv_bfloat16* __restrict__ Q, const float* __restrict_
       }
     }
   }
-  if (row < s.N) sel.emit(idx + ((int64_t)unit * s.N + row) * s.k);
+  if (row < s.N) sel.emit(idx + ((int64_t)unit * s.N + row) * s.k, s.k);
 }
 
 static size_t select_simt_smem(const Shape& s, int kcap) {

@@ -226,7 +226,8 @@ select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
       // block_indexer.py:46-50 keeps block j while j * bs <= row.
       const int lim = !valid ? 0 : (s.causal ? min(s.nb, row / s.bs + 1) : s.nb);
       RowTopK<KCAP> sel;
-      sel.init(cbuf + r, kSelRows, C::kCap, s.k);
+      const int ku = unit_top_k(s, unit);   // this head's budget (s.k unless per head)
+      sel.init(cbuf + r, kSelRows, C::kCap, ku);
       // Group maxima: 32 strided groups (column % 32) for top_k <= 16; for
       // larger top_k 64 groups (column % 64: the two halves gm / gm2, by the
       // parity of the 32-column chunk), whose k-th largest maximum is a much
@@ -298,12 +299,12 @@ select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
         // The floor: the k-th largest group maximum (-inf if fewer than k
         // groups are non-empty).
         if (pass == 0 && w == nw - 1) {
-          if constexpr (kG64) sel.raise_floor(kth_of_64(gm, gm2, s.k));
-          else if (s.k <= 32) sel.raise_floor(kth_of_32(gm, s.k));
+          if constexpr (kG64) sel.raise_floor(kth_of_64(gm, gm2, ku));
+          else if (ku <= 32) sel.raise_floor(kth_of_32(gm, ku));
         }
       }
       if (!ok) break;
-      if (valid) sel.emit(prm.idx + ((int64_t)unit * s.N + row) * s.k);
+      if (valid) sel.emit(prm.idx + ((int64_t)unit * s.N + row) * s.k, s.k);
     }
     if (!ok) *abort_flag = 1;
   }

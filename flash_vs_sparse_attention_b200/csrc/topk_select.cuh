@@ -157,16 +157,17 @@ struct RowTopK {
     update_thr();
   }
 
-  // Final top-k, written as k int32 in ascending block order, -1 padded
-  // (16-byte stores when k is a multiple of 4 and out is 16-byte aligned).
-  __device__ __forceinline__ void emit(int32_t* out) {
+  // Final top-k, written as `slots` (>= k) int32 in ascending block order,
+  // -1 padded (16-byte stores when slots is a multiple of 4 and out is
+  // 16-byte aligned).
+  __device__ __forceinline__ void emit(int32_t* out, int slots) {
     compact();
     auto at = [&](int e) { return e < cnt ? (int32_t)buf[e * stride].y : -1; };
-    if ((k & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
-      for (int e = 0; e < k; e += 4)
+    if ((slots & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+      for (int e = 0; e < slots; e += 4)
         *reinterpret_cast<int4*>(out + e) = make_int4(at(e), at(e + 1), at(e + 2), at(e + 3));
     } else {
-      for (int e = 0; e < k; ++e) out[e] = at(e);
+      for (int e = 0; e < slots; ++e) out[e] = at(e);
     }
   }
 };

@@ -40,6 +40,15 @@ def compute_flops(batch, heads, seq_len, head_dim, variant="dense", block_size=6
     raise ValueError(f"Unknown variant: {variant}")
 
 
+def compute_flops_per_head(batch, seq_len, head_dim, head_top_k, variant="block_indexer_b200",
+                           block_size=64):
+    """compute_flops with a per-head budget (the reference's stated next step,
+    blog.md:135): the sum over heads of the one-head count with that head's
+    top_k."""
+    return sum(compute_flops(batch, 1, seq_len, head_dim, variant, block_size, int(k))
+               for k in head_top_k)
+
+
 def compute_io_bytes(batch, heads, seq_len, head_dim, variant="naive", bytes_per_element=2,
                      block_size=64):
     B, H, N, D = batch, heads, seq_len, head_dim

@@ -111,6 +111,17 @@ int bsa_forward_ex(const bsa_problem* p, const void* Q, const void* K, const voi
                    void* O, void* workspace, size_t workspace_bytes, void* stream,
                    void* const* events, int n_events, int* n_launches);
 
+/* Per-head top_k, the reference's stated next step (a per-head sparsity
+ * budget, blog.md:135): head h of every batch keeps head_top_k[h] blocks per
+ * query row instead of p->top_k, which is then the slot count of each row of
+ * the selection (slots past a head's budget hold -1, as for a row with fewer
+ * eligible blocks).  head_top_k: DEVICE array of p->heads int32, each in
+ * [1, p->top_k] (values outside are clamped).  Everything else as
+ * bsa_forward; not with BSA_FLAG_QBLOCK (BSA_ERR_UNSUPPORTED). */
+int bsa_forward_heads(const bsa_problem* p, const int32_t* head_top_k, const void* Q,
+                      const void* K, const void* V, void* O, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
 /* Bytes of device workspace bsa_forward_host needs with `units_per_chunk`
  * (batch*head) units per chunk (<= 0: the default, a quarter of the units
  * rounded up): two device copies of one chunk's Q, K, V and O, and the
@@ -189,6 +200,12 @@ int bsa_decode_step(const bsa_problem* p, const void* q_new, const void* k_new,
  * with BSA_FLAG_SIMT_SELECT). */
 int bsa_select_blocks(const bsa_problem* p, const void* Q, const float* K_repr,
                       const void* K_split, int32_t* idx, void* stream);
+
+/* bsa_select_blocks with per-head budgets (see bsa_forward_heads): row r of
+ * head h lists its head_top_k[h] selected blocks, then -1 up to p->top_k. */
+int bsa_select_blocks_heads(const bsa_problem* p, const int32_t* head_top_k, const void* Q,
+                            const float* K_repr, const void* K_split, int32_t* idx,
+                            void* stream);
 
 /* Stage 4 alone (block_indexer_triton.py:132-145 and the Triton kernel
  * _fine_attn_fwd, :12-83): O from Q, K, V and a selection `idx` laid out as

@@ -159,9 +159,11 @@ def attention(Q, K, V, causal=False, block_size=64, top_k=16, threads=None):
     """The reference variant API on numpy arrays: (B, H, N, D) -> (B, H, N, D).
 
     Same contract as ``block_indexer.attention`` (block_indexer.py:4-86):
-    asserts ``N % block_size == 0`` and ``top_k <= num_blocks``.  Units run on
-    a thread pool (numpy releases the GIL in its kernels); ``threads=None``
-    uses every host core.
+    asserts ``N % block_size == 0`` and ``top_k <= num_blocks``.  ``top_k``
+    may also be a sequence of H per-head budgets (the per-head sparsity the
+    reference names as its next step, blog.md:135): head h then runs the same
+    algorithm with ``top_k[h]``.  Units run on a thread pool (numpy releases
+    the GIL in its kernels); ``threads=None`` uses every host core.
     """
     Q = np.asarray(Q, np.float32)
     K = np.asarray(K, np.float32)
@@ -169,7 +171,10 @@ def attention(Q, K, V, causal=False, block_size=64, top_k=16, threads=None):
     B, H, N, D = Q.shape
     assert N % block_size == 0, f"seq_len {N} must be divisible by block_size {block_size}"
     nb = N // block_size
-    assert top_k <= nb, f"top_k {top_k} exceeds num_blocks {nb}"
+    ks = [int(top_k)] * H if np.ndim(top_k) == 0 else [int(x) for x in top_k]
+    assert len(ks) == H, f"per-head top_k needs {H} values"
+    for k_h in ks:
+        assert 1 <= k_h <= nb, f"top_k {k_h} exceeds num_blocks {nb}"
     out = np.empty_like(Q)
     tasks = [(b, h, c0) for b in range(B) for h in range(H) for c0 in range(0, N, _CHUNK)]
     threads = threads or os.cpu_count() or 1
@@ -183,7 +188,7 @@ def attention(Q, K, V, causal=False, block_size=64, top_k=16, threads=None):
         b, h, c0 = task
         r = np.arange(c0, min(c0 + _CHUNK, N))
         s = coarse_scores(Q[b, h, r], pooled[b, h], scale, c0, block_size, causal)
-        idx = select_blocks(s, top_k)
+        idx = select_blocks(s, ks[h])
         out[b, h, r] = fine_stage(Q[b, h, r], K[b, h].reshape(nb, block_size, D),
                                   V[b, h].reshape(nb, block_size, D), idx, c0, causal, scale)
 
