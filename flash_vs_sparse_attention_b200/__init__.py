@@ -12,3 +12,4 @@ The arithmetic lives in ``libbsattn.so`` (C ABI: ``include/bsattn.h``); see
 
 from . import block_indexer_b200, flops  # noqa: F401
 from .block_indexer_b200 import attention, select_blocks, pool_k, fine  # noqa: F401
+from .block_indexer_b200 import attention_trainable, backward  # noqa: F401

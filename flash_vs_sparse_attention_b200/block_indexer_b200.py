@@ -370,6 +370,63 @@ def fine(Q, K, V, idx, causal=False, block_size=64, *, flags=0, check_errors=Tru
 
 
 # ---------------------------------------------------------------------------
+# Backward pass (the reference's stated next step, blog.md:133).  Its PyTorch
+# variant is differentiable: autograd gives Q, K, V the gradient of the fine
+# stage over the selected keys (block_indexer.py:55-84) and nothing through
+# the top-k indices (:53).  These compute the same gradients on the GPU.
+
+def backward(Q, K, V, dO, idx, causal=False, block_size=64):
+    """dQ, dK, dV (bf16, Q's shape) of the fine stage over the selection
+    ``idx`` (as ``select_blocks`` returns it), for the output gradient dO."""
+    L = _require_backend()
+    B, H, N, D = Q.shape
+    _check_inputs(Q, K, V)
+    if dO.shape != Q.shape or dO.dtype != torch.bfloat16 or dO.device != Q.device:
+        raise ValueError(f"{VARIANT}: dO must be a bf16 tensor of Q's shape on Q's device")
+    top_k = idx.shape[-1]
+    Qc, Kc, Vc, dOc = (t.contiguous() for t in (Q, K, V, dO))
+    idxc = idx.to(torch.int32).contiguous()
+    p = problem(B, H, N, D, causal, block_size, top_k, 0)
+    with torch.cuda.device(Q.device):
+        dQ, dK, dV = (torch.empty_like(Qc) for _ in range(3))
+        need = L.bsa_backward_workspace_bytes(ctypes.byref(p))
+        if need == 0:
+            _lib.check(L.bsa_check_problem(ctypes.byref(p)), VARIANT)
+        ws = torch.empty(max(need, 16), dtype=torch.uint8, device=Q.device)
+        _lib.check(L.bsa_backward(ctypes.byref(p), _ptr(Qc), _ptr(Kc), _ptr(Vc), _ptr(dOc),
+                                  _ptr(idxc), _ptr(dQ), _ptr(dK), _ptr(dV), _ptr(ws),
+                                  ctypes.c_size_t(ws.numel()), _stream(Q.device)), VARIANT)
+    return dQ, dK, dV
+
+
+class _BlockSparseAttention(torch.autograd.Function):
+    """Forward: selection then the fine stage (the selection is saved);
+    backward: ``backward`` over that selection."""
+
+    @staticmethod
+    def forward(ctx, Q, K, V, causal, block_size, top_k, flags):
+        idx = select_blocks(Q, K, causal, block_size, top_k, flags=flags)
+        O = fine(Q, K, V, idx, causal, block_size, flags=flags)
+        ctx.save_for_backward(Q, K, V, idx)
+        ctx.causal, ctx.block_size = causal, block_size
+        return O
+
+    @staticmethod
+    def backward(ctx, dO):
+        Q, K, V, idx = ctx.saved_tensors
+        dQ, dK, dV = backward(Q, K, V, dO.to(torch.bfloat16), idx, ctx.causal, ctx.block_size)
+        return dQ, dK, dV, None, None, None, None
+
+
+def attention_trainable(Q, K, V, causal=False, block_size=64, top_k=16, *, flags=0):
+    """``attention`` with a backward pass (torch autograd): the same output,
+    and gradients for Q, K, V as autograd gives the reference's PyTorch
+    variant (block_indexer.py:4-86) -- the fine stage's, with the selection
+    held fixed.  top_k may be a sequence of per-head budgets."""
+    return _BlockSparseAttention.apply(Q, K, V, causal, block_size, top_k, flags)
+
+
+# ---------------------------------------------------------------------------
 # Decode-time reuse: block means kept beside a KV cache.  The reference has
 # no decode path (its stated future work); these evaluate its algorithm
 # (block_indexer.py:33-84) for new query rows against a cache.

@@ -556,6 +556,36 @@ int bsa_fine(const bsa_problem* p, const void* Q, const void* K, const void* V, 
   return e == cudaSuccess ? BSA_OK : cuda_fail(e, "fine launch");
 }
 
+size_t bsa_backward_workspace_bytes(const bsa_problem* p) {
+  if (check(p) != BSA_OK) return 0;
+  Shape s = make_shape(p, (int)total_units(p));
+  return backward_supported(s) ? backward_workspace_bytes(s) : 0;
+}
+
+int bsa_backward(const bsa_problem* p, const void* Q, const void* K, const void* V,
+                 const void* dO, const int32_t* idx, void* dQ, void* dK, void* dV,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  int st = check(p);
+  if (st != BSA_OK) return st;
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(dO) || !aligned16(idx) ||
+      !aligned16(dQ) || !aligned16(dK) || !aligned16(dV) || !aligned16(workspace))
+    return fail(BSA_ERR_ALIGNMENT, "Q, K, V, dO, idx, dQ, dK, dV and workspace must be 16-byte aligned");
+  Shape s = make_shape(p, (int)total_units(p));
+  if (!backward_supported(s))
+    return fail(BSA_ERR_UNSUPPORTED, "backward: head_dim %d, block_size %d, top_k %d not covered",
+                s.D, s.bs, s.k);
+  const size_t need = backward_workspace_bytes(s);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(BSA_ERR_WORKSPACE, "backward needs %zu bytes of workspace, got %zu", need,
+                workspace_bytes);
+  cudaError_t e = launch_backward((const __nv_bfloat16*)Q, (const __nv_bfloat16*)K,
+                                  (const __nv_bfloat16*)V, (const __nv_bfloat16*)dO, idx,
+                                  (__nv_bfloat16*)dQ, (__nv_bfloat16*)dK, (__nv_bfloat16*)dV,
+                                  (unsigned char*)workspace, s, (cudaStream_t)stream);
+  return e == cudaSuccess ? BSA_OK : cuda_fail(e, "backward launch");
+}
+
 int bsa_workspace_error_offset(const bsa_problem* p, size_t workspace_bytes, int from_forward,
                                size_t* offset) {
   g_last_error.clear();

@@ -1357,6 +1357,48 @@ static cudaError_t launch_kv_kernel(const __nv_bfloat16* Q, const __nv_bfloat16*
   return cudaGetLastError();
 }
 
+// bucket_count + bucket_scatter: per (unit, block) the query rows that
+// picked it (rows of query tiles excluded when `tm` has any).
+static cudaError_t launch_buckets(const int32_t* idx, const __nv_bfloat16* V, const FineWs& w,
+                                  QTiles tm, const Shape& s, cudaStream_t st) {
+  cudaError_t e = cudaSuccess;
+  const BucketGeom g = bucket_geom(s);
+  const dim3 bgrid(g.chunks, s.units);
+  const size_t count_smem = sizeof(int32_t) * s.nb;
+  const size_t scatter_smem = sizeof(int32_t) * (2 * (size_t)s.nb + kBucketBatch);
+  // 16-byte entry loads when every batch starts on a 16-byte boundary.
+  const bool vec = (s.k % 4 == 0) && ((uintptr_t)idx % 16 == 0);
+  auto count_k = vec ? bucket_count_kernel<true> : bucket_count_kernel<false>;
+  auto scatter_k = vec ? bucket_scatter_kernel<true> : bucket_scatter_kernel<false>;
+  if (count_smem > 48 * 1024 &&
+      (e = cudaFuncSetAttribute(count_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)count_smem)) != cudaSuccess)
+    return e;
+  if ((e = cudaFuncSetAttribute(scatter_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)scatter_smem)) != cudaSuccess)
+    return e;
+  count_k<<<bgrid, kBucketThreads, count_smem, st>>>(idx, w.cursor, w.chunk_rel, w.done,
+                                                     w.offsets, w.item_row, w.items, w.ctr, V,
+                                                     w.vexp, tm, s, g, 1.0f / (float)s.k);
+  scatter_k<<<bgrid, kBucketThreads, scatter_smem, st>>>(idx, w.chunk_rel, w.offsets, w.item_row,
+                                                         w.lists, w.inv, tm, s, g,
+                                                         1.0f / (float)s.k);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bucket_lists(const int32_t* idx, const __nv_bfloat16* V, unsigned char* ws,
+                                const Shape& s, cudaStream_t st, BucketLists* out) {
+  FineWs w = fine_ws_layout(s, ws);
+  cudaError_t e = cudaMemsetAsync(w.err, 0, w.zero_bytes, st);
+  if (e != cudaSuccess) return e;
+  const QTiles tm{nullptr, w.ctr + 2, 0};
+  if ((e = launch_buckets(idx, V, w, tm, s, st)) != cudaSuccess) return e;
+  out->lists = w.lists;
+  out->offsets = w.offsets;
+  out->counts = w.cursor;
+  return cudaSuccess;
+}
+
 cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                            const __nv_bfloat16* V, const int32_t* idx, __nv_bfloat16* O,
                            unsigned char* ws, const Shape& s, uint32_t flags, cudaStream_t st,
@@ -1384,27 +1426,7 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
       (e = launch_classify_tiles(idx, w.tile_mode, w.qt_bits, w.qt_info, w.ctr + 2, s, max_union,
                                  st)) != cudaSuccess)
     return e;
-  const BucketGeom g = bucket_geom(s);
-  const dim3 bgrid(g.chunks, s.units);
-  const size_t count_smem = sizeof(int32_t) * s.nb;
-  const size_t scatter_smem = sizeof(int32_t) * (2 * (size_t)s.nb + kBucketBatch);
-  // 16-byte entry loads when every batch starts on a 16-byte boundary.
-  const bool vec = (s.k % 4 == 0) && ((uintptr_t)idx % 16 == 0);
-  auto count_k = vec ? bucket_count_kernel<true> : bucket_count_kernel<false>;
-  auto scatter_k = vec ? bucket_scatter_kernel<true> : bucket_scatter_kernel<false>;
-  if (count_smem > 48 * 1024 &&
-      (e = cudaFuncSetAttribute(count_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)count_smem)) != cudaSuccess)
-    return e;
-  if ((e = cudaFuncSetAttribute(scatter_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)scatter_smem)) != cudaSuccess)
-    return e;
-  count_k<<<bgrid, kBucketThreads, count_smem, st>>>(idx, w.cursor, w.chunk_rel, w.done,
-                                                     w.offsets, w.item_row, w.items, w.ctr, V,
-                                                     w.vexp, tm, s, g, 1.0f / (float)s.k);
-  scatter_k<<<bgrid, kBucketThreads, scatter_smem, st>>>(idx, w.chunk_rel, w.offsets, w.item_row,
-                                                         w.lists, w.inv, tm, s, g,
-                                                         1.0f / (float)s.k);
+  if ((e = launch_buckets(idx, V, w, tm, s, st)) != cudaSuccess) return e;
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   mark(2);
   if (s.bs == 64 && s.D == 64) e = launch_kv_kernel<64, 64>(Q, K, V, w, s, st);

@@ -36,6 +36,25 @@ cudaError_t launch_fine_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                            const __nv_bfloat16* V, const int32_t* idx, __nv_bfloat16* O,
                            unsigned char* ws, const Shape& s, uint32_t flags, cudaStream_t st,
                            int* n_launches, void* const* events, int n_events, bool pre_zeroed);
+// Per (unit, key block) the query rows that picked it, from the forward's
+// bucket kernels over every row (the fine workspace of `s` at `ws`):
+// lists + unit * N * k + offsets[unit * nb + j] holds counts[unit * nb + j] rows.
+struct BucketLists {
+  const int32_t* lists;
+  const int32_t* offsets;
+  const int32_t* counts;
+};
+cudaError_t launch_bucket_lists(const int32_t* idx, const __nv_bfloat16* V, unsigned char* ws,
+                                const Shape& s, cudaStream_t st, BucketLists* out);
+
+// Backward of the fine stage (backward.cu): dQ, dK, dV for a fixed selection.
+bool backward_supported(const Shape& s);
+size_t backward_workspace_bytes(const Shape& s);
+cudaError_t launch_backward(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                            const __nv_bfloat16* V, const __nv_bfloat16* dO, const int32_t* idx,
+                            __nv_bfloat16* dQ, __nv_bfloat16* dK, __nv_bfloat16* dV,
+                            unsigned char* ws, const Shape& s, cudaStream_t st);
+
 // Query-stationary fine kernel for query tiles (fine_q.cu): the shapes it
 // covers, the union limit for a tile under `flags` (0: none), tiles per
 // unit, the tile classifier and the kernel.

@@ -214,6 +214,20 @@ int bsa_fine(const bsa_problem* p, const void* Q, const void* K, const void* V,
              const int32_t* idx, void* O, void* workspace, size_t workspace_bytes,
              void* stream);
 
+/* Backward pass of the fine stage, the reference's stated next step
+ * (blog.md:133): dQ, dK, dV (B, H, N, D) bf16 for the output gradient dO of
+ * O = fine attention over the selection `idx` (as bsa_select_blocks writes
+ * it, including per-head budgets), the selection held fixed -- what torch
+ * autograd gives the reference's differentiable variant, where the top-k
+ * indices (block_indexer.py:53) carry no gradient and Q, K, V receive the
+ * fine stage's (block_indexer.py:55-84).  CUDA cores; the result does not
+ * depend on the order of the GPU's work (no atomics).  head_dim 32, 64, 96
+ * or 128, block_size * head_dim <= 8192 (BSA_ERR_UNSUPPORTED otherwise). */
+size_t bsa_backward_workspace_bytes(const bsa_problem* p);
+int bsa_backward(const bsa_problem* p, const void* Q, const void* K, const void* V,
+                 const void* dO, const int32_t* idx, void* dQ, void* dK, void* dV,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
 /* Bytes of workspace bsa_fine needs for all units at once. */
 size_t bsa_fine_workspace_bytes(const bsa_problem* p);
 

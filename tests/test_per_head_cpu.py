@@ -30,3 +30,17 @@ def test_flops_per_head():
     mixed = F.compute_flops_per_head(1, 4096, 64, [4, 16])
     assert mixed == (F.compute_flops(1, 1, 4096, 64, "block_indexer_b200", 64, 4)
                      + F.compute_flops(1, 1, 4096, 64, "block_indexer_b200", 64, 16))
+
+
+def test_oracle_backward_matches_reference_autograd():
+    """The oracle's gradients against the reference's own (torch autograd of
+    attention/block_indexer.py on the golden inputs, fp32)."""
+    import os
+    from oracle.backward_np import backward
+    here = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    for name in ("bwd_refshape_full", "bwd_refshape_causal", "bwd_n256_causal"):
+        z = np.load(os.path.join(here, name + ".npz"))
+        B, H, N, D, bs, k, causal = (int(x) for x in z["meta"])
+        dQ, dK, dV = backward(z["Q"], z["K"], z["V"], z["dO"], bool(causal), bs, k)
+        for got, key in ((dQ, "dQ"), (dK, "dK"), (dV, "dV")):
+            assert np.abs(got - z[key]).max() <= 1e-5 * max(1.0, np.abs(z[key]).max()), (name, key)
