@@ -730,6 +730,77 @@ def run_decode(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+BACKWARD_METRIC = "block-sparse attn bwd ms (fine-stage dQ, dK, dV; selection fixed)"
+
+
+def run_backward(args, cfg):
+    """One step = the backward pass of the workload's fine stage (bsa_backward:
+    the per-row kernel, the bucket lists, the per-block kernel) for a fixed
+    selection and output gradient.  L2 is flushed before every step, outside
+    the events.  Algorithmic work: the five products of an attention backward
+    over the selected keys (scores, dP, dQ, dK, dV), 10 N k bs D FLOP a unit."""
+    import torch
+
+    from flash_vs_sparse_attention_b200 import block_indexer_b200 as bi
+
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        raise SystemExit("--mode backward runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    U = args.units or cfg["B"] * cfg["H"]
+    N, D, bs, k, causal = cfg["N"], cfg["D"], cfg["block_size"], cfg["top_k"], cfg["causal"]
+    Q, K, V = gpu_inputs(cfg, U, seed=9, device=dev)
+    dO = torch.randn(Q.shape, generator=torch.Generator(device=dev).manual_seed(10),
+                     device=dev).to(torch.bfloat16)
+    idx = bi.select_blocks(Q, K, causal=causal, block_size=bs, top_k=k)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        flush.zero_()
+        bi.backward(Q, K, V, dO, idx, causal, bs)
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(0) as clk:
+        for j in range(args.steps):
+            flush.zero_()
+            starts[j].record()
+            bi.backward(Q, K, V, dO, idx, causal, bs)
+            ends[j].record()
+        torch.cuda.synchronize()
+    ms_step = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / args.steps
+    flop = 10 * U * N * k * bs * D
+    peaks, peak_kind = load_peaks()
+    tflops = flop / (ms_step * 1e-3) / 1e12
+    # The oracle's backward on the host for a sample: the first rows of unit
+    # 0 (causal rows see only earlier keys, so a prefix is their whole work).
+    from oracle.backward_np import backward_unit
+    rows = min(N, 2048)
+    q, kk, v, g = (t[0, 0, :rows].float().cpu().numpy() for t in (Q, K, V, dO))
+    t0 = time.perf_counter()
+    backward_unit(q, kk, v, g, causal, bs, min(k, rows // bs))
+    cpu_ms = (time.perf_counter() - t0) * 1e3
+    line = {
+        "metric": BACKWARD_METRIC, "value": round(ms_step, 4), "unit": "ms", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": f"backward {workload_name(cfg)}", "units": U,
+                   "l2": f"flushed before every step ({L2_FLUSH_BYTES >> 20} MiB write, outside the events)"},
+        "tflops": round(tflops, 2),
+        "roofline": {"kernel": "backward (CUDA cores: per-row dQ, per-block dK/dV)", "bound": "tensor",
+                     "achieved": round(tflops, 2), "peak": float(peaks["bf16_tflops"]),
+                     "unit": "TFLOP/s", "frac": round(tflops / float(peaks["bf16_tflops"]), 5),
+                     "peak_source": f"{peak_kind} bf16_tflops", "traffic": None,
+                     "flops_per_step": flop,
+                     "note": "CUDA-core kernels measured against the tensor-core peak"},
+        "clocks": clk.summary(), "gpu_launches": 5 * args.steps,
+        "cpu_baseline": {"value": round(cpu_ms, 3), "unit": "ms", "cores": 1, "kind": "port",
+                         "sample": f"rows 0..{rows - 1} of unit 0 through the numpy backward "
+                                   "oracle, 1 thread (a causal prefix is the rows' whole work)"},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -750,14 +821,17 @@ def main(argv=None):
     ap.add_argument("--no-graph", action="store_true",
                     help="launch the timed steps directly instead of replaying a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", default="forward", choices=["forward", "decode"],
-                    help="decode: one-token decode steps over a KV cache (its own JSON line)")
+    ap.add_argument("--mode", default="forward", choices=["forward", "decode", "backward"],
+                    help="decode: one-token decode steps over a KV cache; backward: the fine "
+                         "stage's gradients (each its own JSON line)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
     cfg = WORKLOADS[args.config]
     if args.mode == "decode":
         run_decode(args, cfg)
+    elif args.mode == "backward":
+        run_backward(args, cfg)
     elif args.impl == "reference":
         run_reference(args, cfg)
     else:
