@@ -63,7 +63,10 @@ __device__ __forceinline__ void load_cols(const __nv_bfloat16* __restrict__ row,
   for (int c = 0; c < DPL; ++c) out[c] = __bfloat162float(row[lane * DPL + c]);
 }
 
-template <int DPL>
+// CACHE: each warp keeps its row's scores and dP (k * bs floats each) in
+// shared memory from the first pass, so the later passes read every key
+// row once, coalesced; otherwise they recompute them.
+template <int DPL, bool CACHE>
 __global__ void __launch_bounds__(kBwdRowsWarps * 32)
 bwd_rows_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restrict__ K,
                 const __nv_bfloat16* __restrict__ V, const __nv_bfloat16* __restrict__ dO,
@@ -71,9 +74,13 @@ bwd_rows_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __rest
                 float* __restrict__ lse_out, float* __restrict__ delta_out, Shape s) {
   constexpr int D = DPL * 32;
   __shared__ float q_s[kBwdRowsWarps][D], g_s[kBwdRowsWarps][D], w_s[kBwdRowsWarps][32];
+  extern __shared__ float cache_f[];   // CACHE: per warp, k * bs scores then k * bs dP
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int u = blockIdx.y, row = blockIdx.x * kBwdRowsWarps + warp;
   if (row >= s.N) return;   // whole warp; no CTA barrier below
+  const int kb = s.k * s.bs;
+  float* s_c = cache_f + (size_t)warp * 2 * kb;
+  float* dp_c = s_c + kb;
   const int64_t R = (int64_t)u * s.N + row;
   float qd[DPL], gd[DPL];
   load_cols<DPL>(Q + R * D, lane, qd);
@@ -93,13 +100,20 @@ bwd_rows_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __rest
     const bool live = in_block && (!s.causal || key <= row);
     return live ? dot_row<DPL>(q_s[warp], Ku + (int64_t)key * D) * sc : -INFINITY;
   };
-  // 1. log-sum-exp (base 2) over the selected keys.
+  // 1. log-sum-exp (base 2) over the selected keys (and, cached, dP).
   float m = -INFINITY, l = 0.f;
   for (int q = 0; q < s.k; ++q) {
     const int j = sel[q];
     if (j < 0) continue;
     for (int c0 = 0; c0 < s.bs; c0 += 32) {
-      const float x = score(j * s.bs + c0 + lane, c0 + lane < s.bs);
+      const int key = j * s.bs + c0 + lane;
+      const bool in_block = c0 + lane < s.bs;
+      const float x = score(key, in_block);
+      if (CACHE && in_block) {
+        s_c[q * s.bs + c0 + lane] = x;
+        dp_c[q * s.bs + c0 + lane] =
+            x != -INFINITY ? dot_row<DPL>(g_s[warp], Vu + (int64_t)key * D) : 0.f;
+      }
       const float gm = warp_max(x);
       if (gm == -INFINITY) continue;
       if (gm > m) {
@@ -109,6 +123,7 @@ bwd_rows_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __rest
       l += warp_sum(exp2f(x - m));
     }
   }
+  __syncwarp();
   const float lse = m + log2f(l);
   // 2. O (fp32) and delta = dO . O.
   float o[DPL];
@@ -118,7 +133,9 @@ bwd_rows_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __rest
     const int j = sel[q];
     if (j < 0) continue;
     for (int c0 = 0; c0 < s.bs; c0 += 32) {
-      const float x = score(j * s.bs + c0 + lane, c0 + lane < s.bs);
+      const bool in_block = c0 + lane < s.bs;
+      const float x = CACHE ? (in_block ? s_c[q * s.bs + c0 + lane] : -INFINITY)
+                            : score(j * s.bs + c0 + lane, in_block);
       w_s[warp][lane] = exp2f(x - lse);
       __syncwarp();
       const int n = min(32, s.bs - c0);
@@ -147,9 +164,15 @@ bwd_rows_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __rest
     for (int c0 = 0; c0 < s.bs; c0 += 32) {
       const int key = j * s.bs + c0 + lane;
       const bool in_block = c0 + lane < s.bs;
-      const float x = score(key, in_block);
+      float x, dp;
+      if (CACHE) {
+        x = in_block ? s_c[q * s.bs + c0 + lane] : -INFINITY;
+        dp = in_block ? dp_c[q * s.bs + c0 + lane] : 0.f;
+      } else {
+        x = score(key, in_block);
+        dp = x != -INFINITY ? dot_row<DPL>(g_s[warp], Vu + (int64_t)key * D) : 0.f;
+      }
       const float p = exp2f(x - lse);
-      const float dp = (p != 0.f) ? dot_row<DPL>(g_s[warp], Vu + (int64_t)key * D) : 0.f;
       w_s[warp][lane] = p * (dp - delta);
       __syncwarp();
       const int n = min(32, s.bs - c0);
@@ -172,8 +195,8 @@ bwd_rows_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __rest
   }
 }
 
-template <int DPL>
-__global__ void __launch_bounds__(kBwdKvThreads)
+template <int DPL, int EPT>   // EPT: gradient elements per thread, >= bs * D / 256
+__global__ void __launch_bounds__(kBwdKvThreads, 2)
 bwd_kv_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restrict__ K,
               const __nv_bfloat16* __restrict__ V, const __nv_bfloat16* __restrict__ dO,
               const float* __restrict__ lse, const float* __restrict__ delta,
@@ -181,7 +204,6 @@ bwd_kv_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restri
               const int32_t* __restrict__ counts, __nv_bfloat16* __restrict__ dK,
               __nv_bfloat16* __restrict__ dV, Shape s) {
   constexpr int D = DPL * 32;
-  constexpr int EPT = 32;   // gradient elements per thread at most (bs * D <= 8192)
   extern __shared__ float smem_f[];
   const int j = blockIdx.x, u = blockIdx.y, t = threadIdx.x;
   const int warp = t >> 5, lane = t & 31;
@@ -306,6 +328,21 @@ size_t backward_workspace_bytes(const Shape& s) {
   return fine_kv_workspace_bytes(s) + ((2 * rows * sizeof(float) + 255) & ~(size_t)255);
 }
 
+template <int DPL, int EPT>
+static cudaError_t launch_bwd_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                 const __nv_bfloat16* V, const __nv_bfloat16* dO,
+                                 const float* lse, const float* delta, const BucketLists& bl,
+                                 __nv_bfloat16* dK, __nv_bfloat16* dV, const Shape& s,
+                                 cudaStream_t st) {
+  const size_t smem = bwd_kv_smem(s);
+  cudaError_t e = cudaFuncSetAttribute(bwd_kv_kernel<DPL, EPT>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  bwd_kv_kernel<DPL, EPT><<<dim3(s.nb, s.units), kBwdKvThreads, smem, st>>>(
+      Q, K, V, dO, lse, delta, bl.lists, bl.offsets, bl.counts, dK, dV, s);
+  return cudaGetLastError();
+}
+
 template <int DPL>
 static cudaError_t launch_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                               const __nv_bfloat16* V, const __nv_bfloat16* dO,
@@ -315,18 +352,31 @@ static cudaError_t launch_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
   float* lse = reinterpret_cast<float*>(ws + fine_kv_workspace_bytes(s));
   float* delta = lse + (size_t)s.units * s.N;
   dim3 g1((s.N + kBwdRowsWarps - 1) / kBwdRowsWarps, s.units);
-  bwd_rows_kernel<DPL><<<g1, kBwdRowsWarps * 32, 0, st>>>(Q, K, V, dO, idx, dQ, lse, delta, s);
-  cudaError_t e = cudaGetLastError();
+  // Cached scores and dP: 8 warps x 2 x k * bs floats (64 KiB at k * bs = 1024).
+  const size_t cache = sizeof(float) * kBwdRowsWarps * 2 * (size_t)s.k * s.bs;
+  cudaError_t e;
+  if (cache <= 96 * 1024) {
+    if ((e = cudaFuncSetAttribute(bwd_rows_kernel<DPL, true>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cache)) !=
+        cudaSuccess)
+      return e;
+    bwd_rows_kernel<DPL, true><<<g1, kBwdRowsWarps * 32, cache, st>>>(Q, K, V, dO, idx, dQ, lse,
+                                                                      delta, s);
+  } else {
+    bwd_rows_kernel<DPL, false><<<g1, kBwdRowsWarps * 32, 0, st>>>(Q, K, V, dO, idx, dQ, lse,
+                                                                   delta, s);
+  }
+  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   BucketLists bl;
   if ((e = launch_bucket_lists(idx, V, ws, s, st, &bl)) != cudaSuccess) return e;
-  const size_t smem = bwd_kv_smem(s);
-  if ((e = cudaFuncSetAttribute(bwd_kv_kernel<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)smem)) != cudaSuccess)
-    return e;
-  bwd_kv_kernel<DPL><<<dim3(s.nb, s.units), kBwdKvThreads, smem, st>>>(
-      Q, K, V, dO, lse, delta, bl.lists, bl.offsets, bl.counts, dK, dV, s);
-  return cudaGetLastError();
+  const int elems = s.bs * s.D;
+  if (elems <= 256) return launch_bwd_kv<DPL, 1>(Q, K, V, dO, lse, delta, bl, dK, dV, s, st);
+  if (elems <= 512) return launch_bwd_kv<DPL, 2>(Q, K, V, dO, lse, delta, bl, dK, dV, s, st);
+  if (elems <= 1024) return launch_bwd_kv<DPL, 4>(Q, K, V, dO, lse, delta, bl, dK, dV, s, st);
+  if (elems <= 2048) return launch_bwd_kv<DPL, 8>(Q, K, V, dO, lse, delta, bl, dK, dV, s, st);
+  if (elems <= 4096) return launch_bwd_kv<DPL, 16>(Q, K, V, dO, lse, delta, bl, dK, dV, s, st);
+  return launch_bwd_kv<DPL, 32>(Q, K, V, dO, lse, delta, bl, dK, dV, s, st);
 }
 
 cudaError_t launch_backward(const __nv_bfloat16* Q, const __nv_bfloat16* K,
