@@ -735,8 +735,8 @@ BACKWARD_METRIC = "block-sparse attn bwd ms (fine-stage dQ, dK, dV; selection fi
 
 def run_backward(args, cfg):
     """One step = the backward pass of the workload's fine stage (bsa_backward:
-    the per-row kernel, the bucket lists, the per-block kernel) for a fixed
-    selection and output gradient.  L2 is flushed before every step, outside
+    the per-row log-sum-exp, the bucket lists, the per-block kernel, the dQ
+    sum) for a fixed selection, forward output and output gradient.  L2 is flushed before every step, outside
     the events.  Algorithmic work: the five products of an attention backward
     over the selected keys (scores, dP, dQ, dK, dV), 10 N k bs D FLOP a unit."""
     import torch
@@ -753,10 +753,11 @@ def run_backward(args, cfg):
     dO = torch.randn(Q.shape, generator=torch.Generator(device=dev).manual_seed(10),
                      device=dev).to(torch.bfloat16)
     idx = bi.select_blocks(Q, K, causal=causal, block_size=bs, top_k=k)
+    O = bi.fine(Q, K, V, idx, causal=causal, block_size=bs)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     for _ in range(args.warmup):
         flush.zero_()
-        bi.backward(Q, K, V, dO, idx, causal, bs)
+        bi.backward(Q, K, V, O, dO, idx, causal, bs)
     torch.cuda.synchronize()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -764,7 +765,7 @@ def run_backward(args, cfg):
         for j in range(args.steps):
             flush.zero_()
             starts[j].record()
-            bi.backward(Q, K, V, dO, idx, causal, bs)
+            bi.backward(Q, K, V, O, dO, idx, causal, bs)
             ends[j].record()
         torch.cuda.synchronize()
     ms_step = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / args.steps
@@ -787,13 +788,13 @@ def run_backward(args, cfg):
         "config": {"workload": f"backward {workload_name(cfg)}", "units": U,
                    "l2": f"flushed before every step ({L2_FLUSH_BYTES >> 20} MiB write, outside the events)"},
         "tflops": round(tflops, 2),
-        "roofline": {"kernel": "backward (CUDA cores: per-row dQ, per-block dK/dV)", "bound": "tensor",
+        "roofline": {"kernel": "backward (CUDA cores: per-block dK, dV and dQ shares)", "bound": "tensor",
                      "achieved": round(tflops, 2), "peak": float(peaks["bf16_tflops"]),
                      "unit": "TFLOP/s", "frac": round(tflops / float(peaks["bf16_tflops"]), 5),
                      "peak_source": f"{peak_kind} bf16_tflops", "traffic": None,
                      "flops_per_step": flop,
                      "note": "CUDA-core kernels measured against the tensor-core peak"},
-        "clocks": clk.summary(), "gpu_launches": 5 * args.steps,
+        "clocks": clk.summary(), "gpu_launches": 6 * args.steps,
         "cpu_baseline": {"value": round(cpu_ms, 3), "unit": "ms", "cores": 1, "kind": "port",
                          "sample": f"rows 0..{rows - 1} of unit 0 through the numpy backward "
                                    "oracle, 1 thread (a causal prefix is the rows' whole work)"},

@@ -67,7 +67,7 @@ SIGNATURES = {
     "bsa_fine": (_c.c_int, [_PP, _P, _P, _P, _P, _P, _P, _c.c_size_t, _P]),
     "bsa_fine_workspace_bytes": (_c.c_size_t, [_PP]),
     "bsa_backward_workspace_bytes": (_c.c_size_t, [_PP]),
-    "bsa_backward": (_c.c_int, [_PP, _P, _P, _P, _P, _P, _P, _P, _P, _P, _c.c_size_t, _P]),
+    "bsa_backward": (_c.c_int, [_PP, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _c.c_size_t, _P]),
     "bsa_workspace_error": (_c.c_int, [_PP, _P, _c.c_size_t, _c.c_int, _c.POINTER(_c.c_uint32)]),
     "bsa_forward_noalloc": (_c.c_int, [_PP, _P, _P, _P, _P, _P]),
     "bsa_noalloc_error": (_c.c_int, [_PP, _c.POINTER(_c.c_uint32)]),

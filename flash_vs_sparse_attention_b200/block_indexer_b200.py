@@ -375,16 +375,18 @@ def fine(Q, K, V, idx, causal=False, block_size=64, *, flags=0, check_errors=Tru
 # stage over the selected keys (block_indexer.py:55-84) and nothing through
 # the top-k indices (:53).  These compute the same gradients on the GPU.
 
-def backward(Q, K, V, dO, idx, causal=False, block_size=64):
+def backward(Q, K, V, O, dO, idx, causal=False, block_size=64):
     """dQ, dK, dV (bf16, Q's shape) of the fine stage over the selection
-    ``idx`` (as ``select_blocks`` returns it), for the output gradient dO."""
+    ``idx`` (as ``select_blocks`` returns it), for the output gradient dO;
+    O is the forward's output over that selection."""
     L = _require_backend()
     B, H, N, D = Q.shape
     _check_inputs(Q, K, V)
-    if dO.shape != Q.shape or dO.dtype != torch.bfloat16 or dO.device != Q.device:
-        raise ValueError(f"{VARIANT}: dO must be a bf16 tensor of Q's shape on Q's device")
+    for name, t in (("O", O), ("dO", dO)):
+        if t.shape != Q.shape or t.dtype != torch.bfloat16 or t.device != Q.device:
+            raise ValueError(f"{VARIANT}: {name} must be a bf16 tensor of Q's shape on Q's device")
     top_k = idx.shape[-1]
-    Qc, Kc, Vc, dOc = (t.contiguous() for t in (Q, K, V, dO))
+    Qc, Kc, Vc, Oc, dOc = (t.contiguous() for t in (Q, K, V, O, dO))
     idxc = idx.to(torch.int32).contiguous()
     p = problem(B, H, N, D, causal, block_size, top_k, 0)
     with torch.cuda.device(Q.device):
@@ -393,8 +395,8 @@ def backward(Q, K, V, dO, idx, causal=False, block_size=64):
         if need == 0:
             _lib.check(L.bsa_check_problem(ctypes.byref(p)), VARIANT)
         ws = torch.empty(max(need, 16), dtype=torch.uint8, device=Q.device)
-        _lib.check(L.bsa_backward(ctypes.byref(p), _ptr(Qc), _ptr(Kc), _ptr(Vc), _ptr(dOc),
-                                  _ptr(idxc), _ptr(dQ), _ptr(dK), _ptr(dV), _ptr(ws),
+        _lib.check(L.bsa_backward(ctypes.byref(p), _ptr(Qc), _ptr(Kc), _ptr(Vc), _ptr(Oc),
+                                  _ptr(dOc), _ptr(idxc), _ptr(dQ), _ptr(dK), _ptr(dV), _ptr(ws),
                                   ctypes.c_size_t(ws.numel()), _stream(Q.device)), VARIANT)
     return dQ, dK, dV
 
@@ -407,14 +409,15 @@ class _BlockSparseAttention(torch.autograd.Function):
     def forward(ctx, Q, K, V, causal, block_size, top_k, flags):
         idx = select_blocks(Q, K, causal, block_size, top_k, flags=flags)
         O = fine(Q, K, V, idx, causal, block_size, flags=flags)
-        ctx.save_for_backward(Q, K, V, idx)
+        ctx.save_for_backward(Q, K, V, O, idx)
         ctx.causal, ctx.block_size = causal, block_size
         return O
 
     @staticmethod
     def backward(ctx, dO):
-        Q, K, V, idx = ctx.saved_tensors
-        dQ, dK, dV = backward(Q, K, V, dO.to(torch.bfloat16), idx, ctx.causal, ctx.block_size)
+        Q, K, V, O, idx = ctx.saved_tensors
+        dQ, dK, dV = backward(Q, K, V, O, dO.to(torch.bfloat16).contiguous(), idx, ctx.causal,
+                              ctx.block_size)
         return dQ, dK, dV, None, None, None, None
 
 

@@ -563,14 +563,16 @@ size_t bsa_backward_workspace_bytes(const bsa_problem* p) {
 }
 
 int bsa_backward(const bsa_problem* p, const void* Q, const void* K, const void* V,
-                 const void* dO, const int32_t* idx, void* dQ, void* dK, void* dV,
-                 void* workspace, size_t workspace_bytes, void* stream) {
+                 const void* O, const void* dO, const int32_t* idx, void* dQ, void* dK,
+                 void* dV, void* workspace, size_t workspace_bytes, void* stream) {
   g_last_error.clear();
   int st = check(p);
   if (st != BSA_OK) return st;
-  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(dO) || !aligned16(idx) ||
-      !aligned16(dQ) || !aligned16(dK) || !aligned16(dV) || !aligned16(workspace))
-    return fail(BSA_ERR_ALIGNMENT, "Q, K, V, dO, idx, dQ, dK, dV and workspace must be 16-byte aligned");
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O) || !aligned16(dO) ||
+      !aligned16(idx) || !aligned16(dQ) || !aligned16(dK) || !aligned16(dV) ||
+      !aligned16(workspace))
+    return fail(BSA_ERR_ALIGNMENT,
+                "Q, K, V, O, dO, idx, dQ, dK, dV and workspace must be 16-byte aligned");
   Shape s = make_shape(p, (int)total_units(p));
   if (!backward_supported(s))
     return fail(BSA_ERR_UNSUPPORTED, "backward: head_dim %d, block_size %d, top_k %d not covered",
@@ -580,7 +582,8 @@ int bsa_backward(const bsa_problem* p, const void* Q, const void* K, const void*
     return fail(BSA_ERR_WORKSPACE, "backward needs %zu bytes of workspace, got %zu", need,
                 workspace_bytes);
   cudaError_t e = launch_backward((const __nv_bfloat16*)Q, (const __nv_bfloat16*)K,
-                                  (const __nv_bfloat16*)V, (const __nv_bfloat16*)dO, idx,
+                                  (const __nv_bfloat16*)V, (const __nv_bfloat16*)O,
+                                  (const __nv_bfloat16*)dO, idx,
                                   (__nv_bfloat16*)dQ, (__nv_bfloat16*)dK, (__nv_bfloat16*)dV,
                                   (unsigned char*)workspace, s, (cudaStream_t)stream);
   return e == cudaSuccess ? BSA_OK : cuda_fail(e, "backward launch");

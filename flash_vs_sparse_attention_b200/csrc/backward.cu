@@ -6,23 +6,24 @@
 // through the top-k indices, :53.)
 //
 // Per query row i over its selected keys (scale = D^-1/2, w the softmax
-// weights):
-//     dV[key] += w * dO_i,   dp = V[key] . dO_i,   ds = w (dp - dO_i . O_i),
+// weights, delta_i = dO_i . O_i):
+//     dV[key] += w * dO_i,   dp = V[key] . dO_i,   ds = w (dp - delta_i),
 //     dQ_i = scale sum ds K[key],   dK[key] += scale ds Q_i.
 //
-//  1. bwd_rows_kernel   query-stationary, a warp per row: the row's log-sum-exp
-//                       and O (recomputed in fp32), D_i = dO_i . O_i, then dQ_i.
-//                       Lanes take keys for the dot products (32 keys at a
-//                       time) and output columns for the weighted sums.
+//  1. bwd_lse_kernel    a warp per row: the row's log-sum-exp over its
+//                       selected keys (lanes take keys) and delta_i from the
+//                       forward's O.
 //  2. bucket lists      per (unit, key block) the rows that picked it -- the
 //                       forward's bucket kernels (fine_kv.cu).
 //  3. bwd_kv_kernel     key-stationary, a CTA per (unit, key block): its
 //                       rows, sorted ascending, 8 at a time (a warp per row
-//                       for the block's scores), dK and dV of the block
-//                       accumulated in registers (thread t owns elements t,
-//                       t + 256, ...) and written once.  No atomics: each
-//                       gradient element is summed by one thread in row
-//                       order, so the result is the same on every run.
+//                       for the block's scores and dP); dK and dV of the
+//                       block summed in registers (thread t owns elements t,
+//                       t + 256, ...) and written once, and for each row the
+//                       block's share of dQ written to the row's slot.
+//  4. bwd_dq_kernel     per row, the sum of its slots' dQ shares.
+// No atomics: every sum runs in a fixed order (rows ascending, slots
+// ascending), so the result is the same on every run.
 #include "common.cuh"
 #include "launchers.cuh"
 
@@ -63,57 +64,41 @@ __device__ __forceinline__ void load_cols(const __nv_bfloat16* __restrict__ row,
   for (int c = 0; c < DPL; ++c) out[c] = __bfloat162float(row[lane * DPL + c]);
 }
 
-// CACHE: each warp keeps its row's scores and dP (k * bs floats each) in
-// shared memory from the first pass, so the later passes read every key
-// row once, coalesced; otherwise they recompute them.
-template <int DPL, bool CACHE>
+template <int DPL>
 __global__ void __launch_bounds__(kBwdRowsWarps * 32)
-bwd_rows_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restrict__ K,
-                const __nv_bfloat16* __restrict__ V, const __nv_bfloat16* __restrict__ dO,
-                const int32_t* __restrict__ idx, __nv_bfloat16* __restrict__ dQ,
-                float* __restrict__ lse_out, float* __restrict__ delta_out, Shape s) {
+bwd_lse_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restrict__ K,
+               const __nv_bfloat16* __restrict__ O, const __nv_bfloat16* __restrict__ dO,
+               const int32_t* __restrict__ idx, float* __restrict__ lse_out,
+               float* __restrict__ delta_out, Shape s) {
   constexpr int D = DPL * 32;
-  __shared__ float q_s[kBwdRowsWarps][D], g_s[kBwdRowsWarps][D], w_s[kBwdRowsWarps][32];
-  extern __shared__ float cache_f[];   // CACHE: per warp, k * bs scores then k * bs dP
+  __shared__ float q_s[kBwdRowsWarps][D];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int u = blockIdx.y, row = blockIdx.x * kBwdRowsWarps + warp;
   if (row >= s.N) return;   // whole warp; no CTA barrier below
-  const int kb = s.k * s.bs;
-  float* s_c = cache_f + (size_t)warp * 2 * kb;
-  float* dp_c = s_c + kb;
   const int64_t R = (int64_t)u * s.N + row;
-  float qd[DPL], gd[DPL];
+  float qd[DPL], od[DPL], gd[DPL];
   load_cols<DPL>(Q + R * D, lane, qd);
+  load_cols<DPL>(O + R * D, lane, od);
   load_cols<DPL>(dO + R * D, lane, gd);
+  float dl = 0.f;
 #pragma unroll
   for (int c = 0; c < DPL; ++c) {
     q_s[warp][lane * DPL + c] = qd[c];
-    g_s[warp][lane * DPL + c] = gd[c];
+    dl = fmaf(gd[c], od[c], dl);
   }
+  const float delta = warp_sum(dl);
   __syncwarp();
   const int32_t* sel = idx + R * s.k;
   const __nv_bfloat16* Ku = K + (int64_t)u * s.N * D;
-  const __nv_bfloat16* Vu = V + (int64_t)u * s.N * D;
   const float sc = s.scale * 1.4426950408889634f;   // scores in the base-2 domain
-  // Score of key `key` for this row in the base-2 domain (-inf if masked).
-  auto score = [&](int key, bool in_block) -> float {
-    const bool live = in_block && (!s.causal || key <= row);
-    return live ? dot_row<DPL>(q_s[warp], Ku + (int64_t)key * D) * sc : -INFINITY;
-  };
-  // 1. log-sum-exp (base 2) over the selected keys (and, cached, dP).
   float m = -INFINITY, l = 0.f;
   for (int q = 0; q < s.k; ++q) {
     const int j = sel[q];
     if (j < 0) continue;
     for (int c0 = 0; c0 < s.bs; c0 += 32) {
       const int key = j * s.bs + c0 + lane;
-      const bool in_block = c0 + lane < s.bs;
-      const float x = score(key, in_block);
-      if (CACHE && in_block) {
-        s_c[q * s.bs + c0 + lane] = x;
-        dp_c[q * s.bs + c0 + lane] =
-            x != -INFINITY ? dot_row<DPL>(g_s[warp], Vu + (int64_t)key * D) : 0.f;
-      }
+      const bool live = c0 + lane < s.bs && (!s.causal || key <= row);
+      const float x = live ? dot_row<DPL>(q_s[warp], Ku + (int64_t)key * D) * sc : -INFINITY;
       const float gm = warp_max(x);
       if (gm == -INFINITY) continue;
       if (gm > m) {
@@ -123,74 +108,8 @@ bwd_rows_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __rest
       l += warp_sum(exp2f(x - m));
     }
   }
-  __syncwarp();
-  const float lse = m + log2f(l);
-  // 2. O (fp32) and delta = dO . O.
-  float o[DPL];
-#pragma unroll
-  for (int c = 0; c < DPL; ++c) o[c] = 0.f;
-  for (int q = 0; q < s.k; ++q) {
-    const int j = sel[q];
-    if (j < 0) continue;
-    for (int c0 = 0; c0 < s.bs; c0 += 32) {
-      const bool in_block = c0 + lane < s.bs;
-      const float x = CACHE ? (in_block ? s_c[q * s.bs + c0 + lane] : -INFINITY)
-                            : score(j * s.bs + c0 + lane, in_block);
-      w_s[warp][lane] = exp2f(x - lse);
-      __syncwarp();
-      const int n = min(32, s.bs - c0);
-      for (int t = 0; t < n; ++t) {
-        const float p = w_s[warp][t];
-        if (p == 0.f) continue;
-        float v[DPL];
-        load_cols<DPL>(Vu + (int64_t)(j * s.bs + c0 + t) * D, lane, v);
-#pragma unroll
-        for (int c = 0; c < DPL; ++c) o[c] = fmaf(p, v[c], o[c]);
-      }
-      __syncwarp();
-    }
-  }
-  float dl = 0.f;
-#pragma unroll
-  for (int c = 0; c < DPL; ++c) dl = fmaf(gd[c], o[c], dl);
-  const float delta = warp_sum(dl);
-  // 3. dQ = scale sum_key w (dp - delta) K[key].
-  float dq[DPL];
-#pragma unroll
-  for (int c = 0; c < DPL; ++c) dq[c] = 0.f;
-  for (int q = 0; q < s.k; ++q) {
-    const int j = sel[q];
-    if (j < 0) continue;
-    for (int c0 = 0; c0 < s.bs; c0 += 32) {
-      const int key = j * s.bs + c0 + lane;
-      const bool in_block = c0 + lane < s.bs;
-      float x, dp;
-      if (CACHE) {
-        x = in_block ? s_c[q * s.bs + c0 + lane] : -INFINITY;
-        dp = in_block ? dp_c[q * s.bs + c0 + lane] : 0.f;
-      } else {
-        x = score(key, in_block);
-        dp = x != -INFINITY ? dot_row<DPL>(g_s[warp], Vu + (int64_t)key * D) : 0.f;
-      }
-      const float p = exp2f(x - lse);
-      w_s[warp][lane] = p * (dp - delta);
-      __syncwarp();
-      const int n = min(32, s.bs - c0);
-      for (int t = 0; t < n; ++t) {
-        const float ds = w_s[warp][t];
-        if (ds == 0.f) continue;
-        float kk[DPL];
-        load_cols<DPL>(Ku + (int64_t)(j * s.bs + c0 + t) * D, lane, kk);
-#pragma unroll
-        for (int c = 0; c < DPL; ++c) dq[c] = fmaf(ds, kk[c], dq[c]);
-      }
-      __syncwarp();
-    }
-  }
-#pragma unroll
-  for (int c = 0; c < DPL; ++c) dQ[R * D + lane * DPL + c] = __float2bfloat16(dq[c] * s.scale);
   if (lane == 0) {
-    lse_out[R] = lse;
+    lse_out[R] = m + log2f(l);
     delta_out[R] = delta;
   }
 }
@@ -201,7 +120,8 @@ bwd_kv_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restri
               const __nv_bfloat16* __restrict__ V, const __nv_bfloat16* __restrict__ dO,
               const float* __restrict__ lse, const float* __restrict__ delta,
               const int32_t* __restrict__ lists, const int32_t* __restrict__ offsets,
-              const int32_t* __restrict__ counts, __nv_bfloat16* __restrict__ dK,
+              const int32_t* __restrict__ counts, const int32_t* __restrict__ idx,
+              float* __restrict__ dq_part, __nv_bfloat16* __restrict__ dK,
               __nv_bfloat16* __restrict__ dV, Shape s) {
   constexpr int D = DPL * 32;
   extern __shared__ float smem_f[];
@@ -216,7 +136,8 @@ bwd_kv_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restri
   float* gb = qb + kBwdBatch * D;                  // kBwdBatch x D
   float* pb = gb + kBwdBatch * D;                  // kBwdBatch x bs
   float* db = pb + kBwdBatch * bs;                 // kBwdBatch x bs
-  int32_t* lst = reinterpret_cast<int32_t*>(db + kBwdBatch * bs);   // kBwdSortCap
+  int32_t* slot_s = reinterpret_cast<int32_t*>(db + kBwdBatch * bs);   // kBwdBatch
+  int32_t* lst = slot_s + kBwdBatch;                                    // kBwdSortCap
   const int64_t blk0 = (int64_t)u * s.N + (int64_t)j * bs;
   for (int e = t; e < bs * D; e += kBwdKvThreads) {
     const int r = e / D, d = e % D;
@@ -268,6 +189,15 @@ bwd_kv_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restri
     __syncwarp();
     const float ls = row >= 0 ? lse[(int64_t)u * s.N + row] : 0.f;
     const float dl = row >= 0 ? delta[(int64_t)u * s.N + row] : 0.f;
+    // The slot of this block in the row's selection: where its dQ share goes.
+    int slot = -1;
+    for (int q0 = 0; q0 < s.k; q0 += 32) {
+      const int q = q0 + lane;
+      const bool hit = row >= 0 && q < s.k && idx[((int64_t)u * s.N + row) * s.k + q] == j;
+      const unsigned bits = __ballot_sync(0xffffffffu, hit);
+      if (slot < 0 && bits != 0u) slot = q0 + __ffs(bits) - 1;
+    }
+    if (lane == 0) slot_s[warp] = row >= 0 ? slot : -1;
     for (int r = lane; r < bs; r += 32) {
       float p = 0.f, ds = 0.f;
       if (row >= 0 && (!s.causal || j * bs + r <= row)) {
@@ -299,6 +229,17 @@ bwd_kv_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restri
         }
       }
     }
+    // Each row's dQ share from this block, sum_r ds[r] K[r] (scaled later),
+    // into the row's slot.
+    for (int o = t; o < kBwdBatch * D; o += kBwdKvThreads) {
+      const int w = o / D, d = o % D;
+      const int sl = slot_s[w];
+      if (sl < 0) continue;
+      float acc = 0.f;
+      for (int r = 0; r < bs; ++r) acc = fmaf(db[w * bs + r], Kb[r * (D + 1) + d], acc);
+      const int row = sorted ? lst[b0 + w] : lg[b0 + w];
+      dq_part[(((int64_t)u * s.N + row) * s.k + sl) * D + d] = acc;
+    }
     __syncthreads();
   }
 #pragma unroll
@@ -312,6 +253,32 @@ bwd_kv_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restri
   }
 }
 
+// dQ of each row: the sum of its slots' shares (slots in order), scaled.
+// D / 4 threads per row, four columns each.
+__global__ void __launch_bounds__(256)
+bwd_dq_kernel(const float* __restrict__ dq_part, const int32_t* __restrict__ idx,
+              __nv_bfloat16* __restrict__ dQ, Shape s) {
+  const int ch = s.D / 4;
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t R = g / ch;
+  if (R >= (int64_t)s.units * s.N) return;
+  const int c = (int)(g % ch);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int q = 0; q < s.k; ++q) {
+    if (idx[R * s.k + q] < 0) continue;
+    const float4 v = reinterpret_cast<const float4*>(dq_part + (R * s.k + q) * s.D)[c];
+    acc.x += v.x;
+    acc.y += v.y;
+    acc.z += v.z;
+    acc.w += v.w;
+  }
+  __nv_bfloat16* o = dQ + R * s.D + 4 * c;
+  o[0] = __float2bfloat16(acc.x * s.scale);
+  o[1] = __float2bfloat16(acc.y * s.scale);
+  o[2] = __float2bfloat16(acc.z * s.scale);
+  o[3] = __float2bfloat16(acc.w * s.scale);
+}
+
 bool backward_supported(const Shape& s) {
   return (s.D == 32 || s.D == 64 || s.D == 96 || s.D == 128) && s.bs * s.D <= 8192 &&
          s.k <= 64 && s.nb <= 16384 && (int64_t)s.units * s.N * s.k < (1LL << 31);
@@ -320,74 +287,74 @@ bool backward_supported(const Shape& s) {
 static size_t bwd_kv_smem(const Shape& s) {
   return sizeof(float) * (2 * (size_t)s.bs * (s.D + 1) + 2 * (size_t)kBwdBatch * s.D +
                           2 * (size_t)kBwdBatch * s.bs) +
-         sizeof(int32_t) * kBwdSortCap;
+         sizeof(int32_t) * (kBwdBatch + kBwdSortCap);
 }
+
+// Workspace: the fine stage's (bucket lists), then per row its log-sum-exp
+// and delta, then per (row, slot) the dQ share (fp32).
+static size_t a256b(size_t x) { return (x + 255) & ~(size_t)255; }
 
 size_t backward_workspace_bytes(const Shape& s) {
   const size_t rows = (size_t)s.units * s.N;
-  return fine_kv_workspace_bytes(s) + ((2 * rows * sizeof(float) + 255) & ~(size_t)255);
+  return fine_kv_workspace_bytes(s) + a256b(2 * rows * sizeof(float)) +
+         a256b(rows * s.k * s.D * sizeof(float));
 }
 
 template <int DPL, int EPT>
 static cudaError_t launch_bwd_kv(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                                  const __nv_bfloat16* V, const __nv_bfloat16* dO,
                                  const float* lse, const float* delta, const BucketLists& bl,
-                                 __nv_bfloat16* dK, __nv_bfloat16* dV, const Shape& s,
-                                 cudaStream_t st) {
+                                 const int32_t* idx, float* dq_part, __nv_bfloat16* dK,
+                                 __nv_bfloat16* dV, const Shape& s, cudaStream_t st) {
   const size_t smem = bwd_kv_smem(s);
   cudaError_t e = cudaFuncSetAttribute(bwd_kv_kernel<DPL, EPT>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   bwd_kv_kernel<DPL, EPT><<<dim3(s.nb, s.units), kBwdKvThreads, smem, st>>>(
-      Q, K, V, dO, lse, delta, bl.lists, bl.offsets, bl.counts, dK, dV, s);
+      Q, K, V, dO, lse, delta, bl.lists, bl.offsets, bl.counts, idx, dq_part, dK, dV, s);
   return cudaGetLastError();
 }
 
 template <int DPL>
 static cudaError_t launch_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
-                              const __nv_bfloat16* V, const __nv_bfloat16* dO,
-                              const int32_t* idx, __nv_bfloat16* dQ, __nv_bfloat16* dK,
-                              __nv_bfloat16* dV, unsigned char* ws, const Shape& s,
-                              cudaStream_t st) {
+                              const __nv_bfloat16* V, const __nv_bfloat16* O,
+                              const __nv_bfloat16* dO, const int32_t* idx, __nv_bfloat16* dQ,
+                              __nv_bfloat16* dK, __nv_bfloat16* dV, unsigned char* ws,
+                              const Shape& s, cudaStream_t st) {
+  const size_t rows = (size_t)s.units * s.N;
   float* lse = reinterpret_cast<float*>(ws + fine_kv_workspace_bytes(s));
-  float* delta = lse + (size_t)s.units * s.N;
+  float* delta = lse + rows;
+  float* dq_part = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(lse) +
+                                            a256b(2 * rows * sizeof(float)));
   dim3 g1((s.N + kBwdRowsWarps - 1) / kBwdRowsWarps, s.units);
-  // Cached scores and dP: 8 warps x 2 x k * bs floats (64 KiB at k * bs = 1024).
-  const size_t cache = sizeof(float) * kBwdRowsWarps * 2 * (size_t)s.k * s.bs;
-  cudaError_t e;
-  if (cache <= 96 * 1024) {
-    if ((e = cudaFuncSetAttribute(bwd_rows_kernel<DPL, true>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cache)) !=
-        cudaSuccess)
-      return e;
-    bwd_rows_kernel<DPL, true><<<g1, kBwdRowsWarps * 32, cache, st>>>(Q, K, V, dO, idx, dQ, lse,
-                                                                      delta, s);
-  } else {
-    bwd_rows_kernel<DPL, false><<<g1, kBwdRowsWarps * 32, 0, st>>>(Q, K, V, dO, idx, dQ, lse,
-                                                                   delta, s);
-  }
-  e = cudaGetLastError();
+  bwd_lse_kernel<DPL><<<g1, kBwdRowsWarps * 32, 0, st>>>(Q, K, O, dO, idx, lse, delta, s);
+  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   BucketLists bl;
   if ((e = launch_bucket_lists(idx, V, ws, s, st, &bl)) != cudaSuccess) return e;
   const int elems = s.bs * s.D;
-  if (elems <= 256) return launch_bwd_kv<DPL, 1>(Q, K, V, dO, lse, delta, bl, dK, dV, s, st);
-  if (elems <= 512) return launch_bwd_kv<DPL, 2>(Q, K, V, dO, lse, delta, bl, dK, dV, s, st);
-  if (elems <= 1024) return launch_bwd_kv<DPL, 4>(Q, K, V, dO, lse, delta, bl, dK, dV, s, st);
-  if (elems <= 2048) return launch_bwd_kv<DPL, 8>(Q, K, V, dO, lse, delta, bl, dK, dV, s, st);
-  if (elems <= 4096) return launch_bwd_kv<DPL, 16>(Q, K, V, dO, lse, delta, bl, dK, dV, s, st);
-  return launch_bwd_kv<DPL, 32>(Q, K, V, dO, lse, delta, bl, dK, dV, s, st);
+  if (elems <= 256) e = launch_bwd_kv<DPL, 1>(Q, K, V, dO, lse, delta, bl, idx, dq_part, dK, dV, s, st);
+  else if (elems <= 512) e = launch_bwd_kv<DPL, 2>(Q, K, V, dO, lse, delta, bl, idx, dq_part, dK, dV, s, st);
+  else if (elems <= 1024) e = launch_bwd_kv<DPL, 4>(Q, K, V, dO, lse, delta, bl, idx, dq_part, dK, dV, s, st);
+  else if (elems <= 2048) e = launch_bwd_kv<DPL, 8>(Q, K, V, dO, lse, delta, bl, idx, dq_part, dK, dV, s, st);
+  else if (elems <= 4096) e = launch_bwd_kv<DPL, 16>(Q, K, V, dO, lse, delta, bl, idx, dq_part, dK, dV, s, st);
+  else e = launch_bwd_kv<DPL, 32>(Q, K, V, dO, lse, delta, bl, idx, dq_part, dK, dV, s, st);
+  if (e != cudaSuccess) return e;
+  const int64_t threads = (int64_t)rows * (s.D / 4);
+  bwd_dq_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(dq_part, idx, dQ, s);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_backward(const __nv_bfloat16* Q, const __nv_bfloat16* K,
-                            const __nv_bfloat16* V, const __nv_bfloat16* dO, const int32_t* idx,
-                            __nv_bfloat16* dQ, __nv_bfloat16* dK, __nv_bfloat16* dV,
-                            unsigned char* ws, const Shape& s, cudaStream_t st) {
+                            const __nv_bfloat16* V, const __nv_bfloat16* O,
+                            const __nv_bfloat16* dO, const int32_t* idx, __nv_bfloat16* dQ,
+                            __nv_bfloat16* dK, __nv_bfloat16* dV, unsigned char* ws,
+                            const Shape& s, cudaStream_t st) {
   switch (s.D) {
-    case 32: return launch_bwd<1>(Q, K, V, dO, idx, dQ, dK, dV, ws, s, st);
-    case 64: return launch_bwd<2>(Q, K, V, dO, idx, dQ, dK, dV, ws, s, st);
-    case 96: return launch_bwd<3>(Q, K, V, dO, idx, dQ, dK, dV, ws, s, st);
-    case 128: return launch_bwd<4>(Q, K, V, dO, idx, dQ, dK, dV, ws, s, st);
+    case 32: return launch_bwd<1>(Q, K, V, O, dO, idx, dQ, dK, dV, ws, s, st);
+    case 64: return launch_bwd<2>(Q, K, V, O, dO, idx, dQ, dK, dV, ws, s, st);
+    case 96: return launch_bwd<3>(Q, K, V, O, dO, idx, dQ, dK, dV, ws, s, st);
+    case 128: return launch_bwd<4>(Q, K, V, O, dO, idx, dQ, dK, dV, ws, s, st);
     default: return cudaErrorNotSupported;
   }
 }

@@ -51,9 +51,10 @@ cudaError_t launch_bucket_lists(const int32_t* idx, const __nv_bfloat16* V, unsi
 bool backward_supported(const Shape& s);
 size_t backward_workspace_bytes(const Shape& s);
 cudaError_t launch_backward(const __nv_bfloat16* Q, const __nv_bfloat16* K,
-                            const __nv_bfloat16* V, const __nv_bfloat16* dO, const int32_t* idx,
-                            __nv_bfloat16* dQ, __nv_bfloat16* dK, __nv_bfloat16* dV,
-                            unsigned char* ws, const Shape& s, cudaStream_t st);
+                            const __nv_bfloat16* V, const __nv_bfloat16* O,
+                            const __nv_bfloat16* dO, const int32_t* idx, __nv_bfloat16* dQ,
+                            __nv_bfloat16* dK, __nv_bfloat16* dV, unsigned char* ws,
+                            const Shape& s, cudaStream_t st);
 
 // Query-stationary fine kernel for query tiles (fine_q.cu): the shapes it
 // covers, the union limit for a tile under `flags` (0: none), tiles per

@@ -220,13 +220,14 @@ int bsa_fine(const bsa_problem* p, const void* Q, const void* K, const void* V,
  * it, including per-head budgets), the selection held fixed -- what torch
  * autograd gives the reference's differentiable variant, where the top-k
  * indices (block_indexer.py:53) carry no gradient and Q, K, V receive the
- * fine stage's (block_indexer.py:55-84).  CUDA cores; the result does not
- * depend on the order of the GPU's work (no atomics).  head_dim 32, 64, 96
- * or 128, block_size * head_dim <= 8192 (BSA_ERR_UNSUPPORTED otherwise). */
+ * fine stage's (block_indexer.py:55-84).  O: the forward's output (for
+ * dO . O per row).  CUDA cores; the result does not depend on the order of
+ * the GPU's work (no atomics).  head_dim 32, 64, 96 or 128, block_size *
+ * head_dim <= 8192 (BSA_ERR_UNSUPPORTED otherwise). */
 size_t bsa_backward_workspace_bytes(const bsa_problem* p);
 int bsa_backward(const bsa_problem* p, const void* Q, const void* K, const void* V,
-                 const void* dO, const int32_t* idx, void* dQ, void* dK, void* dV,
-                 void* workspace, size_t workspace_bytes, void* stream);
+                 const void* O, const void* dO, const int32_t* idx, void* dQ, void* dK,
+                 void* dV, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Bytes of workspace bsa_fine needs for all units at once. */
 size_t bsa_fine_workspace_bytes(const bsa_problem* p);

@@ -52,7 +52,9 @@ def test_backward_matches_oracle(cuda, shape):
     Q, K, V, dO = rand_inputs(B, H, N, D, seed=21)
     Qg, Kg, Vg, dOg = to_gpu(Q, K, V, dO)
     idx = bi.select_blocks(Qg, Kg, causal=causal, block_size=bs, top_k=k)
-    dQ, dK, dV = (t.float().cpu().numpy() for t in bi.backward(Qg, Kg, Vg, dOg, idx, causal, bs))
+    Og = bi.fine(Qg, Kg, Vg, idx, causal=causal, block_size=bs)
+    dQ, dK, dV = (t.float().cpu().numpy()
+                  for t in bi.backward(Qg, Kg, Vg, Og, dOg, idx, causal, bs))
     idx = idx.cpu().numpy()
     for b in range(B):
         for h in range(H):
@@ -66,8 +68,9 @@ def test_backward_matches_oracle(cuda, shape):
 def test_backward_is_deterministic(cuda):
     Q, K, V, dO = to_gpu(*rand_inputs(1, 2, 2048, 64, seed=22))
     idx = bi.select_blocks(Q, K, causal=True)
-    a = bi.backward(Q, K, V, dO, idx, True)
-    b = bi.backward(Q, K, V, dO, idx, True)
+    O = bi.fine(Q, K, V, idx, causal=True)
+    a = bi.backward(Q, K, V, O, dO, idx, True)
+    b = bi.backward(Q, K, V, O, dO, idx, True)
     assert all(torch.equal(x, y) for x, y in zip(a, b))
 
 
@@ -82,7 +85,7 @@ def test_autograd_function(cuda, top_k):
     assert torch.equal(out, bi.attention(Q, K, V, causal=True, top_k=top_k))
     out.backward(dO)
     idx = bi.select_blocks(Q, K, causal=True, top_k=top_k)
-    dQ, dK, dV = bi.backward(Q, K, V, dO, idx, True)
+    dQ, dK, dV = bi.backward(Q, K, V, out.detach(), dO, idx, True)
     assert torch.equal(Qr.grad, dQ) and torch.equal(Kr.grad, dK) and torch.equal(Vr.grad, dV)
 
 
@@ -92,7 +95,9 @@ def test_per_head_budgets_backward(cuda):
     Q, K, V, dO = rand_inputs(B, H, N, D, seed=24)
     Qg, Kg, Vg, dOg = to_gpu(Q, K, V, dO)
     idx = bi.select_blocks(Qg, Kg, causal=True, block_size=bs, top_k=ks)
-    dQ, dK, dV = (t.float().cpu().numpy() for t in bi.backward(Qg, Kg, Vg, dOg, idx, True, bs))
+    Og = bi.fine(Qg, Kg, Vg, idx, causal=True, block_size=bs)
+    dQ, dK, dV = (t.float().cpu().numpy()
+                  for t in bi.backward(Qg, Kg, Vg, Og, dOg, idx, True, bs))
     idx = idx.cpu().numpy()
     for h in range(H):
         wq, wk, wv = backward_unit(Q[0, h], K[0, h], V[0, h], dO[0, h], True, bs, max(ks),
