@@ -300,6 +300,7 @@ select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
         // groups are non-empty).
         if (pass == 0 && w == nw - 1) {
           if constexpr (kG64) sel.raise_floor(kth_of_64(gm, gm2, ku));
+          else if (ku == 16) sel.raise_floor(kth16_of_32(gm));
           else if (ku <= 32) sel.raise_floor(kth_of_32(gm, ku));
         }
       }

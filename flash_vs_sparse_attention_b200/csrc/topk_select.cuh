@@ -22,6 +22,25 @@
 
 namespace bsa {
 
+// Bitonic sort of 32 values, descending, in registers.
+__device__ __forceinline__ void sort32_desc(float (&v)[32]) {
+#pragma unroll
+  for (int k2 = 2; k2 <= 32; k2 <<= 1) {
+#pragma unroll
+    for (int j = k2 >> 1; j > 0; j >>= 1) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int l = i ^ j;
+        if (l > i) {
+          const float a = v[i], b = v[l];
+          const float hi = fmaxf(a, b), lo = fminf(a, b);
+          if ((i & k2) == 0) { v[i] = hi; v[l] = lo; } else { v[i] = lo; v[l] = hi; }
+        }
+      }
+    }
+  }
+}
+
 template <int KCAP>
 struct RowTopK {
   uint2* buf;         // this thread's column: buf[slot * stride]
@@ -103,8 +122,25 @@ struct RowTopK {
   // Exact k-th largest value of the buffer: the KCAP largest values kept
   // in descending registers.  Inserting x sets a[p] = max(a[p], min(a[p-1],
   // x)) from the old a[p-1] (a[0] = max(a[0], x)): 2 ops per cell, and no
-  // cell waits for another, so an entry's update is two ops deep.
+  // cell waits for another, so an entry's update is two ops deep.  A buffer
+  // of at most 32 entries is sorted instead (a 32-value bitonic network,
+  // 480 min/max, fewer than the insertions once it holds ~16 entries).
   __device__ __forceinline__ float kth_value(int* n_gt_out) const {
+    if (cnt <= 32) {
+      float v[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        v[e] = e < cnt ? __uint_as_float(buf[e * stride].x) : -INFINITY;
+      sort32_desc(v);
+      float T = INFINITY;
+      int n_gt = 0;
+#pragma unroll
+      for (int p = 0; p < 32; ++p) T = fminf(T, p < k ? v[p] : INFINITY);
+#pragma unroll
+      for (int p = 0; p < 32; ++p) n_gt += (p < k && v[p] > T) ? 1 : 0;
+      *n_gt_out = n_gt;
+      return T;
+    }
     float a[KCAP];
 #pragma unroll
     for (int p = 0; p < KCAP; ++p) a[p] = -INFINITY;
@@ -176,6 +212,34 @@ struct RowTopK {
 // two 32-candidate chunks between compactions.
 __host__ __device__ constexpr int topk_buffer_slots(int kcap) {
   return kcap <= 32 ? 2 * kcap + 32 : kcap + 64;
+}
+
+// 16th largest of 32 values: the halves sorted in opposite directions (two
+// 16-value bitonic networks) form a bitonic sequence whose pairwise maxima
+// (i, i + 16) are its 16 largest values; their minimum.  351 min/max
+// against 496 for the whole sort.
+__device__ __forceinline__ float kth16_of_32(float (&v)[32]) {
+#pragma unroll
+  for (int k2 = 2; k2 <= 16; k2 <<= 1) {
+#pragma unroll
+    for (int j = k2 >> 1; j > 0; j >>= 1) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int l = i ^ j;
+        if (l > i) {
+          const float a = v[i], b = v[l];
+          const float hi = fmaxf(a, b), lo = fminf(a, b);
+          // the full sort's first stages: after k2 = 16 the first half is
+          // descending and the second ascending
+          if ((i & k2) == 0) { v[i] = hi; v[l] = lo; } else { v[i] = lo; v[l] = hi; }
+        }
+      }
+    }
+  }
+  float T = INFINITY;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) T = fminf(T, fmaxf(v[i], v[16 + i]));
+  return T;
 }
 
 // k-th largest of 32 values (1 <= k <= 32): bitonic sort, descending, in
