@@ -23,6 +23,7 @@ SHAPES = [
     (2, 1, 1024, 128, 64, 8, False),
     (1, 2, 1024, 96, 32, 5, True),
     (1, 1, 4096, 64, 128, 16, True),
+    (1, 1, 4096, 64, 64, 48, False),  # top_k > 32: the slot search spans two words
 ]
 
 # Gradient tolerance: bf16 inputs and outputs, fp32 accumulation; the worst
