@@ -18,9 +18,10 @@
 //  3. bwd_kv_kernel     key-stationary, a CTA per (unit, key block): its
 //                       rows, sorted ascending, 8 at a time (a warp per row
 //                       for the block's scores and dP); dK and dV of the
-//                       block summed in registers (thread t owns elements t,
-//                       t + 256, ...) and written once, and for each row the
-//                       block's share of dQ written to the row's slot.
+//                       block summed in registers (each thread a 4-row tile,
+//                       or elements t, t + 256, ...) and written once, and
+//                       for each row the block's share of dQ written to the
+//                       row's slot.
 //  4. bwd_dq_kernel     per row, the sum of its slots' dQ shares.
 // No atomics: every sum runs in a fixed order (rows ascending, slots
 // ascending), so the result is the same on every run.
@@ -114,6 +115,12 @@ bwd_lse_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restr
   }
 }
 
+// Shared-memory row stride of the block's K and V (floats): a multiple of 4
+// for 16-byte loads, and 4 mod 32 so the rows of a warp's 16-byte loads fall
+// in different bank groups.
+template <int D>
+constexpr int kv_stride() { return D + 4; }
+
 template <int DPL, int EPT>   // EPT: gradient elements per thread, >= bs * D / 256
 __global__ void __launch_bounds__(kBwdKvThreads, 2)
 bwd_kv_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restrict__ K,
@@ -124,15 +131,23 @@ bwd_kv_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restri
               float* __restrict__ dq_part, __nv_bfloat16* __restrict__ dK,
               __nv_bfloat16* __restrict__ dV, Shape s) {
   constexpr int D = DPL * 32;
-  extern __shared__ float smem_f[];
+  constexpr int KS = kv_stride<D>();
+  // When bs * D is exactly 256 EPT (4096 or 8192), each thread owns a 4 x TC
+  // tile of the block's gradient (rows 4 tr.., columns TC tc..), so one
+  // 16-byte load of the weights and of the rows serves 4 TC multiply-adds;
+  // otherwise it owns elements e = t + 256 m.
+  constexpr bool kTiledEpt = (EPT == 16 || EPT == 32);
+  constexpr int TC = EPT / 4;
+  extern __shared__ float4 smem_v4[];
+  float* smem_f = reinterpret_cast<float*>(smem_v4);
   const int j = blockIdx.x, u = blockIdx.y, t = threadIdx.x;
   const int warp = t >> 5, lane = t & 31;
   const int bs = s.bs;
-  // Shared memory: K and V of the block (rows padded by one float against
-  // bank conflicts), the batch's rows of Q and dO, their weights, the list.
-  float* Kb = smem_f;                              // bs x (D + 1)
-  float* Vb = Kb + bs * (D + 1);                   // bs x (D + 1)
-  float* qb = Vb + bs * (D + 1);                   // kBwdBatch x D
+  // Shared memory: K and V of the block, the batch's rows of Q and dO, their
+  // weights, the rows' slots, the list.
+  float* Kb = smem_f;                              // bs x KS
+  float* Vb = Kb + bs * KS;                        // bs x KS
+  float* qb = Vb + bs * KS;                        // kBwdBatch x D
   float* gb = qb + kBwdBatch * D;                  // kBwdBatch x D
   float* pb = gb + kBwdBatch * D;                  // kBwdBatch x bs
   float* db = pb + kBwdBatch * bs;                 // kBwdBatch x bs
@@ -141,8 +156,8 @@ bwd_kv_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restri
   const int64_t blk0 = (int64_t)u * s.N + (int64_t)j * bs;
   for (int e = t; e < bs * D; e += kBwdKvThreads) {
     const int r = e / D, d = e % D;
-    Kb[r * (D + 1) + d] = __bfloat162float(K[(blk0 + r) * D + d]);
-    Vb[r * (D + 1) + d] = __bfloat162float(V[(blk0 + r) * D + d]);
+    Kb[r * KS + d] = __bfloat162float(K[(blk0 + r) * D + d]);
+    Vb[r * KS + d] = __bfloat162float(V[(blk0 + r) * D + d]);
   }
   const int n = counts[(int64_t)u * s.nb + j];
   const int32_t* lg = lists + (int64_t)u * s.N * s.k + offsets[(int64_t)u * s.nb + j];
@@ -174,10 +189,13 @@ bwd_kv_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restri
   float gk[EPT], gv[EPT];
 #pragma unroll
   for (int m = 0; m < EPT; ++m) gk[m] = gv[m] = 0.f;
+  const bool tiled = kTiledEpt && bs * D == kBwdKvThreads * EPT && bs % 4 == 0;
+  const int tr = tiled ? t / (D / TC) : 0, tc = tiled ? t % (D / TC) : 0;
   const float sc = s.scale * 1.4426950408889634f;
   for (int b0 = 0; b0 < n; b0 += kBwdBatch) {
-    // Warp w: row b0 + w of the list -- its Q and dO rows, then the block's
-    // weights p and p (dp - delta) for that row (zero for a missing row).
+    // Warp w: row b0 + w of the list -- its Q and dO rows, its slot, then
+    // the block's weights p and p (dp - delta) for that row (zero for a
+    // missing row).
     const int i = b0 + warp;
     const int row = i < n ? (sorted ? lst[i] : lg[i]) : -1;
     float* qw = qb + warp * D;
@@ -186,7 +204,6 @@ bwd_kv_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restri
       qw[d] = row >= 0 ? __bfloat162float(Q[((int64_t)u * s.N + row) * D + d]) : 0.f;
       gw[d] = row >= 0 ? __bfloat162float(dO[((int64_t)u * s.N + row) * D + d]) : 0.f;
     }
-    __syncwarp();
     const float ls = row >= 0 ? lse[(int64_t)u * s.N + row] : 0.f;
     const float dl = row >= 0 ? delta[(int64_t)u * s.N + row] : 0.f;
     // The slot of this block in the row's selection: where its dQ share goes.
@@ -198,16 +215,22 @@ bwd_kv_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restri
       if (slot < 0 && bits != 0u) slot = q0 + __ffs(bits) - 1;
     }
     if (lane == 0) slot_s[warp] = row >= 0 ? slot : -1;
+    __syncwarp();
     for (int r = lane; r < bs; r += 32) {
       float p = 0.f, ds = 0.f;
       if (row >= 0 && (!s.causal || j * bs + r <= row)) {
         float x = 0.f, dp = 0.f;
-        const float* kr = Kb + r * (D + 1);
-        const float* vr = Vb + r * (D + 1);
-#pragma unroll 8
-        for (int d = 0; d < D; ++d) {
-          x = fmaf(qw[d], kr[d], x);
-          dp = fmaf(gw[d], vr[d], dp);
+        const float4* kr = reinterpret_cast<const float4*>(Kb + r * KS);
+        const float4* vr = reinterpret_cast<const float4*>(Vb + r * KS);
+        const float4* q4 = reinterpret_cast<const float4*>(qw);
+        const float4* g4 = reinterpret_cast<const float4*>(gw);
+#pragma unroll 4
+        for (int c = 0; c < D / 4; ++c) {
+          const float4 kk = kr[c], vv = vr[c], qq = q4[c], gg = g4[c];
+          x = fmaf(qq.x, kk.x, x); x = fmaf(qq.y, kk.y, x);
+          x = fmaf(qq.z, kk.z, x); x = fmaf(qq.w, kk.w, x);
+          dp = fmaf(gg.x, vv.x, dp); dp = fmaf(gg.y, vv.y, dp);
+          dp = fmaf(gg.z, vv.z, dp); dp = fmaf(gg.w, vv.w, dp);
         }
         p = exp2f(x * sc - ls);
         ds = p * (dp - dl);
@@ -217,38 +240,83 @@ bwd_kv_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restri
     }
     __syncthreads();
     // dV[r][d] += p_w[r] dO_w[d], dK[r][d] += ds_w[r] Q_w[d], rows in order.
+    if (kTiledEpt && tiled) {
+#pragma unroll
+      for (int w = 0; w < kBwdBatch; ++w) {
+        const float4 p4 = *reinterpret_cast<const float4*>(pb + w * bs + 4 * tr);
+        const float4 d4 = *reinterpret_cast<const float4*>(db + w * bs + 4 * tr);
+        const float pr[4] = {p4.x, p4.y, p4.z, p4.w}, dr[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+        for (int c4 = 0; c4 < TC / 4; ++c4) {
+          const float4 g = *reinterpret_cast<const float4*>(gb + w * D + TC * tc + 4 * c4);
+          const float4 q = *reinterpret_cast<const float4*>(qb + w * D + TC * tc + 4 * c4);
+          const float gc[4] = {g.x, g.y, g.z, g.w}, qc[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int rr = 0; rr < 4; ++rr) {
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+              const int m = rr * TC + 4 * c4 + cc;
+              gv[m] = fmaf(pr[rr], gc[cc], gv[m]);
+              gk[m] = fmaf(dr[rr], qc[cc], gk[m]);
+            }
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int m = 0; m < EPT; ++m) {
+        const int e = t + m * kBwdKvThreads;
+        if (e < bs * D) {
+          const int r = e / D, d = e % D;
+#pragma unroll
+          for (int w = 0; w < kBwdBatch; ++w) {
+            gv[m] = fmaf(pb[w * bs + r], gb[w * D + d], gv[m]);
+            gk[m] = fmaf(db[w * bs + r], qb[w * D + d], gk[m]);
+          }
+        }
+      }
+    }
+    // Each row's dQ share from this block, sum_r ds[r] K[r] (scaled later),
+    // into the row's slot: warp w takes row w, each lane DPL columns.
+    {
+      const int sl = slot_s[warp];
+      if (sl >= 0) {
+        float acc[DPL];
+#pragma unroll
+        for (int c = 0; c < DPL; ++c) acc[c] = 0.f;
+        const float* dw = db + warp * bs;
+        for (int r = 0; r < bs; ++r) {
+          const float w_r = dw[r];
+#pragma unroll
+          for (int c = 0; c < DPL; ++c) acc[c] = fmaf(w_r, Kb[r * KS + lane * DPL + c], acc[c]);
+        }
+        const int rw = sorted ? lst[b0 + warp] : lg[b0 + warp];
+        float* dst = dq_part + (((int64_t)u * s.N + rw) * s.k + sl) * D + lane * DPL;
+#pragma unroll
+        for (int c = 0; c < DPL; ++c) dst[c] = acc[c];
+      }
+    }
+    __syncthreads();
+  }
+  if (kTiledEpt && tiled) {
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+#pragma unroll
+      for (int c = 0; c < TC; ++c) {
+        const int64_t o = (blk0 + 4 * tr + rr) * D + TC * tc + c;
+        dK[o] = __float2bfloat16(gk[rr * TC + c] * s.scale);
+        dV[o] = __float2bfloat16(gv[rr * TC + c]);
+      }
+    }
+  } else {
 #pragma unroll
     for (int m = 0; m < EPT; ++m) {
       const int e = t + m * kBwdKvThreads;
       if (e < bs * D) {
         const int r = e / D, d = e % D;
-#pragma unroll
-        for (int w = 0; w < kBwdBatch; ++w) {
-          gv[m] = fmaf(pb[w * bs + r], gb[w * D + d], gv[m]);
-          gk[m] = fmaf(db[w * bs + r], qb[w * D + d], gk[m]);
-        }
+        dK[(blk0 + r) * D + d] = __float2bfloat16(gk[m] * s.scale);
+        dV[(blk0 + r) * D + d] = __float2bfloat16(gv[m]);
       }
-    }
-    // Each row's dQ share from this block, sum_r ds[r] K[r] (scaled later),
-    // into the row's slot.
-    for (int o = t; o < kBwdBatch * D; o += kBwdKvThreads) {
-      const int w = o / D, d = o % D;
-      const int sl = slot_s[w];
-      if (sl < 0) continue;
-      float acc = 0.f;
-      for (int r = 0; r < bs; ++r) acc = fmaf(db[w * bs + r], Kb[r * (D + 1) + d], acc);
-      const int row = sorted ? lst[b0 + w] : lg[b0 + w];
-      dq_part[(((int64_t)u * s.N + row) * s.k + sl) * D + d] = acc;
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int m = 0; m < EPT; ++m) {
-    const int e = t + m * kBwdKvThreads;
-    if (e < bs * D) {
-      const int r = e / D, d = e % D;
-      dK[(blk0 + r) * D + d] = __float2bfloat16(gk[m] * s.scale);
-      dV[(blk0 + r) * D + d] = __float2bfloat16(gv[m]);
     }
   }
 }
@@ -285,7 +353,7 @@ bool backward_supported(const Shape& s) {
 }
 
 static size_t bwd_kv_smem(const Shape& s) {
-  return sizeof(float) * (2 * (size_t)s.bs * (s.D + 1) + 2 * (size_t)kBwdBatch * s.D +
+  return sizeof(float) * (2 * (size_t)s.bs * (s.D + 4) + 2 * (size_t)kBwdBatch * s.D +
                           2 * (size_t)kBwdBatch * s.bs) +
          sizeof(int32_t) * (kBwdBatch + kBwdSortCap);
 }
