@@ -22,6 +22,8 @@
 //                       or elements t, t + 256, ...) and written once, and
 //                       for each row the block's share of dQ written to the
 //                       row's slot.
+//                       At block_size 64 and head_dim 64 the same step runs
+//                       on tensor cores (bwd_kv_mma_kernel, mma.sync).
 //  4. bwd_dq_kernel     per row, the sum of its slots' dQ shares.
 // No atomics: every sum runs in a fixed order (rows ascending, slots
 // ascending), so the result is the same on every run.
@@ -321,6 +323,232 @@ bwd_kv_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restri
   }
 }
 
+// The per-block kernel on tensor cores (mma.sync, bf16 in, fp32 out), for
+// block_size 64 and head_dim 64: 16 rows of the block's list at a time.
+//   S = Q K^T and dP = dO V^T (16 x 64): warp w the keys 8w .. 8w + 7;
+//   P = 2^(S sc - lse), dS = P (dP - delta), rounded to bf16 as the
+//   operands of the next products;
+//   dV += P^T dO and dK += dS^T Q (64 x 64, kept in registers over the whole
+//   list): warp w the keys 16 (w / 2) .., columns 32 (w % 2) ..;
+//   dQ share = dS K (16 x 64): warp w the columns 8w .. 8w + 7.
+// The operands sit in shared memory in the layouts the fragments read
+// (rows padded to 72 or 24 elements against bank conflicts).  Rows in list
+// order and the products' fixed order: the same result on every run.
+namespace bwdmma {
+constexpr int kB = 16;          // rows per batch
+constexpr int kS64 = 72;        // row stride of 64-wide arrays (bf16)
+constexpr int kS16 = 24;        // row stride of 16-wide arrays (bf16)
+__device__ __forceinline__ uint32_t ld32(const __nv_bfloat16* p) {
+  return *reinterpret_cast<const uint32_t*>(p);
+}
+__device__ __forceinline__ void mma(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                    uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+}  // namespace bwdmma
+
+__global__ void __launch_bounds__(kBwdKvThreads, 2)
+bwd_kv_mma_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restrict__ K,
+                  const __nv_bfloat16* __restrict__ V, const __nv_bfloat16* __restrict__ dO,
+                  const float* __restrict__ lse, const float* __restrict__ delta,
+                  const int32_t* __restrict__ lists, const int32_t* __restrict__ offsets,
+                  const int32_t* __restrict__ counts, const int32_t* __restrict__ idx,
+                  float* __restrict__ dq_part, __nv_bfloat16* __restrict__ dK,
+                  __nv_bfloat16* __restrict__ dV, Shape s) {
+  using namespace bwdmma;
+  constexpr int D = 64, BS = 64;
+  extern __shared__ float4 smem_v4[];
+  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(smem_v4);   // [key][d]
+  __nv_bfloat16* KTs = Ks + BS * kS64;                              // [d][key]
+  __nv_bfloat16* Vs = KTs + D * kS64;                               // [key][d]
+  __nv_bfloat16* Qb = Vs + BS * kS64;                               // [row][d]
+  __nv_bfloat16* Gb = Qb + kB * kS64;                               // [row][d]  (dO)
+  __nv_bfloat16* DSr = Gb + kB * kS64;                              // [row][key]
+  __nv_bfloat16* QT = DSr + kB * kS64;                              // [d][row]
+  __nv_bfloat16* GT = QT + D * kS16;                                // [d][row]
+  __nv_bfloat16* PT = GT + D * kS16;                                // [key][row]
+  __nv_bfloat16* DST = PT + BS * kS16;                              // [key][row]
+  float* ls_s = reinterpret_cast<float*>(DST + BS * kS16);          // [kB]
+  float* dl_s = ls_s + kB;
+  int32_t* row_s = reinterpret_cast<int32_t*>(dl_s + kB);
+  int32_t* slot_s = row_s + kB;
+  int32_t* lst = slot_s + kB;                                       // kBwdSortCap
+  const int j = blockIdx.x, u = blockIdx.y, t = threadIdx.x;
+  const int warp = t >> 5, lane = t & 31, g = lane >> 2, q4 = lane & 3;
+  const int64_t blk0 = (int64_t)u * s.N + (int64_t)j * BS;
+  for (int e = t; e < BS * D / 2; e += kBwdKvThreads) {
+    const int r = (2 * e) / D, d = (2 * e) % D;
+    const __nv_bfloat162 kk = *reinterpret_cast<const __nv_bfloat162*>(K + (blk0 + r) * D + d);
+    const __nv_bfloat162 vv = *reinterpret_cast<const __nv_bfloat162*>(V + (blk0 + r) * D + d);
+    *reinterpret_cast<__nv_bfloat162*>(Ks + r * kS64 + d) = kk;
+    *reinterpret_cast<__nv_bfloat162*>(Vs + r * kS64 + d) = vv;
+    KTs[d * kS64 + r] = kk.x;
+    KTs[(d + 1) * kS64 + r] = kk.y;
+  }
+  const int n = counts[(int64_t)u * s.nb + j];
+  const int32_t* lg = lists + (int64_t)u * s.N * s.k + offsets[(int64_t)u * s.nb + j];
+  const bool sorted = n <= kBwdSortCap;
+  if (sorted) {
+    int n2 = 1;
+    while (n2 < n) n2 <<= 1;
+    for (int i = t; i < n2; i += kBwdKvThreads) lst[i] = i < n ? lg[i] : 0x7fffffff;
+    __syncthreads();
+    for (int k2 = 2; k2 <= n2; k2 <<= 1) {
+      for (int h = k2 >> 1; h > 0; h >>= 1) {
+        for (int i = t; i < n2; i += kBwdKvThreads) {
+          const int l = i ^ h;
+          if (l > i) {
+            const int a = lst[i], b = lst[l];
+            const bool up = (i & k2) == 0;
+            if ((a > b) == up) {
+              lst[i] = b;
+              lst[l] = a;
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
+  }
+  __syncthreads();
+  const float sc = s.scale * 1.4426950408889634f;
+  const int mt = warp >> 1, nh = warp & 1;   // dK/dV tile of this warp
+  float accV[4][4], accK[4][4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) accV[a][c] = accK[a][c] = 0.f;
+  for (int b0 = 0; b0 < n; b0 += kB) {
+    // Rows 2w and 2w + 1 of the batch: Q and dO in both layouts,
+    // log-sum-exp, delta and the slot of this block (-1 for a missing row).
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = 2 * warp + h;
+      const int i = b0 + r;
+      const int row = i < n ? (sorted ? lst[i] : lg[i]) : -1;
+      const int64_t R = (int64_t)u * s.N + (row >= 0 ? row : 0);
+      __nv_bfloat162 qq = __floats2bfloat162_rn(0.f, 0.f), gg = qq;
+      if (row >= 0) {
+        qq = *reinterpret_cast<const __nv_bfloat162*>(Q + R * D + 2 * lane);
+        gg = *reinterpret_cast<const __nv_bfloat162*>(dO + R * D + 2 * lane);
+      }
+      *reinterpret_cast<__nv_bfloat162*>(Qb + r * kS64 + 2 * lane) = qq;
+      *reinterpret_cast<__nv_bfloat162*>(Gb + r * kS64 + 2 * lane) = gg;
+      QT[(2 * lane) * kS16 + r] = qq.x;
+      QT[(2 * lane + 1) * kS16 + r] = qq.y;
+      GT[(2 * lane) * kS16 + r] = gg.x;
+      GT[(2 * lane + 1) * kS16 + r] = gg.y;
+      int slot = -1;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int q = lane + 32 * hh;
+        const bool hit = row >= 0 && q < s.k && idx[R * s.k + q] == j;
+        const unsigned bits = __ballot_sync(0xffffffffu, hit);
+        if (slot < 0 && bits != 0u) slot = 32 * hh + __ffs(bits) - 1;
+      }
+      if (lane == 0) {
+        row_s[r] = row;
+        slot_s[r] = row >= 0 ? slot : -1;
+        ls_s[r] = row >= 0 ? lse[R] : 0.f;
+        dl_s[r] = row >= 0 ? delta[R] : 0.f;
+      }
+    }
+    __syncthreads();
+    // S and dP for keys 8w .. 8w + 7.
+    {
+      float sacc[4] = {0.f, 0.f, 0.f, 0.f}, pacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const int c0 = 16 * ks + 2 * q4;
+        const uint32_t a0 = ld32(Qb + g * kS64 + c0), a1 = ld32(Qb + (g + 8) * kS64 + c0);
+        const uint32_t a2 = ld32(Qb + g * kS64 + c0 + 8), a3 = ld32(Qb + (g + 8) * kS64 + c0 + 8);
+        mma(sacc, a0, a1, a2, a3, ld32(Ks + (8 * warp + g) * kS64 + c0),
+            ld32(Ks + (8 * warp + g) * kS64 + c0 + 8));
+        const uint32_t e0 = ld32(Gb + g * kS64 + c0), e1 = ld32(Gb + (g + 8) * kS64 + c0);
+        const uint32_t e2 = ld32(Gb + g * kS64 + c0 + 8), e3 = ld32(Gb + (g + 8) * kS64 + c0 + 8);
+        mma(pacc, e0, e1, e2, e3, ld32(Vs + (8 * warp + g) * kS64 + c0),
+            ld32(Vs + (8 * warp + g) * kS64 + c0 + 8));
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int r = g + 8 * (c >> 1), key = 8 * warp + 2 * q4 + (c & 1);
+        const int row = row_s[r];
+        float p = 0.f, ds = 0.f;
+        if (row >= 0 && (!s.causal || j * BS + key <= row)) {
+          p = exp2f(sacc[c] * sc - ls_s[r]);
+          ds = p * (pacc[c] - dl_s[r]);
+        }
+        const __nv_bfloat16 pb = __float2bfloat16(p), db = __float2bfloat16(ds);
+        PT[key * kS16 + r] = pb;
+        DST[key * kS16 + r] = db;
+        DSr[r * kS64 + key] = db;
+      }
+    }
+    __syncthreads();
+    // dV += P^T dO, dK += dS^T Q over this batch's 16 rows.
+    {
+      const int k0 = 2 * q4;
+      const __nv_bfloat16* pa = PT + (16 * mt) * kS16;
+      const __nv_bfloat16* da = DST + (16 * mt) * kS16;
+      const uint32_t p0 = ld32(pa + g * kS16 + k0), p1 = ld32(pa + (g + 8) * kS16 + k0);
+      const uint32_t p2 = ld32(pa + g * kS16 + k0 + 8), p3 = ld32(pa + (g + 8) * kS16 + k0 + 8);
+      const uint32_t d0 = ld32(da + g * kS16 + k0), d1 = ld32(da + (g + 8) * kS16 + k0);
+      const uint32_t d2 = ld32(da + g * kS16 + k0 + 8), d3 = ld32(da + (g + 8) * kS16 + k0 + 8);
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        const int nt = 4 * nh + a;
+        mma(accV[a], p0, p1, p2, p3, ld32(GT + (8 * nt + g) * kS16 + k0),
+            ld32(GT + (8 * nt + g) * kS16 + k0 + 8));
+        mma(accK[a], d0, d1, d2, d3, ld32(QT + (8 * nt + g) * kS16 + k0),
+            ld32(QT + (8 * nt + g) * kS16 + k0 + 8));
+      }
+    }
+    // This block's dQ share of each row, columns 8w .. 8w + 7, into its slot.
+    {
+      float qacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ks = 0; ks < BS / 16; ++ks) {
+        const int c0 = 16 * ks + 2 * q4;
+        mma(qacc, ld32(DSr + g * kS64 + c0), ld32(DSr + (g + 8) * kS64 + c0),
+            ld32(DSr + g * kS64 + c0 + 8), ld32(DSr + (g + 8) * kS64 + c0 + 8),
+            ld32(KTs + (8 * warp + g) * kS64 + c0), ld32(KTs + (8 * warp + g) * kS64 + c0 + 8));
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int r = g + 8 * h;
+        const int sl = slot_s[r];
+        if (sl >= 0) {
+          float* dst = dq_part + (((int64_t)u * s.N + row_s[r]) * s.k + sl) * D + 8 * warp + 2 * q4;
+          *reinterpret_cast<float2*>(dst) = make_float2(qacc[2 * h], qacc[2 * h + 1]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int col = 8 * (4 * nh + a) + 2 * q4;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int64_t o = (blk0 + 16 * mt + g + 8 * h) * D + col;
+      *reinterpret_cast<__nv_bfloat162*>(dK + o) =
+          __floats2bfloat162_rn(accK[a][2 * h] * s.scale, accK[a][2 * h + 1] * s.scale);
+      *reinterpret_cast<__nv_bfloat162*>(dV + o) =
+          __floats2bfloat162_rn(accV[a][2 * h], accV[a][2 * h + 1]);
+    }
+  }
+}
+
+static size_t bwd_kv_mma_smem() {
+  using namespace bwdmma;
+  return sizeof(__nv_bfloat16) * (3 * 64 * kS64 + 3 * kB * kS64 + 4 * 64 * kS16) +
+         sizeof(float) * 2 * kB + sizeof(int32_t) * (2 * kB + kBwdSortCap);
+}
+
 // dQ of each row: the sum of its slots' shares (slots in order), scaled.
 // D / 4 threads per row, four columns each.
 __global__ void __launch_bounds__(256)
@@ -401,7 +629,15 @@ static cudaError_t launch_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
   BucketLists bl;
   if ((e = launch_bucket_lists(idx, V, ws, s, st, &bl)) != cudaSuccess) return e;
   const int elems = s.bs * s.D;
-  if (elems <= 256) e = launch_bwd_kv<DPL, 1>(Q, K, V, dO, lse, delta, bl, idx, dq_part, dK, dV, s, st);
+  if (s.bs == 64 && s.D == 64) {
+    const size_t smem = bwd_kv_mma_smem();
+    if ((e = cudaFuncSetAttribute(bwd_kv_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem)) != cudaSuccess)
+      return e;
+    bwd_kv_mma_kernel<<<dim3(s.nb, s.units), kBwdKvThreads, smem, st>>>(
+        Q, K, V, dO, lse, delta, bl.lists, bl.offsets, bl.counts, idx, dq_part, dK, dV, s);
+    e = cudaGetLastError();
+  } else if (elems <= 256) e = launch_bwd_kv<DPL, 1>(Q, K, V, dO, lse, delta, bl, idx, dq_part, dK, dV, s, st);
   else if (elems <= 512) e = launch_bwd_kv<DPL, 2>(Q, K, V, dO, lse, delta, bl, idx, dq_part, dK, dV, s, st);
   else if (elems <= 1024) e = launch_bwd_kv<DPL, 4>(Q, K, V, dO, lse, delta, bl, idx, dq_part, dK, dV, s, st);
   else if (elems <= 2048) e = launch_bwd_kv<DPL, 8>(Q, K, V, dO, lse, delta, bl, idx, dq_part, dK, dV, s, st);
