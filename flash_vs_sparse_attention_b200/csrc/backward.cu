@@ -23,7 +23,11 @@
 //                       for each row the block's share of dQ written to the
 //                       row's slot.
 //                       At block_size 64 and head_dim 64 the same step runs
-//                       on tensor cores (bwd_kv_mma_kernel, mma.sync).
+//                       on tensor cores (bwd_kv_mma_kernel, mma.sync), and
+//                       step 1 is replaced by a key-block pass
+//                       (bwd_lse_mma_kernel: each row's per-block share of
+//                       its normaliser) and a per-row merge
+//                       (bwd_lse_merge_kernel).
 //  4. bwd_dq_kernel     per row, the sum of its slots' dQ shares.
 // No atomics: every sum runs in a fixed order (rows ascending, slots
 // ascending), so the result is the same on every run.
@@ -543,6 +547,142 @@ bwd_kv_mma_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __re
   }
 }
 
+// Log-sum-exp on the key-block side (block_size 64, head_dim 64): per
+// (unit, key block), for every row of its list, the block's share of the
+// row's softmax normaliser -- the maximum m of its 64 scores (base 2) and
+// l = sum 2^(x - m) -- into the row's slot; S = Q K^T on tensor cores as in
+// bwd_kv_mma_kernel.  bwd_lse_merge_kernel then merges a row's shares.  Each
+// share is written once, so the list's order does not matter here.
+__global__ void __launch_bounds__(kBwdKvThreads, 2)
+bwd_lse_mma_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restrict__ K,
+                   const int32_t* __restrict__ lists, const int32_t* __restrict__ offsets,
+                   const int32_t* __restrict__ counts, const int32_t* __restrict__ idx,
+                   float2* __restrict__ ml_part, Shape s) {
+  using namespace bwdmma;
+  constexpr int D = 64, BS = 64;
+  __shared__ __align__(16) __nv_bfloat16 Ks[BS * kS64], Qb[kB * kS64];
+  __shared__ float wm[8 * kB], wl[8 * kB];
+  __shared__ int32_t row_s[kB], slot_s[kB];
+  const int j = blockIdx.x, u = blockIdx.y, t = threadIdx.x;
+  const int warp = t >> 5, lane = t & 31, g = lane >> 2, q4 = lane & 3;
+  const int64_t blk0 = (int64_t)u * s.N + (int64_t)j * BS;
+  for (int e = t; e < BS * D / 2; e += kBwdKvThreads) {
+    const int r = (2 * e) / D, d = (2 * e) % D;
+    *reinterpret_cast<__nv_bfloat162*>(Ks + r * kS64 + d) =
+        *reinterpret_cast<const __nv_bfloat162*>(K + (blk0 + r) * D + d);
+  }
+  const int n = counts[(int64_t)u * s.nb + j];
+  const int32_t* lg = lists + (int64_t)u * s.N * s.k + offsets[(int64_t)u * s.nb + j];
+  const float sc = s.scale * 1.4426950408889634f;
+  for (int b0 = 0; b0 < n; b0 += kB) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = 2 * warp + h;
+      const int i = b0 + r;
+      const int row = i < n ? lg[i] : -1;
+      const int64_t R = (int64_t)u * s.N + (row >= 0 ? row : 0);
+      __nv_bfloat162 qq = __floats2bfloat162_rn(0.f, 0.f);
+      if (row >= 0) qq = *reinterpret_cast<const __nv_bfloat162*>(Q + R * D + 2 * lane);
+      *reinterpret_cast<__nv_bfloat162*>(Qb + r * kS64 + 2 * lane) = qq;
+      int slot = -1;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int q = lane + 32 * hh;
+        const bool hit = row >= 0 && q < s.k && idx[R * s.k + q] == j;
+        const unsigned bits = __ballot_sync(0xffffffffu, hit);
+        if (slot < 0 && bits != 0u) slot = 32 * hh + __ffs(bits) - 1;
+      }
+      if (lane == 0) {
+        row_s[r] = row;
+        slot_s[r] = row >= 0 ? slot : -1;
+      }
+    }
+    __syncthreads();
+    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      const int c0 = 16 * ks + 2 * q4;
+      mma(sacc, ld32(Qb + g * kS64 + c0), ld32(Qb + (g + 8) * kS64 + c0),
+          ld32(Qb + g * kS64 + c0 + 8), ld32(Qb + (g + 8) * kS64 + c0 + 8),
+          ld32(Ks + (8 * warp + g) * kS64 + c0), ld32(Ks + (8 * warp + g) * kS64 + c0 + 8));
+    }
+    // Per row (g and g + 8) this warp's 8 keys: maximum and sum.
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = g + 8 * h;
+      const int row = row_s[r];
+      float x[2];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int key = 8 * warp + 2 * q4 + c;
+        const bool live = row >= 0 && (!s.causal || j * BS + key <= row);
+        x[c] = live ? sacc[2 * h + c] * sc : -INFINITY;
+      }
+      float m = fmaxf(x[0], x[1]);
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+      float l = m == -INFINITY ? 0.f : exp2f(x[0] - m) + exp2f(x[1] - m);
+      l += __shfl_xor_sync(0xffffffffu, l, 1);
+      l += __shfl_xor_sync(0xffffffffu, l, 2);
+      if (q4 == 0) {
+        wm[warp * kB + r] = m;
+        wl[warp * kB + r] = l;
+      }
+    }
+    __syncthreads();
+    if (t < kB) {
+      const int row = row_s[t], sl = slot_s[t];
+      if (row >= 0 && sl >= 0) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) M = fmaxf(M, wm[w * kB + t]);
+        float L = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w)
+          L += wm[w * kB + t] == -INFINITY ? 0.f : wl[w * kB + t] * exp2f(wm[w * kB + t] - M);
+        ml_part[((int64_t)u * s.N + row) * s.k + sl] = make_float2(M, L);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// Per row (a warp): the log-sum-exp from its slots' shares, and delta =
+// dO . O from the forward's O.
+template <int DPL>
+__global__ void __launch_bounds__(kBwdRowsWarps * 32)
+bwd_lse_merge_kernel(const float2* __restrict__ ml_part, const int32_t* __restrict__ idx,
+                     const __nv_bfloat16* __restrict__ O, const __nv_bfloat16* __restrict__ dO,
+                     float* __restrict__ lse_out, float* __restrict__ delta_out, Shape s) {
+  constexpr int D = DPL * 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t R = ((int64_t)blockIdx.x * kBwdRowsWarps + warp);
+  if (R >= (int64_t)s.units * s.N) return;   // whole warp
+  float od[DPL], gd[DPL];
+  load_cols<DPL>(O + R * D, lane, od);
+  load_cols<DPL>(dO + R * D, lane, gd);
+  float dl = 0.f;
+#pragma unroll
+  for (int c = 0; c < DPL; ++c) dl = fmaf(gd[c], od[c], dl);
+  const float delta = warp_sum(dl);
+  float2 ml[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int q = lane + 32 * h;
+    const bool live = q < s.k && idx[R * s.k + q] >= 0;
+    ml[h] = live ? ml_part[R * s.k + q] : make_float2(-INFINITY, 0.f);
+  }
+  const float M = warp_max(fmaxf(ml[0].x, ml[1].x));
+  float L = 0.f;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) L += ml[h].x == -INFINITY ? 0.f : ml[h].y * exp2f(ml[h].x - M);
+  L = warp_sum(L);
+  if (lane == 0) {
+    lse_out[R] = M + log2f(L);
+    delta_out[R] = delta;
+  }
+}
+
 static size_t bwd_kv_mma_smem() {
   using namespace bwdmma;
   return sizeof(__nv_bfloat16) * (3 * 64 * kS64 + 3 * kB * kS64 + 4 * 64 * kS16) +
@@ -622,12 +762,27 @@ static cudaError_t launch_bwd(const __nv_bfloat16* Q, const __nv_bfloat16* K,
   float* delta = lse + rows;
   float* dq_part = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(lse) +
                                             a256b(2 * rows * sizeof(float)));
-  dim3 g1((s.N + kBwdRowsWarps - 1) / kBwdRowsWarps, s.units);
-  bwd_lse_kernel<DPL><<<g1, kBwdRowsWarps * 32, 0, st>>>(Q, K, O, dO, idx, lse, delta, s);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  const bool mma_path = (s.bs == 64 && s.D == 64);
+  cudaError_t e;
+  if (!mma_path) {
+    dim3 g1((s.N + kBwdRowsWarps - 1) / kBwdRowsWarps, s.units);
+    bwd_lse_kernel<DPL><<<g1, kBwdRowsWarps * 32, 0, st>>>(Q, K, O, dO, idx, lse, delta, s);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
   BucketLists bl;
   if ((e = launch_bucket_lists(idx, V, ws, s, st, &bl)) != cudaSuccess) return e;
+  if (mma_path) {
+    // The rows' log-sum-exp from the key-block side: shares per (row, slot),
+    // held in the dQ-share array until the per-block pass overwrites it.
+    float2* ml_part = reinterpret_cast<float2*>(dq_part);
+    bwd_lse_mma_kernel<<<dim3(s.nb, s.units), kBwdKvThreads, 0, st>>>(
+        Q, K, bl.lists, bl.offsets, bl.counts, idx, ml_part, s);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const unsigned g2 = (unsigned)((rows + kBwdRowsWarps - 1) / kBwdRowsWarps);
+    bwd_lse_merge_kernel<DPL><<<g2, kBwdRowsWarps * 32, 0, st>>>(ml_part, idx, O, dO, lse, delta,
+                                                                 s);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
   const int elems = s.bs * s.D;
   if (s.bs == 64 && s.D == 64) {
     const size_t smem = bwd_kv_mma_smem();
