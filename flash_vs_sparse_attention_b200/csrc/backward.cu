@@ -328,20 +328,21 @@ bwd_kv_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __restri
 }
 
 // The per-block kernel on tensor cores (mma.sync, bf16 in, fp32 out), for
-// block_size 64 and head_dim 64: 16 rows of the block's list at a time.
-//   S = Q K^T and dP = dO V^T (16 x 64): warp w the keys 8w .. 8w + 7;
+// block_size 64 and head_dim 64: 32 rows of the block's list at a time.
+//   S = Q K^T and dP = dO V^T (32 x 64): warp w the keys 8w .. 8w + 7;
 //   P = 2^(S sc - lse), dS = P (dP - delta), rounded to bf16 as the
 //   operands of the next products;
 //   dV += P^T dO and dK += dS^T Q (64 x 64, kept in registers over the whole
 //   list): warp w the keys 16 (w / 2) .., columns 32 (w % 2) ..;
-//   dQ share = dS K (16 x 64): warp w the columns 8w .. 8w + 7.
+//   dQ share = dS K (32 x 64): warp w the columns 8w .. 8w + 7.
 // The operands sit in shared memory in the layouts the fragments read
-// (rows padded to 72 or 24 elements against bank conflicts).  Rows in list
+// (rows padded by 8 elements against bank conflicts).  Rows in list
 // order and the products' fixed order: the same result on every run.
 namespace bwdmma {
-constexpr int kB = 16;          // rows per batch
+constexpr int kMT = 2;          // 16-row tiles per batch
+constexpr int kB = 16 * kMT;    // rows per batch
 constexpr int kS64 = 72;        // row stride of 64-wide arrays (bf16)
-constexpr int kS16 = 24;        // row stride of 16-wide arrays (bf16)
+constexpr int kS16 = kB + 8;    // row stride of kB-wide arrays (bf16)
 __device__ __forceinline__ uint32_t ld32(const __nv_bfloat16* p) {
   return *reinterpret_cast<const uint32_t*>(p);
 }
@@ -427,11 +428,11 @@ bwd_kv_mma_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __re
 #pragma unroll
     for (int c = 0; c < 4; ++c) accV[a][c] = accK[a][c] = 0.f;
   for (int b0 = 0; b0 < n; b0 += kB) {
-    // Rows 2w and 2w + 1 of the batch: Q and dO in both layouts,
-    // log-sum-exp, delta and the slot of this block (-1 for a missing row).
+    // Rows kB/8 w .. of the batch: Q and dO in both layouts, log-sum-exp,
+    // delta and the slot of this block (-1 for a missing row).
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int r = 2 * warp + h;
+    for (int h = 0; h < kB / 8; ++h) {
+      const int r = (kB / 8) * warp + h;
       const int i = b0 + r;
       const int row = i < n ? (sorted ? lst[i] : lg[i]) : -1;
       const int64_t R = (int64_t)u * s.N + (row >= 0 ? row : 0);
@@ -462,24 +463,27 @@ bwd_kv_mma_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __re
       }
     }
     __syncthreads();
-    // S and dP for keys 8w .. 8w + 7.
-    {
+    // S and dP for keys 8w .. 8w + 7, each 16-row tile of the batch.
+#pragma unroll
+    for (int m = 0; m < kMT; ++m) {
+      const __nv_bfloat16* qa = Qb + (16 * m) * kS64;
+      const __nv_bfloat16* ga = Gb + (16 * m) * kS64;
       float sacc[4] = {0.f, 0.f, 0.f, 0.f}, pacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int ks = 0; ks < D / 16; ++ks) {
         const int c0 = 16 * ks + 2 * q4;
-        const uint32_t a0 = ld32(Qb + g * kS64 + c0), a1 = ld32(Qb + (g + 8) * kS64 + c0);
-        const uint32_t a2 = ld32(Qb + g * kS64 + c0 + 8), a3 = ld32(Qb + (g + 8) * kS64 + c0 + 8);
+        const uint32_t a0 = ld32(qa + g * kS64 + c0), a1 = ld32(qa + (g + 8) * kS64 + c0);
+        const uint32_t a2 = ld32(qa + g * kS64 + c0 + 8), a3 = ld32(qa + (g + 8) * kS64 + c0 + 8);
         mma(sacc, a0, a1, a2, a3, ld32(Ks + (8 * warp + g) * kS64 + c0),
             ld32(Ks + (8 * warp + g) * kS64 + c0 + 8));
-        const uint32_t e0 = ld32(Gb + g * kS64 + c0), e1 = ld32(Gb + (g + 8) * kS64 + c0);
-        const uint32_t e2 = ld32(Gb + g * kS64 + c0 + 8), e3 = ld32(Gb + (g + 8) * kS64 + c0 + 8);
+        const uint32_t e0 = ld32(ga + g * kS64 + c0), e1 = ld32(ga + (g + 8) * kS64 + c0);
+        const uint32_t e2 = ld32(ga + g * kS64 + c0 + 8), e3 = ld32(ga + (g + 8) * kS64 + c0 + 8);
         mma(pacc, e0, e1, e2, e3, ld32(Vs + (8 * warp + g) * kS64 + c0),
             ld32(Vs + (8 * warp + g) * kS64 + c0 + 8));
       }
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const int r = g + 8 * (c >> 1), key = 8 * warp + 2 * q4 + (c & 1);
+        const int r = 16 * m + g + 8 * (c >> 1), key = 8 * warp + 2 * q4 + (c & 1);
         const int row = row_s[r];
         float p = 0.f, ds = 0.f;
         if (row >= 0 && (!s.causal || j * BS + key <= row)) {
@@ -493,9 +497,10 @@ bwd_kv_mma_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __re
       }
     }
     __syncthreads();
-    // dV += P^T dO, dK += dS^T Q over this batch's 16 rows.
-    {
-      const int k0 = 2 * q4;
+    // dV += P^T dO, dK += dS^T Q over this batch's rows (16 at a time).
+#pragma unroll
+    for (int kk = 0; kk < kMT; ++kk) {
+      const int k0 = 16 * kk + 2 * q4;
       const __nv_bfloat16* pa = PT + (16 * mt) * kS16;
       const __nv_bfloat16* da = DST + (16 * mt) * kS16;
       const uint32_t p0 = ld32(pa + g * kS16 + k0), p1 = ld32(pa + (g + 8) * kS16 + k0);
@@ -512,18 +517,20 @@ bwd_kv_mma_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __re
       }
     }
     // This block's dQ share of each row, columns 8w .. 8w + 7, into its slot.
-    {
+#pragma unroll
+    for (int m = 0; m < kMT; ++m) {
+      const __nv_bfloat16* sa = DSr + (16 * m) * kS64;
       float qacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int ks = 0; ks < BS / 16; ++ks) {
         const int c0 = 16 * ks + 2 * q4;
-        mma(qacc, ld32(DSr + g * kS64 + c0), ld32(DSr + (g + 8) * kS64 + c0),
-            ld32(DSr + g * kS64 + c0 + 8), ld32(DSr + (g + 8) * kS64 + c0 + 8),
+        mma(qacc, ld32(sa + g * kS64 + c0), ld32(sa + (g + 8) * kS64 + c0),
+            ld32(sa + g * kS64 + c0 + 8), ld32(sa + (g + 8) * kS64 + c0 + 8),
             ld32(KTs + (8 * warp + g) * kS64 + c0), ld32(KTs + (8 * warp + g) * kS64 + c0 + 8));
       }
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int r = g + 8 * h;
+        const int r = 16 * m + g + 8 * h;
         const int sl = slot_s[r];
         if (sl >= 0) {
           float* dst = dq_part + (((int64_t)u * s.N + row_s[r]) * s.k + sl) * D + 8 * warp + 2 * q4;
@@ -576,8 +583,8 @@ bwd_lse_mma_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __r
   const float sc = s.scale * 1.4426950408889634f;
   for (int b0 = 0; b0 < n; b0 += kB) {
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int r = 2 * warp + h;
+    for (int h = 0; h < kB / 8; ++h) {
+      const int r = (kB / 8) * warp + h;
       const int i = b0 + r;
       const int row = i < n ? lg[i] : -1;
       const int64_t R = (int64_t)u * s.N + (row >= 0 ? row : 0);
@@ -598,35 +605,39 @@ bwd_lse_mma_kernel(const __nv_bfloat16* __restrict__ Q, const __nv_bfloat16* __r
       }
     }
     __syncthreads();
-    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-      const int c0 = 16 * ks + 2 * q4;
-      mma(sacc, ld32(Qb + g * kS64 + c0), ld32(Qb + (g + 8) * kS64 + c0),
-          ld32(Qb + g * kS64 + c0 + 8), ld32(Qb + (g + 8) * kS64 + c0 + 8),
-          ld32(Ks + (8 * warp + g) * kS64 + c0), ld32(Ks + (8 * warp + g) * kS64 + c0 + 8));
-    }
-    // Per row (g and g + 8) this warp's 8 keys: maximum and sum.
+    for (int mm = 0; mm < kMT; ++mm) {
+      const __nv_bfloat16* qa = Qb + (16 * mm) * kS64;
+      float sacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int r = g + 8 * h;
-      const int row = row_s[r];
-      float x[2];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int key = 8 * warp + 2 * q4 + c;
-        const bool live = row >= 0 && (!s.causal || j * BS + key <= row);
-        x[c] = live ? sacc[2 * h + c] * sc : -INFINITY;
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const int c0 = 16 * ks + 2 * q4;
+        mma(sacc, ld32(qa + g * kS64 + c0), ld32(qa + (g + 8) * kS64 + c0),
+            ld32(qa + g * kS64 + c0 + 8), ld32(qa + (g + 8) * kS64 + c0 + 8),
+            ld32(Ks + (8 * warp + g) * kS64 + c0), ld32(Ks + (8 * warp + g) * kS64 + c0 + 8));
       }
-      float m = fmaxf(x[0], x[1]);
-      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-      float l = m == -INFINITY ? 0.f : exp2f(x[0] - m) + exp2f(x[1] - m);
-      l += __shfl_xor_sync(0xffffffffu, l, 1);
-      l += __shfl_xor_sync(0xffffffffu, l, 2);
-      if (q4 == 0) {
-        wm[warp * kB + r] = m;
-        wl[warp * kB + r] = l;
+      // Per row (g and g + 8 of this tile) this warp's 8 keys: maximum, sum.
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int r = 16 * mm + g + 8 * h;
+        const int row = row_s[r];
+        float x[2];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int key = 8 * warp + 2 * q4 + c;
+          const bool live = row >= 0 && (!s.causal || j * BS + key <= row);
+          x[c] = live ? sacc[2 * h + c] * sc : -INFINITY;
+        }
+        float m = fmaxf(x[0], x[1]);
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        float l = m == -INFINITY ? 0.f : exp2f(x[0] - m) + exp2f(x[1] - m);
+        l += __shfl_xor_sync(0xffffffffu, l, 1);
+        l += __shfl_xor_sync(0xffffffffu, l, 2);
+        if (q4 == 0) {
+          wm[warp * kB + r] = m;
+          wl[warp * kB + r] = l;
+        }
       }
     }
     __syncthreads();
