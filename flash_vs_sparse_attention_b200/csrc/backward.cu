@@ -1,5 +1,6 @@
-// The backward pass of the fine stage, on CUDA cores: dQ, dK, dV of
-// O = attention over the selected blocks, the selection held fixed.
+// The backward pass of the fine stage: dQ, dK, dV of O = attention over the
+// selected blocks, the selection held fixed (CUDA cores, and mma.sync tensor
+// cores for the per-block products at block_size 64 / head_dim 64).
 // (The reference's stated next step, blog.md:133.  Its PyTorch variant,
 // block_indexer.py, is differentiable; autograd gives Q, K and V the
 // gradient of the fine stage, block_indexer.py:55-84, and nothing flows
